@@ -1,0 +1,118 @@
+/*
+ * llamini_b200.h -- additive C entry points of the B200 library.
+ *
+ * Everything here is new: the reference (llamini.cpp) has no GPU, no batching
+ * and no device-resident sessions, so none of these functions replaces a
+ * reference symbol one-for-one. Each comment names the reference code whose
+ * behaviour the function exposes or extends. All functions return 0 on success
+ * and -1 on failure unless stated otherwise; the reason is kept in
+ * llamini_last_error(). No function aborts the process.
+ */
+#ifndef LLAMINI_B200_H
+#define LLAMINI_B200_H
+
+#include "common.h"
+#include "gguf.h"
+#include "model.h"
+#include "gpt2.h"
+#include "kv_cache.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- runtime --------------------------------------------------------------- */
+
+/* Sticky description of the last failure ("" if none). The reference reports
+ * errors only through -1 returns and stderr (gguf.h comments, main.c:472-477). */
+const char* llamini_last_error(void);
+void llamini_clear_error(void);
+
+/* Number of visible CUDA devices (0 without a GPU; never fails). */
+int llamini_device_count(void);
+
+/* Select the CUDA device used by every later call of this process. Must be
+ * called before the first model is loaded. Default: device 0, or the value of
+ * the LLAMINI_DEVICE environment variable. */
+int llamini_set_device(int device);
+
+/* The library's CUDA stream (a cudaStream_t) on the current device, created on
+ * first use; NULL without a device. Timing code records events on it. */
+void* llamini_stream(void);
+
+/* Release every device resource the library holds (weights, KV caches, graphs). */
+void llamini_release(void);
+
+/* ---- block decoders and GEMV on raw blocks (the gguf.c:409-594 and
+ *      model.c:66-176 hot loops, exposed without a GGUF file) ------------------ */
+
+/* Bytes taken by n_elems elements of ggml `type` (0 if the type is unsupported
+ * or n_elems is not a multiple of its block size). */
+u64 llamini_type_bytes(u32 type, u64 n_elems);
+
+/* Decode n_elems elements of raw `type` blocks from host memory into host f32
+ * out, on the GPU. Bit-identical to gguf.c:409-594. */
+int llamini_dequant_host(u32 type, const void* blocks, u64 n_elems, f32* out);
+
+/* Same decode between device buffers, enqueued on llamini_stream(). */
+int llamini_dequant_device(u32 type, const void* d_blocks, u64 n_elems, f32* d_out);
+
+/* y[b][r] = sum_k W[r][k] * x[b][k] for b < batch, W given as raw `type` rows of
+ * `cols` elements (cols a multiple of the block size). Host buffers; x is
+ * batch x cols f32, y is batch x rows f32 (model.c:66-73 per column). */
+int llamini_gemv_host(u32 type, const void* w, u32 rows, u32 cols,
+                      const f32* x, u32 batch, f32* y);
+
+/* Device-pointer form of llamini_gemv_host, enqueued on llamini_stream(). */
+int llamini_gemv_device(u32 type, const void* d_w, u32 rows, u32 cols,
+                        const f32* d_x, u32 batch, f32* d_y);
+
+/* ---- device-resident decoding sessions (generate.c:122-167 without host
+ *      round trips) --------------------------------------------------------- */
+
+typedef struct llamini_session llamini_session;
+
+/* Session for a loaded LLaMA-family model and its per-layer caches. The session
+ * owns the device KV cache, the step graph and the token buffer; it is created
+ * on first use by forward_step/generate_autoregressive as well, and this call
+ * returns that same session. NULL on failure. */
+llamini_session* llamini_llama_session(LLaMAModel* model, KVCache* caches);
+
+/* Same for a GPT-2 model (gpt2.c:150-229). */
+llamini_session* llamini_gpt2_session(GPT2Model* model, KVCache* caches);
+
+/* Reset the session to position 0 with the given prompt (n_prompt >= 1). */
+int llamini_session_begin(llamini_session* s, const u32* prompt, u32 n_prompt);
+
+/* Enqueue n_steps forward passes without waiting. Step at position p embeds
+ * token[p]; when p+1 >= n_prompt it also stores the greedy token as token[p+1].
+ * Fails if the run would pass the cache capacity. */
+int llamini_session_step(llamini_session* s, u32 n_steps);
+
+/* Wait for queued steps, then copy token[0..n) to host out. Returns the number
+ * of valid tokens (prompt + generated), or -1. */
+int llamini_session_tokens(llamini_session* s, u32* out, u32 n);
+
+/* Wait, then copy the logits of the most recent step (vocab_size floats). */
+int llamini_session_logits(llamini_session* s, f32* out);
+
+/* Current position (number of tokens already run through the stack). */
+u32 llamini_session_pos(llamini_session* s);
+
+/* Algorithmic bytes one step reads: every weight matrix once, norms, biases and
+ * one embedding row (the quantized sizes of gguf.c's block formats). */
+u64 llamini_session_weight_bytes(llamini_session* s);
+
+/* KV-cache bytes per cached position (all layers, K and V, fp16). */
+u64 llamini_session_kv_bytes_per_pos(llamini_session* s);
+
+/* Per-layer residual stream of the most recent step: n_layers x dim floats,
+ * captured when `enable` was set before the step ran. For parity tests. */
+int llamini_session_trace(llamini_session* s, int enable);
+int llamini_session_trace_read(llamini_session* s, f32* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

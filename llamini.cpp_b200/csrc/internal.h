@@ -1,0 +1,179 @@
+// internal.h -- declarations shared by the host and device translation units of
+// libllamini_cuda.so. Not installed; the public C ABI is include/*.h.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstddef>
+
+#include "common.h"
+#include "gguf.h"
+#include "tensor.h"
+#include "kv_cache.h"
+#include "model.h"
+#include "gpt2.h"
+
+namespace lm {
+
+// ---------------------------------------------------------------- errors
+// Every failure is recorded here (sticky until llamini_clear_error) and echoed
+// to stderr once; no call aborts the process.
+void set_error(const char* fmt, ...);
+bool cuda_ok(cudaError_t e, const char* what);
+#define LM_CUDA(call) ::lm::cuda_ok((call), #call)
+
+// ---------------------------------------------------------------- device
+// Selects/initialises the CUDA device on first use. False (with an error set)
+// when no device is usable; every GPU entry point checks this first.
+bool ensure_device();
+cudaStream_t stream();
+int sm_count();
+
+// Device allocations go through these so that failures are reported uniformly.
+void* dev_alloc(size_t bytes);
+void dev_free(void* p);
+
+// ---------------------------------------------------------------- formats
+struct TypeInfo { uint32_t block_elems, block_bytes; };
+bool type_info(uint32_t type, TypeInfo* ti);
+uint64_t type_bytes(uint32_t type, uint64_t n_elems);   // 0 if unsupported/misaligned
+
+// A weight matrix in GPU memory: the GGUF bytes of `rows` rows of `cols`
+// elements each, stored unchanged (row r starts at ptr + r*row_bytes).
+struct DevMat {
+    const uint8_t* ptr = nullptr;
+    uint32_t type = 0, rows = 0, cols = 0;
+    uint64_t row_bytes = 0;
+};
+
+// ---------------------------------------------------------------- kernels (launchers)
+// All launchers enqueue on `st` and return false (error set) on a launch failure.
+bool kernels_init();
+bool launch_dequant(uint32_t type, const uint8_t* d_raw, uint64_t n_elems, float* d_out, cudaStream_t st);
+
+enum Epi : uint32_t {
+    EPI_STORE = 0,      // out[r] = acc (+ bias[r])
+    EPI_RESID = 1,      // out[r] += acc (+ bias[r])        (out is the residual stream)
+    EPI_GLU_SILU = 2,   // out[r] = silu(acc_gate) * acc_up  (two matrices)
+    EPI_GLU_GELU = 3,   // out[r] = gelu(acc_gate) * acc_up
+    EPI_GELU = 4,       // out[r] = gelu(acc + bias[r])
+};
+
+enum Norm : uint32_t { NORM_NONE = 0, NORM_RMS = 1, NORM_LAYER = 2 };
+
+// One group of output rows of a fused GEMV launch.
+struct GemvSeg {
+    const uint8_t* w = nullptr;    // matrix (gate matrix for GLU)
+    const uint8_t* w2 = nullptr;   // up matrix for GLU
+    uint64_t row_bytes = 0, row_bytes2 = 0;
+    uint32_t type = 0, type2 = 0;
+    uint32_t rows = 0;
+    uint32_t epi = EPI_STORE;
+    float* out = nullptr;
+    const float* bias = nullptr;
+    uint32_t tile0 = 0;            // first tile of this segment (filled by the launcher)
+    uint32_t argmax = 0;           // 1: fold rows into the step's argmax key
+};
+
+constexpr int kMaxSegs = 4;
+
+struct GemvArgs {
+    const float* x = nullptr;      // input vector (normalised first when norm != NONE)
+    uint32_t K = 0;
+    uint32_t norm = NORM_NONE;
+    const float* norm_w = nullptr;
+    const float* norm_b = nullptr;
+    float eps = 0.f;
+    uint32_t nseg = 0;
+    GemvSeg seg[kMaxSegs];
+    unsigned long long* argmax_key = nullptr;
+    float* x_out = nullptr;        // optional: store the normalised x (block 0 writes it)
+};
+
+bool launch_gemv(const GemvArgs& a, cudaStream_t st);
+
+// Plain multi-column GEMV used by llamini_gemv_* (no fusion).
+bool launch_gemv_plain(uint32_t type, const uint8_t* w, uint32_t rows, uint32_t cols,
+                       const float* x, uint32_t batch, float* y, cudaStream_t st);
+
+// Per-step device state shared by the kernels of one session.
+struct StepState {
+    uint32_t pos;          // position of the current step
+    uint32_t n_prompt;     // tokens [0, n_prompt) are given; later ones are generated
+    uint32_t trace;        // 1: copy the residual stream after each layer
+    uint32_t pad;
+    unsigned long long argmax_key;
+    double nll;            // perplexity accumulator
+    uint32_t nll_count;
+};
+
+struct EmbedArgs {
+    StepState* st;
+    const uint32_t* tokens;
+    DevMat tok;            // token embedding table
+    DevMat pos;            // learned position table (GPT-2) or ptr == nullptr
+    float scale;           // embedding scale (1 unless gemma)
+    float* hidden;
+    uint32_t dim;
+};
+bool launch_embed(const EmbedArgs& a, cudaStream_t st);
+
+struct AttnArgs {
+    StepState* st;
+    const float* qkv;      // q [n_heads*hd] | k [n_kv*hd] | v [n_kv*hd]
+    uint16_t* kc;          // this layer's cache: [n_kv][max_seq][hd] fp16 bits
+    uint16_t* vc;
+    float* out;            // [n_heads*hd]
+    float* part;           // [n_heads][n_split][hd + 2] partial results
+    uint32_t* counter;     // [n_kv] completion counters (return to 0 after use)
+    uint32_t n_heads, n_kv, hd, max_seq, n_split;
+    uint32_t rope;         // 0 none, 1 NORM, 2 NEOX
+    float rope_base;
+};
+bool launch_attention(const AttnArgs& a, cudaStream_t st);
+
+struct FinishArgs {
+    StepState* st;
+    uint32_t* tokens;
+    uint32_t max_tokens;
+    const float* logits;   // for the perplexity accumulator (may be null)
+    uint32_t vocab;
+    uint32_t nll;          // 1: accumulate -log p(tokens[pos+1])
+};
+bool launch_finish(const FinishArgs& a, cudaStream_t st);
+
+// Host-pointer op kernels (model.h per-op exports), device buffers in/out.
+bool launch_rms_norm(float* out, const float* x, const float* w, uint32_t dim, float eps, cudaStream_t st);
+bool launch_layer_norm(float* out, const float* x, const float* w, const float* b, uint32_t dim, float eps, cudaStream_t st);
+bool launch_rope(float* v, uint32_t pos, uint32_t dim, uint32_t hd, float base, uint32_t neox, cudaStream_t st);
+bool launch_glu(float* out, const float* g, const float* u, uint32_t n, uint32_t gelu, cudaStream_t st);
+bool launch_gelu_inplace(float* x, uint32_t n, cudaStream_t st);
+bool launch_add(float* out, const float* a, const float* b, uint32_t n, cudaStream_t st);
+bool launch_scale(float* out, const float* a, float s, uint32_t n, cudaStream_t st);
+bool launch_argmax(const float* x, uint32_t n, uint32_t* out, cudaStream_t st);
+bool launch_matmul(const float* A, const float* B, float* C, uint32_t m, uint32_t k, uint32_t n, cudaStream_t st);
+bool launch_mha_f32(const float* q, float* kc, float* vc, float* out, uint32_t pos,
+                    uint32_t n_heads, uint32_t n_kv, uint32_t hd, cudaStream_t st);
+bool launch_copy_f32(float* dst, const float* src, uint32_t n, cudaStream_t st);
+
+// ---------------------------------------------------------------- weight registry
+// Device copies of GGUF tensors, keyed by the GGUFTensorInfo they came from.
+// Filled by llama_load_weights / gpt2_load_weights (or on demand), dropped by
+// gguf_close.
+bool upload_gguf_tensor(GGUFFile* gf, const GGUFTensorInfo* info, DevMat* out,
+                        uint32_t rows, uint32_t cols);
+const DevMat* find_gguf_tensor(const GGUFTensorInfo* info);
+void drop_gguf(GGUFFile* gf);
+
+// GPT-2's loader keeps eager f32 host tensors (gpt2.c:91-127); the GGUF tensor
+// each one came from is remembered so the GPU can stream the quantized bytes.
+void remember_source(const Tensor* t, GGUFFile* gf, const GGUFTensorInfo* info);
+bool source_of(const Tensor* t, GGUFFile** gf, const GGUFTensorInfo** info);
+void forget_sources(const Tensor* t);
+
+// Sessions (session.cu)
+void drop_sessions_for_model(const void* model);
+void drop_sessions_for_gguf(const GGUFFile* gf);
+void drop_all_sessions();
+
+}  // namespace lm

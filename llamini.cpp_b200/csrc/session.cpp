@@ -1,0 +1,658 @@
+// session.cpp -- the device-resident token loop.
+//
+// A session binds one model to one array of per-layer KV caches. It owns the
+// fp16 device cache, the activation buffers, a token buffer and a StepState
+// block in GPU memory, and two CUDA graphs: one step and a run of kStepsPerGraph
+// steps. A step (generate.c:62-120 for LLaMA, gpt2.c:150-192 for GPT-2) is
+//
+//   embed -> per layer: [norm+QKV GEMV] -> attention -> [O GEMV + residual]
+//                       -> [norm+gate/up GEMV + activation] -> [down GEMV + residual]
+//         -> [norm + lm_head GEMV + argmax] -> finish
+//
+// and reads its position and input token from device memory, so consecutive
+// steps need no host involvement: the argmax of step p becomes the input of
+// step p+1 on the device (generate.c:143-156 without the round trip).
+#include "internal.h"
+#include "llamini_b200.h"
+#include "generate.h"
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <cmath>
+#include <ctime>
+#include <vector>
+
+struct llamini_session {
+    int kind = 0;                         // 0 LLaMA family, 1 GPT-2
+    const void* model = nullptr;
+    KVCache* caches = nullptr;
+    u32 cache_max_seq = 0, cache_dim = 0;
+    const GGUFFile* gf = nullptr;         // file whose device tensors we use (may be null)
+
+    // shape
+    u32 n_layers = 0, dim = 0, n_heads = 0, n_kv = 0, hd = 0, ffn = 0, vocab = 0, max_seq = 0;
+    u32 qd = 0, kvd = 0, n_split = 1, max_pos = 0;
+    f32 eps = 0, rope_base = 0, emb_scale = 1;
+    u32 rope_mode = 0;                    // 0 none, 1 NORM, 2 NEOX
+    u32 act_gelu = 0;
+
+    // weights (device)
+    struct Layer {
+        lm::DevMat q, k, v, o, gate, up, down;    // LLaMA (for GPT-2: q = fused qkv, o = out)
+        const float *n1w = nullptr, *n1b = nullptr, *n2w = nullptr, *n2b = nullptr;
+        const float *bq = nullptr, *bk = nullptr, *bv = nullptr, *bo = nullptr, *bup = nullptr, *bdown = nullptr;
+    };
+    std::vector<Layer> layers;
+    lm::DevMat tok, pos_tab, head;
+    const float *fnw = nullptr, *fnb = nullptr;
+    u64 weight_bytes = 0;
+
+    // buffers (device)
+    std::vector<void*> owned;
+    float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *ffn_h = nullptr, *logits = nullptr;
+    float *part = nullptr, *trace = nullptr;
+    u32 *counters = nullptr, *tokens = nullptr;
+    uint16_t *kc = nullptr, *vc = nullptr;
+    lm::StepState* st = nullptr;
+    lm::StepState* st_host = nullptr;     // pinned staging for StepState writes/reads
+
+    // graphs
+    cudaGraphExec_t g_one = nullptr, g_many = nullptr, g_trace = nullptr, g_nll = nullptr;
+    bool trace_on = false;
+
+    // host mirror of the device position / prompt length
+    u32 pos = 0, n_prompt = 0;
+};
+
+namespace lm {
+namespace {
+
+constexpr u32 kStepsPerGraph = 8;
+std::vector<llamini_session*> g_sessions;
+
+void* own(llamini_session* s, size_t bytes) {
+    void* p = dev_alloc(bytes);
+    if (p) s->owned.push_back(p);
+    return p;
+}
+
+// Device copy of an f32 host vector (norm weights, biases).
+const float* upload_f32(llamini_session* s, const f32* h, size_t n) {
+    float* d = (float*)own(s, n * sizeof(float));
+    if (!d) return nullptr;
+    if (!LM_CUDA(cudaMemcpy(d, h, n * sizeof(float), cudaMemcpyHostToDevice))) return nullptr;
+    return d;
+}
+
+// Device matrix for a weight tensor of shape rows x cols: the uploaded GGUF
+// bytes when the tensor is lazy or was loaded from a GGUF file, otherwise its
+// eager f32 host data.
+bool weight(llamini_session* s, const Tensor* t, u32 rows, u32 cols, DevMat* out) {
+    if (!t) { set_error("missing weight tensor"); return false; }
+    if ((u64)t->size != (u64)rows * cols) { set_error("weight shape mismatch: %u elements, expected %ux%u", t->size, rows, cols); return false; }
+    GGUFFile* gf = nullptr;
+    const GGUFTensorInfo* info = nullptr;
+    if (!t->data) { gf = t->src_gf; info = t->src_info; }
+    else source_of(t, &gf, &info);
+    if (info) {
+        const DevMat* m = find_gguf_tensor(info);
+        if (m && m->rows == rows && m->cols == cols) { *out = *m; }
+        else if (!upload_gguf_tensor(gf, info, out, rows, cols)) return false;
+        s->gf = gf;
+        s->weight_bytes += out->row_bytes * rows;
+        return true;
+    }
+    const float* d = upload_f32(s, t->data, (size_t)rows * cols);
+    if (!d) return false;
+    out->ptr = (const uint8_t*)d;
+    out->type = GGML_TYPE_F32;
+    out->rows = rows;
+    out->cols = cols;
+    out->row_bytes = (u64)cols * 4;
+    s->weight_bytes += out->row_bytes * rows;
+    return true;
+}
+
+const float* vec(llamini_session* s, const Tensor* t, u32 n) {
+    if (!t || !t->data || t->size < n) { set_error("missing or short f32 tensor"); return nullptr; }
+    s->weight_bytes += (u64)n * 4;
+    return upload_f32(s, t->data, n);
+}
+
+bool alloc_buffers(llamini_session* s) {
+    const u32 L = s->n_layers;
+    s->hidden = (float*)own(s, (size_t)s->dim * 4);
+    s->qkv = (float*)own(s, (size_t)(s->qd + 2 * s->kvd) * 4);
+    s->attn = (float*)own(s, (size_t)s->qd * 4);
+    s->ffn_h = (float*)own(s, (size_t)s->ffn * 4);
+    s->logits = (float*)own(s, (size_t)s->vocab * 4);
+    s->part = (float*)own(s, (size_t)s->n_heads * s->n_split * (s->hd + 2) * 4);
+    s->trace = (float*)own(s, (size_t)L * s->dim * 4);
+    s->counters = (u32*)own(s, (size_t)s->n_kv * 4);
+    s->tokens = (u32*)own(s, ((size_t)s->max_seq + 1) * 4);
+    const size_t kv_elems = (size_t)L * s->n_kv * s->max_seq * s->hd;
+    s->kc = (uint16_t*)own(s, kv_elems * 2);
+    s->vc = (uint16_t*)own(s, kv_elems * 2);
+    s->st = (StepState*)own(s, sizeof(StepState));
+    if (!s->hidden || !s->qkv || !s->attn || !s->ffn_h || !s->logits || !s->part || !s->trace ||
+        !s->counters || !s->tokens || !s->kc || !s->vc || !s->st)
+        return false;
+    if (!LM_CUDA(cudaMallocHost((void**)&s->st_host, sizeof(StepState)))) return false;
+    memset(s->st_host, 0, sizeof(StepState));
+    return LM_CUDA(cudaMemset(s->counters, 0, (size_t)s->n_kv * 4)) &&
+           LM_CUDA(cudaMemset(s->st, 0, sizeof(StepState))) &&
+           LM_CUDA(cudaMemset(s->tokens, 0, ((size_t)s->max_seq + 1) * 4)) &&
+           LM_CUDA(cudaMemset(s->kc, 0, kv_elems * 2)) && LM_CUDA(cudaMemset(s->vc, 0, kv_elems * 2));
+}
+
+u32 choose_splits(u32 n_kv, u32 max_seq) {
+    u32 s = 256 / (n_kv ? n_kv : 1);
+    if (s < 1) s = 1;
+    if (s > 32) s = 32;
+    if (s > max_seq) s = max_seq;
+    return s;
+}
+
+// ---------------------------------------------------------------- the step
+
+bool enqueue_step(llamini_session* s, cudaStream_t st, bool trace, bool nll) {
+    EmbedArgs e;
+    e.st = s->st;
+    e.tokens = s->tokens;
+    e.tok = s->tok;
+    e.pos = s->pos_tab;
+    e.scale = s->emb_scale;
+    e.hidden = s->hidden;
+    e.dim = s->dim;
+    if (!launch_embed(e, st)) return false;
+    const bool gpt2 = s->kind == 1;
+    for (u32 l = 0; l < s->n_layers; l++) {
+        const llamini_session::Layer& W = s->layers[l];
+        // norm + QKV
+        GemvArgs a;
+        a.x = s->hidden;
+        a.K = s->dim;
+        a.norm = gpt2 ? NORM_LAYER : NORM_RMS;
+        a.norm_w = W.n1w;
+        a.norm_b = W.n1b;
+        a.eps = s->eps;
+        if (gpt2) {
+            a.nseg = 1;
+            a.seg[0] = {W.q.ptr, nullptr, W.q.row_bytes, 0, W.q.type, 0, W.q.rows, EPI_STORE, s->qkv, W.bq, 0, 0};
+        } else {
+            a.nseg = 3;
+            a.seg[0] = {W.q.ptr, nullptr, W.q.row_bytes, 0, W.q.type, 0, W.q.rows, EPI_STORE, s->qkv, W.bq, 0, 0};
+            a.seg[1] = {W.k.ptr, nullptr, W.k.row_bytes, 0, W.k.type, 0, W.k.rows, EPI_STORE, s->qkv + s->qd, W.bk, 0, 0};
+            a.seg[2] = {W.v.ptr, nullptr, W.v.row_bytes, 0, W.v.type, 0, W.v.rows, EPI_STORE, s->qkv + s->qd + s->kvd, W.bv, 0, 0};
+        }
+        if (!launch_gemv(a, st)) return false;
+        // attention
+        AttnArgs at;
+        at.st = s->st;
+        at.qkv = s->qkv;
+        const size_t per_layer = (size_t)s->n_kv * s->max_seq * s->hd;
+        at.kc = s->kc + l * per_layer;
+        at.vc = s->vc + l * per_layer;
+        at.out = s->attn;
+        at.part = s->part;
+        at.counter = s->counters;
+        at.n_heads = s->n_heads;
+        at.n_kv = s->n_kv;
+        at.hd = s->hd;
+        at.max_seq = s->max_seq;
+        at.n_split = s->n_split;
+        at.rope = s->rope_mode;
+        at.rope_base = s->rope_base;
+        if (!launch_attention(at, st)) return false;
+        // O projection + residual
+        GemvArgs o;
+        o.x = s->attn;
+        o.K = s->qd;
+        o.nseg = 1;
+        o.seg[0] = {W.o.ptr, nullptr, W.o.row_bytes, 0, W.o.type, 0, W.o.rows, EPI_RESID, s->hidden, W.bo, 0, 0};
+        if (!launch_gemv(o, st)) return false;
+        // norm + FFN up (gated for LLaMA, GELU for GPT-2)
+        GemvArgs f;
+        f.x = s->hidden;
+        f.K = s->dim;
+        f.norm = gpt2 ? NORM_LAYER : NORM_RMS;
+        f.norm_w = W.n2w;
+        f.norm_b = W.n2b;
+        f.eps = s->eps;
+        f.nseg = 1;
+        if (gpt2)
+            f.seg[0] = {W.up.ptr, nullptr, W.up.row_bytes, 0, W.up.type, 0, W.up.rows, EPI_GELU, s->ffn_h, W.bup, 0, 0};
+        else
+            f.seg[0] = {W.gate.ptr, W.up.ptr, W.gate.row_bytes, W.up.row_bytes, W.gate.type, W.up.type, W.gate.rows,
+                        s->act_gelu ? (u32)EPI_GLU_GELU : (u32)EPI_GLU_SILU, s->ffn_h, nullptr, 0, 0};
+        if (!launch_gemv(f, st)) return false;
+        // down + residual
+        GemvArgs d;
+        d.x = s->ffn_h;
+        d.K = s->ffn;
+        d.nseg = 1;
+        d.seg[0] = {W.down.ptr, nullptr, W.down.row_bytes, 0, W.down.type, 0, W.down.rows, EPI_RESID, s->hidden, W.bdown, 0, 0};
+        if (!launch_gemv(d, st)) return false;
+        if (trace && !launch_copy_f32(s->trace + (size_t)l * s->dim, s->hidden, s->dim, st)) return false;
+    }
+    GemvArgs h;
+    h.x = s->hidden;
+    h.K = s->dim;
+    h.norm = gpt2 ? NORM_LAYER : NORM_RMS;
+    h.norm_w = s->fnw;
+    h.norm_b = s->fnb;
+    h.eps = s->eps;
+    h.nseg = 1;
+    h.seg[0] = {s->head.ptr, nullptr, s->head.row_bytes, 0, s->head.type, 0, s->head.rows, EPI_STORE, s->logits, nullptr, 0, 1};
+    h.argmax_key = &s->st->argmax_key;
+    if (!launch_gemv(h, st)) return false;
+    FinishArgs fa;
+    fa.st = s->st;
+    fa.tokens = s->tokens;
+    fa.max_tokens = s->max_seq + 1;
+    fa.logits = s->logits;
+    fa.vocab = s->vocab;
+    fa.nll = nll ? 1u : 0u;
+    return launch_finish(fa, st);
+}
+
+bool capture(llamini_session* s, u32 steps, bool trace, bool nll, cudaGraphExec_t* out) {
+    cudaStream_t st = stream();
+    cudaGraph_t g = nullptr;
+    if (!LM_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal))) return false;
+    bool ok = true;
+    for (u32 i = 0; i < steps && ok; i++) ok = enqueue_step(s, st, trace, nll);
+    cudaError_t e = cudaStreamEndCapture(st, &g);
+    if (!ok || !LM_CUDA(e)) { if (g) cudaGraphDestroy(g); return false; }
+    ok = LM_CUDA(cudaGraphInstantiate(out, g, 0));
+    cudaGraphDestroy(g);
+    return ok;
+}
+
+void destroy(llamini_session* s) {
+    if (!s) return;
+    cudaStreamSynchronize(stream());
+    cudaGraphExec_t gs[] = {s->g_one, s->g_many, s->g_trace, s->g_nll};
+    for (auto g : gs) if (g) cudaGraphExecDestroy(g);
+    for (void* p : s->owned) dev_free(p);
+    if (s->st_host) cudaFreeHost(s->st_host);
+    delete s;
+}
+
+bool finish_build(llamini_session* s) {
+    s->n_split = choose_splits(s->n_kv, s->max_seq);
+    if (!alloc_buffers(s)) return false;
+    if (!capture(s, 1, false, false, &s->g_one)) return false;
+    if (!capture(s, kStepsPerGraph, false, false, &s->g_many)) return false;
+    return true;
+}
+
+llamini_session* find(const void* model, KVCache* caches) {
+    for (auto* s : g_sessions)
+        if (s->model == model && s->caches == caches && s->cache_max_seq == caches[0].max_seq &&
+            s->cache_dim == caches[0].dim)
+            return s;
+    return nullptr;
+}
+
+void drop_where(bool (*pred)(const llamini_session*, const void*), const void* key) {
+    for (auto it = g_sessions.begin(); it != g_sessions.end();) {
+        if (pred(*it, key)) { destroy(*it); it = g_sessions.erase(it); }
+        else ++it;
+    }
+}
+
+llamini_session* build_llama(LLaMAModel* m, KVCache* caches) {
+    if (!ensure_device()) return nullptr;
+    const LLaMAConfig& c = m->cfg;
+    auto* s = new llamini_session();
+    s->kind = 0;
+    s->model = m;
+    s->caches = caches;
+    s->cache_max_seq = caches[0].max_seq;
+    s->cache_dim = caches[0].dim;
+    s->n_layers = c.n_layers; s->dim = c.dim; s->n_heads = c.n_heads; s->n_kv = c.n_heads_kv;
+    s->hd = c.head_dim; s->ffn = c.ffn_dim; s->vocab = c.vocab_size;
+    s->qd = c.n_heads * c.head_dim; s->kvd = c.n_heads_kv * c.head_dim;
+    s->max_seq = caches[0].max_seq;
+    s->max_pos = caches[0].max_seq;                   // generate.c:142
+    s->eps = c.rms_eps; s->rope_base = c.rope_freq_base; s->emb_scale = c.embedding_scale;
+    s->rope_mode = c.rope_type == ROPE_NEOX ? 2u : 1u;
+    s->act_gelu = c.ffn_act == ACT_GELU;
+    bool ok = s->n_kv > 0 && s->n_heads % s->n_kv == 0 && s->hd > 0 && caches[0].dim == s->kvd;
+    if (!ok) set_error("llama session: inconsistent heads/cache (heads %u kv %u hd %u cache dim %u)",
+                       s->n_heads, s->n_kv, s->hd, caches[0].dim);
+    ok = ok && weight(s, m->embeddings, c.vocab_size, c.dim, &s->tok);
+    ok = ok && weight(s, m->lm_head, c.vocab_size, c.dim, &s->head);
+    s->fnw = ok ? vec(s, m->final_norm, c.dim) : nullptr;
+    ok = ok && s->fnw;
+    s->layers.resize(c.n_layers);
+    for (u32 l = 0; ok && l < c.n_layers; l++) {
+        const DecoderLayer& L = m->layers[l];
+        auto& W = s->layers[l];
+        ok = weight(s, L.q_proj, s->qd, c.dim, &W.q) && weight(s, L.k_proj, s->kvd, c.dim, &W.k) &&
+             weight(s, L.v_proj, s->kvd, c.dim, &W.v) && weight(s, L.o_proj, c.dim, s->qd, &W.o) &&
+             weight(s, L.gate_proj, c.ffn_dim, c.dim, &W.gate) && weight(s, L.up_proj, c.ffn_dim, c.dim, &W.up) &&
+             weight(s, L.down_proj, c.dim, c.ffn_dim, &W.down);
+        if (ok) { W.n1w = vec(s, L.attn_norm, c.dim); W.n2w = vec(s, L.ffn_norm, c.dim); ok = W.n1w && W.n2w; }
+        if (ok && c.qkv_bias) {
+            W.bq = vec(s, L.q_bias, s->qd); W.bk = vec(s, L.k_bias, s->kvd); W.bv = vec(s, L.v_bias, s->kvd);
+            ok = W.bq && W.bk && W.bv;
+        }
+    }
+    // the tok table is read one row per step, not whole
+    if (ok) s->weight_bytes -= s->tok.row_bytes * (s->tok.rows - 1);
+    ok = ok && finish_build(s);
+    if (!ok) { destroy(s); return nullptr; }
+    g_sessions.push_back(s);
+    return s;
+}
+
+llamini_session* build_gpt2(GPT2Model* m, KVCache* caches) {
+    if (!ensure_device()) return nullptr;
+    const GPT2Config& c = m->cfg;
+    auto* s = new llamini_session();
+    s->kind = 1;
+    s->model = m;
+    s->caches = caches;
+    s->cache_max_seq = caches[0].max_seq;
+    s->cache_dim = caches[0].dim;
+    s->n_layers = c.n_layers; s->dim = c.dim; s->n_heads = c.n_heads; s->n_kv = c.n_heads;
+    s->hd = c.n_heads ? c.dim / c.n_heads : 0; s->ffn = c.ffn_dim; s->vocab = c.vocab_size;
+    s->qd = c.dim; s->kvd = c.dim;
+    s->max_seq = caches[0].max_seq;
+    s->max_pos = caches[0].max_seq < c.n_ctx ? caches[0].max_seq : c.n_ctx;   // gpt2.c:205
+    s->eps = c.ln_eps; s->rope_mode = 0; s->emb_scale = 1.0f;
+    bool ok = s->hd > 0 && caches[0].dim == c.dim;
+    if (!ok) set_error("gpt2 session: cache dim %u != model dim %u", caches[0].dim, c.dim);
+    ok = ok && weight(s, m->token_embd, c.vocab_size, c.dim, &s->tok);
+    ok = ok && weight(s, m->pos_embd, c.n_ctx, c.dim, &s->pos_tab);
+    ok = ok && weight(s, m->lm_head, c.vocab_size, c.dim, &s->head);
+    if (ok) { s->fnw = vec(s, m->output_norm_w, c.dim); s->fnb = vec(s, m->output_norm_b, c.dim); ok = s->fnw && s->fnb; }
+    s->layers.resize(c.n_layers);
+    for (u32 l = 0; ok && l < c.n_layers; l++) {
+        const GPT2Layer& L = m->layers[l];
+        auto& W = s->layers[l];
+        ok = weight(s, L.attn_qkv_w, 3 * c.dim, c.dim, &W.q) && weight(s, L.attn_out_w, c.dim, c.dim, &W.o) &&
+             weight(s, L.ffn_up_w, c.ffn_dim, c.dim, &W.up) && weight(s, L.ffn_down_w, c.dim, c.ffn_dim, &W.down);
+        if (ok) {
+            W.n1w = vec(s, L.attn_norm_w, c.dim); W.n1b = vec(s, L.attn_norm_b, c.dim);
+            W.n2w = vec(s, L.ffn_norm_w, c.dim); W.n2b = vec(s, L.ffn_norm_b, c.dim);
+            W.bq = vec(s, L.attn_qkv_b, 3 * c.dim); W.bo = vec(s, L.attn_out_b, c.dim);
+            W.bup = vec(s, L.ffn_up_b, c.ffn_dim); W.bdown = vec(s, L.ffn_down_b, c.dim);
+            ok = W.n1w && W.n1b && W.n2w && W.n2b && W.bq && W.bo && W.bup && W.bdown;
+        }
+    }
+    if (ok) {
+        s->weight_bytes -= s->tok.row_bytes * (s->tok.rows - 1);
+        s->weight_bytes -= s->pos_tab.row_bytes * (s->pos_tab.rows - 1);
+    }
+    ok = ok && finish_build(s);
+    if (!ok) { destroy(s); return nullptr; }
+    g_sessions.push_back(s);
+    return s;
+}
+
+// ---------------------------------------------------------------- running
+
+bool write_state(llamini_session* s, u32 pos, u32 n_prompt, bool reset_nll) {
+    cudaStream_t st = stream();
+    if (!LM_CUDA(cudaStreamSynchronize(st))) return false;   // st_host is reused
+    s->st_host->pos = pos;
+    s->st_host->n_prompt = n_prompt;
+    s->st_host->trace = 0;
+    s->st_host->pad = 0;
+    s->st_host->argmax_key = 0;
+    s->st_host->nll = 0.0;
+    s->st_host->nll_count = 0;
+    const size_t n = reset_nll ? sizeof(StepState) : offsetof(StepState, nll);
+    if (!LM_CUDA(cudaMemcpyAsync(s->st, s->st_host, n, cudaMemcpyHostToDevice, st))) return false;
+    s->pos = pos;
+    s->n_prompt = n_prompt;
+    return true;
+}
+
+bool run_steps(llamini_session* s, u32 n) {
+    if ((u64)s->pos + n > s->max_pos) {
+        set_error("position %u + %u steps passes the cache capacity %u", s->pos, n, s->max_pos);
+        return false;
+    }
+    cudaStream_t st = stream();
+    if (s->trace_on) {
+        if (!s->g_trace && !capture(s, 1, true, false, &s->g_trace)) return false;
+        for (u32 i = 0; i < n; i++) if (!LM_CUDA(cudaGraphLaunch(s->g_trace, st))) return false;
+        s->pos += n;
+        return true;
+    }
+    u32 left = n;
+    while (left >= kStepsPerGraph) {
+        if (!LM_CUDA(cudaGraphLaunch(s->g_many, st))) return false;
+        left -= kStepsPerGraph;
+    }
+    while (left--) if (!LM_CUDA(cudaGraphLaunch(s->g_one, st))) return false;
+    s->pos += n;
+    return true;
+}
+
+void set_cur_seq(llamini_session* s, u32 n) {
+    for (u32 l = 0; l < s->n_layers; l++) s->caches[l].cur_seq = n;
+}
+void set_cur_seq(llamini_session* s) { set_cur_seq(s, s->pos); }
+
+}  // namespace
+
+void drop_sessions_for_model(const void* model) {
+    drop_where([](const llamini_session* s, const void* k) { return s->model == k; }, model);
+}
+void drop_sessions_for_gguf(const GGUFFile* gf) {
+    drop_where([](const llamini_session* s, const void* k) { return s->gf == k; }, gf);
+}
+void drop_all_sessions() {
+    for (auto* s : g_sessions) destroy(s);
+    g_sessions.clear();
+}
+
+// Shared by forward_step and gpt2_forward_step.
+static void forward_one(llamini_session* s, u32 pos, u32 token, f32* logits_out) {
+    if (!s) { if (logits_out) memset(logits_out, 0, 4); return; }
+    if (pos >= s->max_seq) { set_error("forward: position %u outside the cache (%u)", pos, s->max_seq); return; }
+    cudaStream_t st = stream();
+    if (!write_state(s, pos, 0xFFFFFFFFu, false)) return;
+    if (!LM_CUDA(cudaMemcpyAsync(s->tokens + pos, &token, 4, cudaMemcpyHostToDevice, st))) return;
+    const u32 saved = s->max_pos;
+    s->max_pos = s->max_seq;
+    bool ok = run_steps(s, 1);
+    s->max_pos = saved;
+    if (!ok) return;
+    if (logits_out && !LM_CUDA(cudaMemcpyAsync(logits_out, s->logits, (size_t)s->vocab * 4, cudaMemcpyDeviceToHost, st))) return;
+    LM_CUDA(cudaStreamSynchronize(st));
+    set_cur_seq(s);
+}
+
+// generate.c:122-167 / gpt2.c:194-229.
+static u32 generate(llamini_session* s, u32* input, u32 n_in, u32* out, u32 max_gen, u32 eos, f32 temp, f32 top_p) {
+    memcpy(out, input, (size_t)n_in * sizeof(u32));
+    if (!s) return n_in;
+    struct timespec t0, t1;
+    clock_gettime(CLOCK_MONOTONIC, &t0);
+    u32 total = n_in;
+    cudaStream_t st = stream();
+    if (temp > 0.0f) {
+        // sampled decoding: the draw uses the host rand() stream (generate.c:50)
+        std::vector<f32> logits(s->vocab);
+        for (u32 pos = 0; pos < s->max_pos; pos++) {
+            forward_one(s, pos, out[pos], logits.data());
+            if (pos + 1 < n_in) continue;
+            u32 t = sample_token(logits.data(), s->vocab, temp, top_p);
+            out[total++] = t;
+            if (t == eos || total - n_in >= max_gen) break;
+        }
+    } else {
+        // Forward passes the reference runs without an early EOS: every prompt
+        // position, then one per generated token, the last one producing the
+        // max_gen-th token (at least one token is always generated).
+        const u32 gen_target = max_gen > 0 ? max_gen : 1;
+        u64 want = (n_in > 0 ? (u64)n_in - 1 : 0) + gen_target;
+        if (want > s->max_pos) want = s->max_pos;
+        const u32 first = n_in > 0 ? n_in : 1;
+        if (!write_state(s, 0, first, true)) return total;
+        if (!LM_CUDA(cudaMemcpyAsync(s->tokens, out, (size_t)first * 4, cudaMemcpyHostToDevice, st))) return total;
+        const bool eos_possible = eos < s->vocab;
+        u32 done = 0;
+        // prefill positions produce no tokens; run them in one go
+        u32 pre = n_in > 1 ? n_in - 1 : 0;
+        if (pre > want) pre = (u32)want;
+        if (pre && !run_steps(s, pre)) return total;
+        done = pre;
+        std::vector<u32> buf;
+        u32 last = done;                                   // positions run, as the reference counts them
+        while (done < want) {
+            u32 chunk = (u32)(want - done);
+            if (eos_possible && chunk > 16) chunk = 16;
+            if (!run_steps(s, chunk)) break;
+            // tokens produced: positions done+1 .. done+chunk
+            buf.resize(chunk);
+            if (!LM_CUDA(cudaMemcpyAsync(buf.data(), s->tokens + done + 1, (size_t)chunk * 4, cudaMemcpyDeviceToHost, st)) ||
+                !LM_CUDA(cudaStreamSynchronize(st)))
+                break;
+            bool stop = false;
+            for (u32 i = 0; i < chunk; i++) {
+                const u32 p = done + i;                       // step position
+                if (p + 1 < n_in) continue;
+                out[total++] = buf[i];
+                last = p + 1;
+                if (buf[i] == eos || total - n_in >= gen_target) { stop = true; break; }
+            }
+            done += chunk;
+            if (!stop) last = done;
+            if (stop) break;
+        }
+        set_cur_seq(s, last);
+    }
+    clock_gettime(CLOCK_MONOTONIC, &t1);
+    const u32 ng = total - n_in;
+    const double el = (double)(t1.tv_sec - t0.tv_sec) + (double)(t1.tv_nsec - t0.tv_nsec) * 1e-9;
+    if (ng > 0 && el > 0.0) fprintf(stderr, "[%u tokens in %.2fs, %.2f tok/s]\n", ng, el, ng / el);
+    return total;
+}
+
+// generate.c:169-197 / gpt2.c:231-256.
+static f32 perplexity(llamini_session* s, const u32* tokens, u32 n) {
+    if (!s) return -1.0f;
+    for (u32 l = 0; l < s->n_layers; l++) kv_cache_reset(&s->caches[l]);
+    u32 steps = 0;
+    while (steps + 1 < n && steps < s->max_pos) steps++;
+    if (steps == 0) return -1.0f;
+    cudaStream_t st = stream();
+    if (!s->g_nll && !capture(s, 1, false, true, &s->g_nll)) return -1.0f;
+    if (!write_state(s, 0, n, true)) return -1.0f;
+    const u32 ncopy = n < s->max_seq + 1 ? n : s->max_seq + 1;
+    if (!LM_CUDA(cudaMemcpyAsync(s->tokens, tokens, (size_t)ncopy * 4, cudaMemcpyHostToDevice, st))) return -1.0f;
+    for (u32 i = 0; i < steps; i++) if (!LM_CUDA(cudaGraphLaunch(s->g_nll, st))) return -1.0f;
+    s->pos = steps;
+    if (!LM_CUDA(cudaMemcpyAsync(s->st_host, s->st, sizeof(StepState), cudaMemcpyDeviceToHost, st)) ||
+        !LM_CUDA(cudaStreamSynchronize(st)))
+        return -1.0f;
+    set_cur_seq(s);
+    if (s->st_host->nll_count == 0) return -1.0f;
+    return expf((f32)(s->st_host->nll / s->st_host->nll_count));
+}
+
+static llamini_session* llama_session(LLaMAModel* m, KVCache* c) {
+    if (!m || !c) { set_error("null model or caches"); return nullptr; }
+    llamini_session* s = find(m, c);
+    return s ? s : build_llama(m, c);
+}
+static llamini_session* gpt2_session(GPT2Model* m, KVCache* c) {
+    if (!m || !c) { set_error("null model or caches"); return nullptr; }
+    llamini_session* s = find(m, c);
+    return s ? s : build_gpt2(m, c);
+}
+
+}  // namespace lm
+
+extern "C" {
+
+void forward_step(LLaMAModel* model, KVCache* caches, u32 pos, u32 token_id, f32* logits_out) {
+    lm::forward_one(lm::llama_session(model, caches), pos, token_id, logits_out);
+}
+
+u32 generate_autoregressive(LLaMAModel* model, KVCache* caches, u32* input_tokens, u32 in_token_count,
+                            u32* out_tokens, u32 max_gen_tokens, u32 eos_id, f32 temp, f32 top_p) {
+    return lm::generate(lm::llama_session(model, caches), input_tokens, in_token_count, out_tokens,
+                        max_gen_tokens, eos_id, temp, top_p);
+}
+
+f32 compute_perplexity(LLaMAModel* model, KVCache* caches, const u32* tokens, u32 n_tokens) {
+    return lm::perplexity(lm::llama_session(model, caches), tokens, n_tokens);
+}
+
+void gpt2_forward_step(GPT2Model* model, KVCache* caches, u32 pos, u32 token_id, f32* logits_out) {
+    lm::forward_one(lm::gpt2_session(model, caches), pos, token_id, logits_out);
+}
+
+u32 gpt2_generate(GPT2Model* model, KVCache* caches, u32* input_tokens, u32 in_token_count,
+                  u32* out_tokens, u32 max_gen_tokens, u32 eos_id, f32 temp, f32 top_p) {
+    return lm::generate(lm::gpt2_session(model, caches), input_tokens, in_token_count, out_tokens,
+                        max_gen_tokens, eos_id, temp, top_p);
+}
+
+f32 gpt2_compute_perplexity(GPT2Model* model, KVCache* caches, const u32* tokens, u32 n_tokens) {
+    return lm::perplexity(lm::gpt2_session(model, caches), tokens, n_tokens);
+}
+
+llamini_session* llamini_llama_session(LLaMAModel* model, KVCache* caches) { return lm::llama_session(model, caches); }
+llamini_session* llamini_gpt2_session(GPT2Model* model, KVCache* caches) { return lm::gpt2_session(model, caches); }
+
+int llamini_session_begin(llamini_session* s, const u32* prompt, u32 n_prompt) {
+    if (!s || n_prompt == 0 || n_prompt > s->max_seq) { lm::set_error("session_begin: bad prompt"); return -1; }
+    if (!lm::write_state(s, 0, n_prompt, true)) return -1;
+    return LM_CUDA(cudaMemcpyAsync(s->tokens, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, lm::stream())) &&
+                   LM_CUDA(cudaStreamSynchronize(lm::stream()))
+               ? 0 : -1;
+}
+
+int llamini_session_step(llamini_session* s, u32 n_steps) {
+    if (!s) return -1;
+    return lm::run_steps(s, n_steps) ? 0 : -1;
+}
+
+int llamini_session_tokens(llamini_session* s, u32* out, u32 n) {
+    if (!s) return -1;
+    const u32 valid = s->pos + 1 > s->n_prompt ? s->pos + 1 : s->n_prompt;
+    const u32 k = n < valid ? n : valid;
+    if (!LM_CUDA(cudaMemcpyAsync(out, s->tokens, (size_t)k * 4, cudaMemcpyDeviceToHost, lm::stream())) ||
+        !LM_CUDA(cudaStreamSynchronize(lm::stream())))
+        return -1;
+    lm::set_cur_seq(s);
+    return (int)valid;
+}
+
+int llamini_session_logits(llamini_session* s, f32* out) {
+    if (!s) return -1;
+    return LM_CUDA(cudaMemcpyAsync(out, s->logits, (size_t)s->vocab * 4, cudaMemcpyDeviceToHost, lm::stream())) &&
+                   LM_CUDA(cudaStreamSynchronize(lm::stream()))
+               ? 0 : -1;
+}
+
+u32 llamini_session_pos(llamini_session* s) { return s ? s->pos : 0; }
+u64 llamini_session_weight_bytes(llamini_session* s) { return s ? s->weight_bytes : 0; }
+u64 llamini_session_kv_bytes_per_pos(llamini_session* s) {
+    return s ? (u64)s->n_layers * 2 * s->n_kv * s->hd * 2 : 0;
+}
+
+int llamini_session_trace(llamini_session* s, int enable) {
+    if (!s) return -1;
+    s->trace_on = enable != 0;
+    return 0;
+}
+
+int llamini_session_trace_read(llamini_session* s, f32* out) {
+    if (!s) return -1;
+    return LM_CUDA(cudaMemcpyAsync(out, s->trace, (size_t)s->n_layers * s->dim * 4, cudaMemcpyDeviceToHost, lm::stream())) &&
+                   LM_CUDA(cudaStreamSynchronize(lm::stream()))
+               ? 0 : -1;
+}
+
+}  // extern "C"
