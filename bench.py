@@ -1,0 +1,363 @@
+"""Decode benchmark: llama_1b (LLaMA 1.1B shape, Q4_K_M mix), batch 1.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one greedy decode token of the workload (all 22 layers + lm_head +
+argmax) at positions 127.., after a 128-token prompt. The weights (624 MB of
+quantized blocks) exceed the 126 MB L2, so every step streams them from HBM.
+
+  value   tok/s over exactly K device-timed steps (CUDA events on the library's
+          stream, max over ranks), inputs already resident in GPU memory
+  e2e     tok/s through generate_autoregressive (the reference's public call)
+          from host buffers: a one-token prompt, 256 greedy tokens, wall clock
+  roofline  the fused dequant-GEMV kernel at the step's largest launch shape
+          (gate+up, 11264 x 2048 Q4_K = 12.98 MB/launch) timed with CUDA events
+          over 22 distinct weight copies (286 MB > L2); peak = measured HBM copy
+          bandwidth in MEASURED_PEAKS.json
+  cpu_baseline  the reference's own C (oracle/_ref) on the host cores, a bounded
+          sample of the same decode loop
+
+With --gpus N (torchrun) every rank decodes its own sequence (independent
+replicas; the path has no cross-sequence exchange) and value sums the ranks.
+--impl reference times the reference's CPU path on the same workload instead.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+WORKLOAD = "llama_1b"
+N_PROMPT = 128
+METRIC = "decode tok/s (llama_1b Q4_K_M, batch 1)"
+
+
+def _load(name, path):
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, path)
+    m = importlib.util.module_from_spec(spec)
+    sys.modules[name] = m
+    spec.loader.exec_module(m)
+    return m
+
+
+def pkg():
+    return _load("llamini_b200", os.path.join(ROOT, "llamini.cpp_b200", "__init__.py"))
+
+
+def synthetic():
+    return _load("llamini_b200_synthetic", os.path.join(ROOT, "llamini.cpp_b200", "synthetic.py"))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clock and throttle reasons while running."""
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        q = "clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
+            "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + q,
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 6:
+                self.rows.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[2:]) if v.strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(self.rows[0][1]) if self.rows[0][1].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def init_dist(ws, local, backend):
+    import torch
+    import torch.distributed as dist
+    if ws > 1 and not dist.is_initialized():
+        import datetime
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600))
+    return dist if ws > 1 else None
+
+
+def workload_path(rank, dist):
+    S = synthetic()
+    directory = os.environ.get("LLAMINI_WORKDIR", "/tmp/llamini_b200")
+    if rank == 0:
+        S.ensure_workload(WORKLOAD, directory)
+    if dist:
+        dist.barrier()
+    return S.ensure_workload(WORKLOAD, directory)
+
+
+# --------------------------------------------------------------------------- ours
+
+def kernel_roofline(lm, torch, stream, hbm_peak, peak_kind):
+    """Dominant kernel: the fused GEMV at the gate+up launch shape of a layer."""
+    S = synthetic()
+    L = lm.lib()
+    rows, cols, layers = 2 * 5632, 2048, 22
+    raw = S.random_blocks(np.random.default_rng(0), S.Q4_K, rows * cols)
+    nbytes = raw.size
+    w = torch.empty((layers, nbytes + 16), dtype=torch.uint8, device="cuda")
+    host = torch.from_numpy(raw)
+    for i in range(layers):
+        w[i, :nbytes].copy_(host)
+    x = torch.randn(cols, device="cuda", dtype=torch.float32)
+    y = torch.empty(rows, device="cuda", dtype=torch.float32)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(layers):                             # warm-up pass
+            assert L.llamini_gemv_device(12, w[i].data_ptr(), rows, cols, x.data_ptr(), 1, y.data_ptr()) == 0
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 5
+        e0.record(stream)
+        for _ in range(reps):
+            for i in range(layers):
+                L.llamini_gemv_device(12, w[i].data_ptr(), rows, cols, x.data_ptr(), 1, y.data_ptr())
+        e1.record(stream)
+    torch.cuda.synchronize()
+    per_launch_s = e0.elapsed_time(e1) / 1e3 / (reps * layers)
+    algo = nbytes + cols * 4 + rows * 4
+    achieved = algo / per_launch_s / 1e9
+    del w
+    return {"kernel": "gemv_fused_kernel (Q4_K, 11264x2048, gate+up shape)", "bound": "hbm",
+            "achieved": round(achieved, 1), "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 4), "algorithmic_bytes_per_launch": algo,
+            "us_per_launch": round(per_launch_s * 1e6, 2), "traffic": None}
+
+
+def run_ours(args, ws, rank, local):
+    import torch
+    dist = init_dist(ws, local, "nccl")
+    lm = pkg()
+    L = lm.lib()
+    torch.cuda.set_device(local)
+    if L.llamini_set_device(local) != 0:
+        raise RuntimeError(lm.last_error())
+    path = workload_path(rank, dist)
+    model = lm.Model(path, max_seq=2048)
+    sess = model.session()
+    stream = torch.cuda.ExternalStream(L.llamini_stream())
+    n_prompt = args.prompt
+    prompt = synthetic().workload_prompt(WORKLOAD, n_prompt)
+    weight_bytes = L.llamini_session_weight_bytes(sess)
+    kv_per_pos = L.llamini_session_kv_bytes_per_pos(sess)
+    if n_prompt + args.warmup + args.steps > model.max_seq:
+        raise SystemExit("steps + warmup exceed the 2048-position cache")
+    hbm_peak, peak_kind = peaks()
+
+    assert L.llamini_session_begin(sess, lm.ptr(prompt), n_prompt) == 0, lm.last_error()
+    assert L.llamini_session_step(sess, n_prompt - 1) == 0, lm.last_error()   # prefill
+    assert L.llamini_session_step(sess, args.warmup) == 0
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pos0 = L.llamini_session_pos(sess)
+    with Clocks(local) as clk:
+        time.sleep(0.3)
+        e0.record(stream)
+        assert L.llamini_session_step(sess, args.steps) == 0, lm.last_error()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        # e2e through the public call (host buffers), 256 tokens from a 1-token prompt
+        e2e_tok, e2e_s = 256, float("nan")
+        if not args.no_e2e:
+            bos = np.array([1], np.uint32)
+            model.generate(bos, 8)                             # warm
+            t = time.perf_counter()
+            out = model.generate(bos, e2e_tok)
+            e2e_s = time.perf_counter() - t
+            assert len(out) == e2e_tok + 1
+        roof = None
+        if rank == 0 and not args.no_kernel_roofline:
+            roof = kernel_roofline(lm, torch, stream, hbm_peak, peak_kind)
+    t_max = ms
+    e2e_max = e2e_s
+    if dist:
+        tt = torch.tensor([ms, e2e_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_max, e2e_max = float(tt[0]), float(tt[1])
+    if rank == 0:
+        steps = args.steps
+        value = ws * steps / (t_max / 1e3)
+        ctx_mean = pos0 + (steps - 1) / 2 + 1
+        step_bytes = weight_bytes + kv_per_pos * ctx_mean
+        step_s = t_max / 1e3 / steps
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": ws,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": round(t_max / steps, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": "llama_1b: LLaMA 1.1B shape (22 layers, dim 2048, 32/4 heads, ffn 5632, "
+                                   "vocab 32000), Q4_K_M mix, seed 0; batch 1 per GPU; 128-token prompt, "
+                                   "timed decode positions %d..%d" % (pos0, pos0 + steps - 1) +
+                                   ("" if n_prompt == N_PROMPT else " (prompt %d)" % n_prompt),
+                       "global_batch": ws, "seq_len": pos0 + steps, "parallelism": "replicas x%d" % ws,
+                       "l2": "weights %.0f MB > 126 MB L2, streamed every step" % (weight_bytes / 1e6)},
+            "weight_stream_gbs": round(step_bytes / step_s / 1e9, 1),
+            "step_roofline": {"bytes_per_step": int(step_bytes), "achieved_gbs": round(step_bytes / step_s / 1e9, 1),
+                              "peak": hbm_peak, "frac": round(step_bytes / step_s / 1e9 / hbm_peak, 4)},
+            "roofline": roof,
+            "e2e": {"value": round(ws * e2e_tok / e2e_max, 2), "unit": "tok/s",
+                    "h2d_bytes_per_step": round(4 / e2e_tok, 4), "d2h_bytes_per_step": 4,
+                    "call": "generate_autoregressive, 1-token prompt, 256 greedy tokens, wall clock"},
+            "gpu_launches": steps * (1 + 5 * 22 + 2),
+            "clocks": clk.summary(),
+        }
+        if ws == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(path)
+        print(json.dumps(line), flush=True)
+    model.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# --------------------------------------------------------------------------- reference (CPU)
+
+def _ref_lib():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    ref = O.reference()
+    if ref is None:
+        return None, O
+    return ref, O
+
+
+def cpu_baseline(path, budget_s=15.0):
+    """The reference's own C on the host: a 4-token prompt, then greedy decode
+    steps until ~budget_s of decode time (the lazy path is single-threaded)."""
+    ref, O = _ref_lib()
+    if ref is None:
+        return {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference", "sample": "reference not built"}
+    os.environ.setdefault("LLAMINI_THREADS", str(os.cpu_count()))
+    assert ref.drv_open(path.encode(), 0) == 0
+    prompt = synthetic().workload_prompt(WORKLOAD, 4)
+    ref.drv_time_decode(0, int(prompt[0]), 1, None)
+    for p in range(1, 4):
+        ref.drv_time_decode(p, int(prompt[p]), 1, None)
+    n, el, pos = 0, 0.0, 4
+    tok = int(prompt[3])
+    while el < budget_s and n < 64:
+        el += ref.drv_time_decode(pos, tok, 1, None)
+        pos += 1
+        n += 1
+    ref.drv_close()
+    return {"value": round(n / el, 4), "unit": "tok/s", "cores": 1, "kind": "reference",
+            "sample": "%d greedy decode steps of llama_1b at positions 4..%d after a 4-token prompt; "
+                      "the reference's lazy Q4_K path is single-threaded (model.c:147-158)" % (n, pos - 1)}
+
+
+def run_reference(args, ws, rank, local):
+    if rank != 0:
+        return
+    ref, O = _ref_lib()
+    if ref is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libllamini_ref.so was not built"}))
+        return
+    path = synthetic().ensure_workload(WORKLOAD)
+    os.environ.setdefault("LLAMINI_THREADS", str(os.cpu_count()))
+    assert ref.drv_open(path.encode(), 0) == 0
+    prompt = synthetic().workload_prompt(WORKLOAD, 4)
+    for p in range(4):
+        ref.drv_time_decode(p, int(prompt[p]), 1, None)
+    pos = 4
+    for _ in range(args.warmup):
+        ref.drv_time_decode(pos, 5, 1, None)
+        pos += 1
+    # each step is one decode token; stop early (and say so) past ~240 s
+    el, n = 0.0, 0
+    while n < args.steps and el < 240.0:
+        el += ref.drv_time_decode(pos, 5, 1, None)
+        pos += 1
+        n += 1
+    ref.drv_close()
+    value = n / el
+    sample = "%d of %d requested decode steps of llama_1b (positions %d..%d, 4-token prompt), single-threaded " \
+             "lazy Q4_K path (model.c:147-158)" % (n, args.steps, pos - n, pos - 1)
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "tok/s", "n_gpus": ws,
+            "steps": n, "warmup": args.warmup, "ms_per_step": round(el / n * 1e3, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "llama_1b decode, batch 1, reference CPU path", "global_batch": 1,
+                       "seq_len": pos, "parallelism": "none"},
+            "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": 1, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the generate_autoregressive timing")
+    ap.add_argument("--no-kernel-roofline", action="store_true", help="skip the isolated GEMV timing")
+    ap.add_argument("--prompt", type=int, default=N_PROMPT, help="prompt length before the timed steps")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    ws, rank, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, ws, rank, local)
+    else:
+        run_ours(args, ws, rank, local)
+
+
+if __name__ == "__main__":
+    main()

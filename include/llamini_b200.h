@@ -103,8 +103,14 @@ u32 llamini_session_pos(llamini_session* s);
  * one embedding row (the quantized sizes of gguf.c's block formats). */
 u64 llamini_session_weight_bytes(llamini_session* s);
 
-/* KV-cache bytes per cached position (all layers, K and V, fp16). */
+/* KV-cache bytes per cached position (all layers, K and V). */
 u64 llamini_session_kv_bytes_per_pos(llamini_session* s);
+
+/* Element type of the device KV cache of sessions created from now on:
+ * 0 = f32 (default; the reference keeps an f32 cache, model.c:222-224, and the
+ * f32 cache holds the 1e-3 parity bar), 1 = fp16 (half the cache traffic; on
+ * the synthetic models its rounding moves logits by ~2e-3 relative L2). */
+int llamini_set_kv_f16(int enable);
 
 /* Per-layer residual stream of the most recent step: n_layers x dim floats,
  * captured when `enable` was set before the step ran. For parity tests. */

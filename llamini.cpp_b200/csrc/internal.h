@@ -37,6 +37,9 @@ void dev_free(void* p);
 struct TypeInfo { uint32_t block_elems, block_bytes; };
 bool type_info(uint32_t type, TypeInfo* ti);
 uint64_t type_bytes(uint32_t type, uint64_t n_elems);   // 0 if unsupported/misaligned
+// Byte alignment the decoders need for a tensor of this type (16 for the
+// K-quants read with 128-bit loads, the element size for F32/F16, else 1).
+uint32_t type_align(uint32_t type);
 
 // A weight matrix in GPU memory: the GGUF bytes of `rows` rows of `cols`
 // elements each, stored unchanged (row r starts at ptr + r*row_bytes).
@@ -91,6 +94,9 @@ struct GemvArgs {
 };
 
 bool launch_gemv(const GemvArgs& a, cudaStream_t st);
+// Tensor-core variant (k_gemv_mma.cu); *handled is false when some segment's
+// format has no tensor-core path, and launch_gemv then uses the CUDA-core kernel.
+bool launch_gemv_mma(const GemvArgs& a, cudaStream_t st, bool* handled);
 
 // Plain multi-column GEMV used by llamini_gemv_* (no fusion).
 bool launch_gemv_plain(uint32_t type, const uint8_t* w, uint32_t rows, uint32_t cols,
@@ -121,8 +127,9 @@ bool launch_embed(const EmbedArgs& a, cudaStream_t st);
 struct AttnArgs {
     StepState* st;
     const float* qkv;      // q [n_heads*hd] | k [n_kv*hd] | v [n_kv*hd]
-    uint16_t* kc;          // this layer's cache: [n_kv][max_seq][hd] fp16 bits
-    uint16_t* vc;
+    void* kc;              // this layer's cache: [n_kv][max_seq][hd], f32 or fp16
+    void* vc;
+    uint32_t kv_f16;       // 1: fp16 elements, 0: f32 elements
     float* out;            // [n_heads*hd]
     float* part;           // [n_heads][n_split][hd + 2] partial results
     uint32_t* counter;     // [n_kv] completion counters (return to 0 after use)

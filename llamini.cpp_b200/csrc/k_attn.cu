@@ -20,8 +20,12 @@ namespace lm {
 
 constexpr int kAttnThreads = 128;
 
-__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
-__device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+// Cache element access: f32 keeps the reference's precision (model.c:222-224
+// stores f32), fp16 halves the cache traffic.
+__device__ __forceinline__ float kv_load(const float* p) { return *p; }
+__device__ __forceinline__ float kv_load(const __half* p) { return __half2float(*p); }
+__device__ __forceinline__ void kv_store(float* p, float v) { *p = v; }
+__device__ __forceinline__ void kv_store(__half* p, float v) { *p = __float2half_rn(v); }
 
 // Rotate one (a, b) pair of element index `i` of a head (model.c:31-58).
 __device__ __forceinline__ void rope_pair(float* a, float* b, uint32_t pos, uint32_t expo_num,
@@ -44,6 +48,7 @@ __device__ void rope_head(float* v, uint32_t hd, uint32_t pos, uint32_t mode, fl
     }
 }
 
+template <typename KV>
 __global__ void __launch_bounds__(kAttnThreads)
 attn_decode_kernel(const AttnArgs a) {
     extern __shared__ float sm[];
@@ -75,12 +80,12 @@ attn_decode_kernel(const AttnArgs a) {
     for (uint32_t i = 0; i < G; i++) rope_head(qs + i * hd, hd, pos, a.rope, a.rope_base);
     if (has_new) rope_head(kv, hd, pos, a.rope, a.rope_base);
     __syncthreads();
-    uint16_t* kc = a.kc + (uint64_t)g * a.max_seq * hd;
-    uint16_t* vc = a.vc + (uint64_t)g * a.max_seq * hd;
+    KV* kc = reinterpret_cast<KV*>(a.kc) + (uint64_t)g * a.max_seq * hd;
+    KV* vc = reinterpret_cast<KV*>(a.vc) + (uint64_t)g * a.max_seq * hd;
     if (has_new) {
         for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) {
-            kc[(uint64_t)pos * hd + i] = f2h(kv[i]);
-            vc[(uint64_t)pos * hd + i] = f2h(kv[hd + i]);
+            kv_store(kc + (uint64_t)pos * hd + i, kv[i]);
+            kv_store(vc + (uint64_t)pos * hd + i, kv[hd + i]);
         }
     }
     __syncthreads();
@@ -90,10 +95,10 @@ attn_decode_kernel(const AttnArgs a) {
 
     // scores: warp per position, lanes over head_dim, all G heads at once
     for (uint32_t t = t0 + warp; t < t1; t += nw) {
-        const uint16_t* kt = kc + (uint64_t)t * hd;
+        const KV* kt = kc + (uint64_t)t * hd;
         for (uint32_t i = 0; i < G; i++) {
             float s = 0.f;
-            for (uint32_t d = lane; d < hd; d += 32) s = fmaf(qs[i * hd + d], h2f(kt[d]), s);
+            for (uint32_t d = lane; d < hd; d += 32) s = fmaf(qs[i * hd + d], kv_load(kt + d), s);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
             if (lane == 0) sc[i * maxc + (t - t0)] = s / rscale;
@@ -120,7 +125,7 @@ attn_decode_kernel(const AttnArgs a) {
         float* dst = a.part + ((uint64_t)h * a.n_split + split) * stride;
         for (uint32_t d = lane; d < hd; d += 32) {
             float o = 0.f;
-            for (uint32_t t = t0; t < t1; t++) o = fmaf(sc[i * maxc + (t - t0)], h2f(vc[(uint64_t)t * hd + d]), o);
+            for (uint32_t t = t0; t < t1; t++) o = fmaf(sc[i * maxc + (t - t0)], kv_load(vc + (uint64_t)t * hd + d), o);
             if (a.n_split == 1) a.out[(uint64_t)h * hd + d] = o / l;
             else dst[2 + d] = o;
         }
@@ -161,7 +166,8 @@ attn_decode_kernel(const AttnArgs a) {
 }
 
 bool attn_init() {
-    return LM_CUDA(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    return LM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)) &&
+           LM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
 }
 
 bool launch_attention(const AttnArgs& a, cudaStream_t st) {
@@ -174,7 +180,8 @@ bool launch_attention(const AttnArgs& a, cudaStream_t st) {
     size_t smem = ((size_t)G * a.hd + 2 * a.hd + (size_t)G * maxc) * sizeof(float);
     if (smem > 200 * 1024) { set_error("attention: shared memory %zu too large", smem); return false; }
     dim3 grid(a.n_kv, a.n_split);
-    attn_decode_kernel<<<grid, kAttnThreads, smem, st>>>(a);
+    if (a.kv_f16) attn_decode_kernel<__half><<<grid, kAttnThreads, smem, st>>>(a);
+    else attn_decode_kernel<float><<<grid, kAttnThreads, smem, st>>>(a);
     return LM_CUDA(cudaGetLastError());
 }
 

@@ -17,6 +17,7 @@
 #include "quant.cuh"
 
 #include <cuda_fp16.h>
+#include <cstdlib>
 
 namespace lm {
 
@@ -257,8 +258,22 @@ bool launch_gemv(const GemvArgs& in, cudaStream_t st) {
     if (a.nseg == 0 || a.nseg > (uint32_t)kMaxSegs) { set_error("gemv: bad segment count %u", a.nseg); return false; }
     uint32_t tiles = 0;
     for (uint32_t i = 0; i < a.nseg; i++) {
+        const GemvSeg& g = a.seg[i];
+        const bool glu = g.epi == EPI_GLU_SILU || g.epi == EPI_GLU_GELU;
+        if (reinterpret_cast<uintptr_t>(g.w) % type_align(g.type) != 0 || g.row_bytes % type_align(g.type) != 0 ||
+            (glu && (reinterpret_cast<uintptr_t>(g.w2) % type_align(g.type2) != 0 ||
+                     g.row_bytes2 % type_align(g.type2) != 0))) {
+            set_error("gemv: weights of type %u must be %u-byte aligned", g.type, type_align(g.type));
+            return false;
+        }
         a.seg[i].tile0 = tiles;
         tiles += (a.seg[i].rows + kRows - 1) / kRows;
+    }
+    static const bool cuda_cores_only = getenv("LLAMINI_GEMV_CUDA_CORES") != nullptr;
+    if (!cuda_cores_only) {
+        bool handled = false;
+        if (!launch_gemv_mma(in, st, &handled)) return false;
+        if (handled) return true;
     }
     size_t smem = gemv_smem(a.K);
     if (smem > 200 * 1024) { set_error("gemv: K=%u too large", a.K); return false; }

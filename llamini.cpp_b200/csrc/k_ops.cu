@@ -51,6 +51,10 @@ bool launch_dequant(uint32_t type, const uint8_t* raw, uint64_t n, float* out, c
     TypeInfo ti;
     if (!type_info(type, &ti) || n % ti.block_elems != 0) { set_error("dequant: bad type %u / count", type); return false; }
     if (n == 0) return true;
+    if (reinterpret_cast<uintptr_t>(raw) % type_align(type) != 0) {
+        set_error("dequant: blocks of type %u must be %u-byte aligned", type, type_align(type));
+        return false;
+    }
     if (type == T_F32 || type == T_F16) {
         dequant_f_kernel<<<grid_for(n, 256), 256, 0, st>>>(raw, n, type, out);
         return LM_CUDA(cudaGetLastError());
@@ -216,6 +220,7 @@ __global__ void rope_kernel(float* v, uint32_t pos, uint32_t dim, uint32_t hd, f
         if (neox) {
             const uint32_t h = p / half, j = p % half;
             i0 = h * hd + j; i1 = i0 + half; e = 2 * j;
+            if (i1 >= dim) continue;                 // partial last head: left as is
         } else {
             i0 = 2 * p; i1 = i0 + 1; e = i0 % hd;
         }
@@ -375,12 +380,13 @@ bool launch_mha_f32(const float* q, float* kc, float* vc, float* out, uint32_t p
 }
 
 bool gemv_init();
+bool gemv_mma_init();
 bool attn_init();
 
 // Per-kernel attributes, set once when the device is selected (never during a
 // graph capture).
 bool kernels_init() {
-    return gemv_init() && attn_init() &&
+    return gemv_init() && gemv_mma_init() && attn_init() &&
            LM_CUDA(cudaFuncSetAttribute(mha_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
 }
 

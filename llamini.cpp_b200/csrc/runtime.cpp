@@ -107,6 +107,15 @@ uint64_t type_bytes(uint32_t type, uint64_t n) {
     return n / ti.block_elems * ti.block_bytes;
 }
 
+uint32_t type_align(uint32_t type) {
+    switch (type) {
+    case GGML_TYPE_Q4_K: case GGML_TYPE_Q5_K: return 16;
+    case GGML_TYPE_F32: return 4;
+    case GGML_TYPE_F16: return 2;
+    default: return 1;
+    }
+}
+
 // ---------------------------------------------------------------- weight registry
 struct GgufUpload {
     GGUFFile* gf;

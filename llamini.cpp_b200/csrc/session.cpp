@@ -36,6 +36,7 @@ struct llamini_session {
     f32 eps = 0, rope_base = 0, emb_scale = 1;
     u32 rope_mode = 0;                    // 0 none, 1 NORM, 2 NEOX
     u32 act_gelu = 0;
+    u32 kv_f16 = 0;                       // cache element type (f32 unless asked)
 
     // weights (device)
     struct Layer {
@@ -53,7 +54,7 @@ struct llamini_session {
     float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *ffn_h = nullptr, *logits = nullptr;
     float *part = nullptr, *trace = nullptr;
     u32 *counters = nullptr, *tokens = nullptr;
-    uint16_t *kc = nullptr, *vc = nullptr;
+    void *kc = nullptr, *vc = nullptr;
     lm::StepState* st = nullptr;
     lm::StepState* st_host = nullptr;     // pinned staging for StepState writes/reads
 
@@ -131,9 +132,9 @@ bool alloc_buffers(llamini_session* s) {
     s->trace = (float*)own(s, (size_t)L * s->dim * 4);
     s->counters = (u32*)own(s, (size_t)s->n_kv * 4);
     s->tokens = (u32*)own(s, ((size_t)s->max_seq + 1) * 4);
-    const size_t kv_elems = (size_t)L * s->n_kv * s->max_seq * s->hd;
-    s->kc = (uint16_t*)own(s, kv_elems * 2);
-    s->vc = (uint16_t*)own(s, kv_elems * 2);
+    const size_t kv_bytes = (size_t)L * s->n_kv * s->max_seq * s->hd * (s->kv_f16 ? 2 : 4);
+    s->kc = own(s, kv_bytes);
+    s->vc = own(s, kv_bytes);
     s->st = (StepState*)own(s, sizeof(StepState));
     if (!s->hidden || !s->qkv || !s->attn || !s->ffn_h || !s->logits || !s->part || !s->trace ||
         !s->counters || !s->tokens || !s->kc || !s->vc || !s->st)
@@ -143,7 +144,7 @@ bool alloc_buffers(llamini_session* s) {
     return LM_CUDA(cudaMemset(s->counters, 0, (size_t)s->n_kv * 4)) &&
            LM_CUDA(cudaMemset(s->st, 0, sizeof(StepState))) &&
            LM_CUDA(cudaMemset(s->tokens, 0, ((size_t)s->max_seq + 1) * 4)) &&
-           LM_CUDA(cudaMemset(s->kc, 0, kv_elems * 2)) && LM_CUDA(cudaMemset(s->vc, 0, kv_elems * 2));
+           LM_CUDA(cudaMemset(s->kc, 0, kv_bytes)) && LM_CUDA(cudaMemset(s->vc, 0, kv_bytes));
 }
 
 u32 choose_splits(u32 n_kv, u32 max_seq) {
@@ -191,9 +192,10 @@ bool enqueue_step(llamini_session* s, cudaStream_t st, bool trace, bool nll) {
         AttnArgs at;
         at.st = s->st;
         at.qkv = s->qkv;
-        const size_t per_layer = (size_t)s->n_kv * s->max_seq * s->hd;
-        at.kc = s->kc + l * per_layer;
-        at.vc = s->vc + l * per_layer;
+        const size_t per_layer = (size_t)s->n_kv * s->max_seq * s->hd * (s->kv_f16 ? 2 : 4);
+        at.kc = (uint8_t*)s->kc + l * per_layer;
+        at.vc = (uint8_t*)s->vc + l * per_layer;
+        at.kv_f16 = s->kv_f16;
         at.out = s->attn;
         at.part = s->part;
         at.counter = s->counters;
@@ -280,7 +282,10 @@ void destroy(llamini_session* s) {
     delete s;
 }
 
+bool g_kv_f16 = false;
+
 bool finish_build(llamini_session* s) {
+    s->kv_f16 = g_kv_f16 ? 1u : 0u;
     s->n_split = choose_splits(s->n_kv, s->max_seq);
     if (!alloc_buffers(s)) return false;
     if (!capture(s, 1, false, false, &s->g_one)) return false;
@@ -639,7 +644,12 @@ int llamini_session_logits(llamini_session* s, f32* out) {
 u32 llamini_session_pos(llamini_session* s) { return s ? s->pos : 0; }
 u64 llamini_session_weight_bytes(llamini_session* s) { return s ? s->weight_bytes : 0; }
 u64 llamini_session_kv_bytes_per_pos(llamini_session* s) {
-    return s ? (u64)s->n_layers * 2 * s->n_kv * s->hd * 2 : 0;
+    return s ? (u64)s->n_layers * 2 * s->n_kv * s->hd * (s->kv_f16 ? 2 : 4) : 0;
+}
+
+int llamini_set_kv_f16(int enable) {
+    lm::g_kv_f16 = enable != 0;
+    return 0;
 }
 
 int llamini_session_trace(llamini_session* s, int enable) {

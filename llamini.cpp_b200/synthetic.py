@@ -142,9 +142,10 @@ def _tensor_payload(rng, ts: TensorSpec) -> np.ndarray:
     return random_blocks(rng, ts.type, n)
 
 
-def write_gguf(path: str, spec: GGUFSpec, seed: int, align: int = 32) -> None:
+def write_gguf(path: str, spec: GGUFSpec, seed: int, align: int = 32, payloads: dict | None = None) -> None:
     """Write ``spec`` to ``path``; tensor payloads are drawn in spec order from
-    ``default_rng(seed)`` so a (spec, seed) pair always gives the same bytes."""
+    ``default_rng(seed)`` so a (spec, seed) pair always gives the same bytes.
+    ``payloads`` may give the raw bytes of some tensors explicitly."""
     rng = np.random.default_rng(seed)
     sizes = [type_bytes(t.type, int(np.prod(t.ne))) for t in spec.tensors]
     offs, cur = [], 0
@@ -167,6 +168,8 @@ def write_gguf(path: str, spec: GGUFSpec, seed: int, align: int = 32) -> None:
             if off > pos:
                 f.write(b"\0" * (off - pos))
             data = _tensor_payload(rng, ts)
+            if payloads and ts.name in payloads:
+                data = np.asarray(payloads[ts.name], dtype=np.uint8).reshape(-1)
             assert data.size == sz, (ts.name, data.size, sz)
             f.write(data.tobytes())
             pos = off + sz
