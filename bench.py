@@ -171,7 +171,7 @@ def kernel_roofline(lm, torch, stream, hbm_peak, peak_kind):
     algo = nbytes + cols * 4 + rows * 4
     achieved = algo / per_launch_s / 1e9
     del w
-    return {"kernel": "gemv_fused_kernel (Q4_K, 11264x2048, gate+up shape)", "bound": "hbm",
+    return {"kernel": "gemv_mma_kernel (Q4_K, 11264x2048, gate+up shape)", "bound": "hbm",
             "achieved": round(achieved, 1), "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
             "frac": round(achieved / hbm_peak, 4), "algorithmic_bytes_per_launch": algo,
             "us_per_launch": round(per_launch_s * 1e6, 2), "traffic": None}
@@ -251,9 +251,10 @@ def run_ours(args, ws, rank, local):
             "step_roofline": {"bytes_per_step": int(step_bytes), "achieved_gbs": round(step_bytes / step_s / 1e9, 1),
                               "peak": hbm_peak, "frac": round(step_bytes / step_s / 1e9 / hbm_peak, 4)},
             "roofline": roof,
-            "e2e": {"value": round(ws * e2e_tok / e2e_max, 2), "unit": "tok/s",
-                    "h2d_bytes_per_step": round(4 / e2e_tok, 4), "d2h_bytes_per_step": 4,
-                    "call": "generate_autoregressive, 1-token prompt, 256 greedy tokens, wall clock"},
+            "e2e": None if args.no_e2e else {
+                "value": round(ws * e2e_tok / e2e_max, 2), "unit": "tok/s",
+                "h2d_bytes_per_step": round(4 / e2e_tok, 4), "d2h_bytes_per_step": 4,
+                "call": "generate_autoregressive, 1-token prompt, 256 greedy tokens, wall clock"},
             "gpu_launches": steps * (1 + 5 * 22 + 2),
             "clocks": clk.summary(),
         }

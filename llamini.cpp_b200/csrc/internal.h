@@ -135,7 +135,7 @@ struct AttnArgs {
     uint32_t* counter;     // [n_kv] completion counters (return to 0 after use)
     uint32_t n_heads, n_kv, hd, max_seq, n_split;
     uint32_t rope;         // 0 none, 1 NORM, 2 NEOX
-    float rope_base;
+    const float* theta;    // [hd/2] rotation frequencies base^(-2j/hd), computed on the host
 };
 bool launch_attention(const AttnArgs& a, cudaStream_t st);
 

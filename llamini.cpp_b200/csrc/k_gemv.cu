@@ -15,6 +15,7 @@
 // for the R rows. Lane partial sums are combined with warp shuffles.
 #include "internal.h"
 #include "quant.cuh"
+#include "pdl.cuh"
 
 #include <cuda_fp16.h>
 #include <cstdlib>
@@ -138,6 +139,8 @@ gemv_fused_kernel(const __grid_constant__ GemvArgs a) {
     extern __shared__ float xs[];                 // K floats, then reduction scratch
     float* red = xs + ((a.K + 3u) & ~3u);
     const uint32_t K = a.K;
+    pdl_trigger();
+    pdl_wait();                                   // x comes from the previous kernel
 
     // Prologue: stage (and normalise) the input vector.
     if (a.norm == NORM_NONE) {
@@ -281,8 +284,7 @@ bool launch_gemv(const GemvArgs& in, cudaStream_t st) {
     uint32_t cap = (uint32_t)sm_count() * 4;
     uint32_t grid = want < cap ? want : cap;
     if (grid == 0) grid = 1;
-    gemv_fused_kernel<<<grid, kThreads, smem, st>>>(a);
-    return LM_CUDA(cudaGetLastError());
+    return LM_CUDA(launch_k(gemv_fused_kernel, dim3(grid), dim3(kThreads), smem, st, a));
 }
 
 // Multi-column plain GEMV: one fused launch per column (correct, not tuned for

@@ -11,6 +11,7 @@
 //             generate.h host-pointer entry points.
 #include "internal.h"
 #include "quant.cuh"
+#include "pdl.cuh"
 
 #include <cuda_fp16.h>
 
@@ -114,6 +115,8 @@ __device__ void decode_row(const DevMat& m, uint32_t row, float* out, float scal
 }
 
 __global__ void embed_kernel(const EmbedArgs a) {
+    pdl_trigger();
+    pdl_wait();
     const uint32_t pos = a.st->pos;
     uint32_t tok = a.tokens[pos];
     if (tok >= a.tok.rows) tok = 0;            // out-of-range ids read row 0
@@ -128,13 +131,14 @@ __global__ void embed_kernel(const EmbedArgs a) {
 }
 
 bool launch_embed(const EmbedArgs& a, cudaStream_t st) {
-    embed_kernel<<<1, 256, 0, st>>>(a);
-    return LM_CUDA(cudaGetLastError());
+    return LM_CUDA(launch_k(embed_kernel, dim3(1), dim3(256), 0, st, a));
 }
 
 __global__ void finish_kernel(const FinishArgs a) {
     __shared__ float red[32];
     __shared__ float bmax;
+    pdl_trigger();
+    pdl_wait();
     StepState* s = a.st;
     const uint32_t pos = s->pos;
     if (a.nll && pos + 1 < a.max_tokens) {
@@ -176,8 +180,7 @@ __global__ void finish_kernel(const FinishArgs a) {
 }
 
 bool launch_finish(const FinishArgs& a, cudaStream_t st) {
-    finish_kernel<<<1, 1024, 0, st>>>(a);
-    return LM_CUDA(cudaGetLastError());
+    return LM_CUDA(launch_k(finish_kernel, dim3(1), dim3(1024), 0, st, a));
 }
 
 // ------------------------------------------------------------------ host-pointer ops
@@ -260,6 +263,8 @@ __global__ void scale_kernel(float* out, const float* a, float s, uint32_t n) {
 }
 
 __global__ void copy_kernel(float* dst, const float* src, uint32_t n) {
+    pdl_trigger();
+    pdl_wait();
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) dst[i] = src[i];
 }
 
@@ -362,7 +367,7 @@ bool launch_scale(float* out, const float* a, float s, uint32_t n, cudaStream_t 
     scale_kernel<<<g1(n), 256, 0, st>>>(out, a, s, n); return done();
 }
 bool launch_copy_f32(float* dst, const float* src, uint32_t n, cudaStream_t st) {
-    copy_kernel<<<g1(n), 256, 0, st>>>(dst, src, n); return done();
+    return LM_CUDA(launch_k(copy_kernel, dim3(g1(n)), dim3(256), 0, st, dst, src, n));
 }
 bool launch_argmax(const float* x, uint32_t n, uint32_t* out, cudaStream_t st) {
     argmax_kernel<<<1, 1024, 0, st>>>(x, n, out); return done();

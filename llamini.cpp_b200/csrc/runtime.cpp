@@ -71,6 +71,13 @@ bool ensure_device() {
 }
 
 cudaStream_t stream() { return g_stream; }
+
+// Programmatic dependent launch between the step's kernels; LLAMINI_PDL=0
+// turns it off (every launch then waits for its predecessor to finish).
+bool pdl_enabled() {
+    static const bool on = [] { const char* e = getenv("LLAMINI_PDL"); return !(e && e[0] == '0'); }();
+    return on;
+}
 int sm_count() { return g_sms; }
 
 void* dev_alloc(size_t bytes) {

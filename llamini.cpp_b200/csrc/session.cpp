@@ -34,6 +34,7 @@ struct llamini_session {
     u32 n_layers = 0, dim = 0, n_heads = 0, n_kv = 0, hd = 0, ffn = 0, vocab = 0, max_seq = 0;
     u32 qd = 0, kvd = 0, n_split = 1, max_pos = 0;
     f32 eps = 0, rope_base = 0, emb_scale = 1;
+    const float* theta = nullptr;        // RoPE frequencies (device, hd/2)
     u32 rope_mode = 0;                    // 0 none, 1 NORM, 2 NEOX
     u32 act_gelu = 0;
     u32 kv_f16 = 0;                       // cache element type (f32 unless asked)
@@ -205,7 +206,7 @@ bool enqueue_step(llamini_session* s, cudaStream_t st, bool trace, bool nll) {
         at.max_seq = s->max_seq;
         at.n_split = s->n_split;
         at.rope = s->rope_mode;
-        at.rope_base = s->rope_base;
+        at.theta = s->theta;
         if (!launch_attention(at, st)) return false;
         // O projection + residual
         GemvArgs o;
@@ -285,6 +286,11 @@ void destroy(llamini_session* s) {
 bool g_kv_f16 = false;
 
 bool finish_build(llamini_session* s) {
+    // theta_j = base^(-2j/hd), evaluated exactly as model.c:38 / model.c:50 do
+    std::vector<f32> th(s->hd / 2 ? s->hd / 2 : 1);
+    for (u32 j = 0; j < s->hd / 2; j++) th[j] = powf(s->rope_base, -(f32)(2 * j) / (f32)s->hd);
+    s->theta = upload_f32(s, th.data(), th.size());
+    if (!s->theta) return false;
     s->kv_f16 = g_kv_f16 ? 1u : 0u;
     s->n_split = choose_splits(s->n_kv, s->max_seq);
     if (!alloc_buffers(s)) return false;
