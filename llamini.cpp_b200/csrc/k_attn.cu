@@ -47,10 +47,39 @@ __device__ void rope_vecs(float* v, uint32_t nvec, uint32_t hd, uint32_t pos, ui
     }
 }
 
+constexpr uint32_t kChunk = 64;           // positions staged in shared memory at a time
+constexpr uint32_t kMaxHeadsPerWarp = 4;  // G <= 16 query heads per kv head
+constexpr uint32_t kMaxDimPerLane = 8;    // head_dim <= 256
+
+// Stage rows [t0, t0+n) of one kv head's cache (row length hd) as f32.
+__device__ __forceinline__ void stage_rows(float* dst, const float* src, uint32_t n, uint32_t hd) {
+    if ((hd & 3u) == 0) {
+        const float4* s4 = reinterpret_cast<const float4*>(src);
+        float4* d4 = reinterpret_cast<float4*>(dst);
+        for (uint32_t i = threadIdx.x; i < n * hd / 4; i += blockDim.x) d4[i] = s4[i];
+    } else {
+        for (uint32_t i = threadIdx.x; i < n * hd; i += blockDim.x) dst[i] = src[i];
+    }
+}
+__device__ __forceinline__ void stage_rows(float* dst, const __half* src, uint32_t n, uint32_t hd) {
+    if ((hd & 3u) == 0) {
+        const uint2* s2 = reinterpret_cast<const uint2*>(src);
+        float4* d4 = reinterpret_cast<float4*>(dst);
+        for (uint32_t i = threadIdx.x; i < n * hd / 4; i += blockDim.x) {
+            const uint2 v = s2[i];
+            const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+            const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+            d4[i] = make_float4(lo.x, lo.y, hi.x, hi.y);
+        }
+    } else {
+        for (uint32_t i = threadIdx.x; i < n * hd; i += blockDim.x) dst[i] = __half2float(src[i]);
+    }
+}
+
 template <typename KV>
 __global__ void __launch_bounds__(kAttnThreads)
 attn_decode_kernel(const AttnArgs a) {
-    extern __shared__ float sm[];
+    extern __shared__ __align__(16) float sm[];
     __shared__ int is_last;
     pdl_trigger();
     pdl_wait();                                   // q/k/v come from the QKV projection
@@ -66,81 +95,113 @@ attn_decode_kernel(const AttnArgs a) {
     const uint32_t chunk = (L + ns - 1) / ns;
     const uint32_t t0 = min(split * chunk, L);
     const uint32_t t1 = min(t0 + chunk, L);
-    const uint32_t maxc = (a.max_seq + a.n_split - 1) / a.n_split;
-    const uint32_t cap = maxc > kMinSplitLen ? maxc : kMinSplitLen;   // score slots per head
 
-    float* qs = sm;                 // [G][hd]
-    float* kv = qs + G * hd;        // [hd] new key, [hd] new value
-    float* sc = kv + 2 * hd;        // [G][cap] scores, then probabilities
+    const uint32_t hd4 = (hd + 3u) & ~3u;
+    float* qs = sm;                      // [G][hd]
+    float* kvn = qs + G * hd4;           // [2][hd] new key, new value
+    float* ks = kvn + 2 * hd4;           // [kChunk][hd]
+    float* vs = ks + kChunk * hd;        // [kChunk][hd]
+    float* sc = vs + kChunk * hd;        // [G][kChunk] scores / probabilities (and merge scratch)
 
     const float* q = a.qkv + (uint64_t)g * G * hd;
-    for (uint32_t i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i] = q[i];
+    for (uint32_t i = threadIdx.x; i < G * hd; i += blockDim.x) qs[(i / hd) * hd4 + i % hd] = q[i];
     const bool has_new = t0 <= pos && pos < t1;
     if (has_new) {
         const float* kn = a.qkv + (uint64_t)a.n_heads * hd + (uint64_t)g * hd;
         const float* vn = kn + (uint64_t)a.n_kv * hd;
-        for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) { kv[i] = kn[i]; kv[hd + i] = vn[i]; }
+        for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) { kvn[i] = kn[i]; kvn[hd4 + i] = vn[i]; }
     }
     __syncthreads();
-    rope_vecs(qs, G, hd, pos, a.rope, a.theta);
-    if (has_new) rope_vecs(kv, 1, hd, pos, a.rope, a.theta);
+    for (uint32_t i = 0; i < G; i++) rope_vecs(qs + i * hd4, 1, hd, pos, a.rope, a.theta);
+    if (has_new) rope_vecs(kvn, 1, hd, pos, a.rope, a.theta);
     __syncthreads();
     KV* kc = reinterpret_cast<KV*>(a.kc) + (uint64_t)g * a.max_seq * hd;
     KV* vc = reinterpret_cast<KV*>(a.vc) + (uint64_t)g * a.max_seq * hd;
     if (has_new) {
         for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) {
-            kv_store(kc + (uint64_t)pos * hd + i, kv[i]);
-            kv_store(vc + (uint64_t)pos * hd + i, kv[hd + i]);
+            kv_store(kc + (uint64_t)pos * hd + i, kvn[i]);
+            kv_store(vc + (uint64_t)pos * hd + i, kvn[hd4 + i]);
         }
     }
-    __syncthreads();
+    __syncthreads();                               // the new row is visible to the staging loads
 
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const float rscale = sqrtf((float)hd);        // model.c:243
+    // online softmax state of the heads this warp owns (i = warp + nw * j)
+    float mrun[kMaxHeadsPerWarp], lrun[kMaxHeadsPerWarp], o[kMaxHeadsPerWarp][kMaxDimPerLane];
+#pragma unroll
+    for (uint32_t j = 0; j < kMaxHeadsPerWarp; j++) {
+        mrun[j] = -INFINITY;
+        lrun[j] = 0.f;
+#pragma unroll
+        for (uint32_t d = 0; d < kMaxDimPerLane; d++) o[j][d] = 0.f;
+    }
 
-    // scores: warp per position, lanes over head_dim, all G heads
-    for (uint32_t t = t0 + warp; t < t1; t += nw) {
-        const KV* kt = kc + (uint64_t)t * hd;
-        float kr[4];
+    for (uint32_t c0 = t0; c0 < t1; c0 += kChunk) {
+        const uint32_t n = min(kChunk, t1 - c0);
+        __syncthreads();                           // previous chunk fully consumed
+        stage_rows(ks, kc + (uint64_t)c0 * hd, n, hd);
+        stage_rows(vs, vc + (uint64_t)c0 * hd, n, hd);
+        __syncthreads();
+        // scores: warp per position, lanes over head_dim, all G heads
+        for (uint32_t t = warp; t < n; t += nw) {
+            for (uint32_t i = 0; i < G; i++) {
+                float s = 0.f;
+                for (uint32_t d = lane; d < hd; d += 32) s = fmaf(qs[i * hd4 + d], ks[t * hd + d], s);
 #pragma unroll
-        for (int j = 0; j < 4; j++) kr[j] = (lane + 32 * j < hd) ? kv_load(kt + lane + 32 * j) : 0.f;
-        for (uint32_t i = 0; i < G; i++) {
-            float s = 0.f;
+                for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+                if (lane == 0) sc[i * kChunk + t] = s / rscale;
+            }
+        }
+        __syncthreads();
 #pragma unroll
-            for (int j = 0; j < 4; j++) if (lane + 32 * j < hd) s = fmaf(qs[i * hd + lane + 32 * j], kr[j], s);
-            for (uint32_t d = lane + 128; d < hd; d += 32) s = fmaf(qs[i * hd + d], kv_load(kt + d), s);
+        for (uint32_t j = 0; j < kMaxHeadsPerWarp; j++) {
+            const uint32_t i = warp + nw * j;
+            if (i >= G) break;
+            float* si = sc + i * kChunk;
+            float cm = -INFINITY;
+            for (uint32_t t = lane; t < n; t += 32) cm = fmaxf(cm, si[t]);
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-            if (lane == 0) sc[i * cap + (t - t0)] = s / rscale;
+            for (int off = 16; off > 0; off >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, off));
+            const float mnew = fmaxf(mrun[j], cm);
+            const float corr = expf(mrun[j] - mnew);      // 0 on the first chunk
+            float cl = 0.f;
+            for (uint32_t t = lane; t < n; t += 32) {
+                const float p = expf(si[t] - mnew);
+                si[t] = p;
+                cl += p;
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) cl += __shfl_xor_sync(0xffffffffu, cl, off);
+            __syncwarp();
+            lrun[j] = lrun[j] * corr + cl;
+            mrun[j] = mnew;
+#pragma unroll
+            for (uint32_t dd = 0; dd < kMaxDimPerLane; dd++) {
+                const uint32_t d = lane + 32 * dd;
+                if (d >= hd) break;
+                float acc = o[j][dd] * corr;
+                for (uint32_t t = 0; t < n; t++) acc = fmaf(si[t], vs[t * hd + d], acc);
+                o[j][dd] = acc;
+            }
         }
     }
-    __syncthreads();
 
     const uint32_t stride = hd + 2;
-    const uint32_t n = t1 - t0;
-    for (uint32_t i = warp; i < G; i += nw) {
+#pragma unroll
+    for (uint32_t j = 0; j < kMaxHeadsPerWarp; j++) {
+        const uint32_t i = warp + nw * j;
+        if (i >= G) break;
         const uint32_t h = g * G + i;
-        float m = -INFINITY;
-        for (uint32_t t = lane; t < n; t += 32) m = fmaxf(m, sc[i * cap + t]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float l = 0.f;
-        for (uint32_t t = lane; t < n; t += 32) {
-            const float p = expf(sc[i * cap + t] - m);
-            sc[i * cap + t] = p;
-            l += p;
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-        __syncwarp();
         float* dst = a.part + ((uint64_t)h * a.n_split + split) * stride;
-        for (uint32_t d = lane; d < hd; d += 32) {
-            float o = 0.f;
-            for (uint32_t t = 0; t < n; t++) o = fmaf(sc[i * cap + t], kv_load(vc + (uint64_t)(t0 + t) * hd + d), o);
-            if (ns == 1) a.out[(uint64_t)h * hd + d] = o / l;
-            else dst[2 + d] = o;
+#pragma unroll
+        for (uint32_t dd = 0; dd < kMaxDimPerLane; dd++) {
+            const uint32_t d = lane + 32 * dd;
+            if (d >= hd) break;
+            if (ns == 1) a.out[(uint64_t)h * hd + d] = o[j][dd] / lrun[j];
+            else dst[2 + d] = o[j][dd];
         }
-        if (ns > 1 && lane == 0) { dst[0] = m; dst[1] = l; }
+        if (ns > 1 && lane == 0) { dst[0] = mrun[j]; dst[1] = lrun[j]; }
     }
     if (ns == 1) return;
 
@@ -169,16 +230,18 @@ attn_decode_kernel(const AttnArgs a) {
     for (uint32_t idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
         const uint32_t t = idx / hd, d = idx % hd;
         const float* src = a.part + (uint64_t)(g * G + t) * a.n_split * stride + 2 + d;
-        float o = 0.f;
-        for (uint32_t s = 0; s < ns; s++) o = fmaf(__ldcg(src + s * stride), wts[t * ns + s], o);
-        a.out[(uint64_t)(g * G + t) * hd + d] = o / tot[t];
+        float acc = 0.f;
+        for (uint32_t s = 0; s < ns; s++) acc = fmaf(__ldcg(src + s * stride), wts[t * ns + s], acc);
+        a.out[(uint64_t)(g * G + t) * hd + d] = acc / tot[t];
     }
     if (threadIdx.x == 0) a.counter[g] = 0u;
 }
 
 bool attn_init() {
     return LM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)) &&
-           LM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+           LM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)) &&
+           LM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<float>, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) &&
+           LM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<__half>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
 }
 
 bool launch_attention(const AttnArgs& a, cudaStream_t st) {
@@ -187,11 +250,14 @@ bool launch_attention(const AttnArgs& a, cudaStream_t st) {
         return false;
     }
     const uint32_t G = a.n_heads / a.n_kv;
-    const uint32_t maxc = (a.max_seq + a.n_split - 1) / a.n_split;
-    const uint32_t cap = maxc > kMinSplitLen ? maxc : kMinSplitLen;
-    // scores need G*cap floats; the merge reuses them for G*n_split + G floats
-    const size_t tail = (size_t)G * cap > (size_t)G * a.n_split + G ? (size_t)G * cap : (size_t)G * a.n_split + G;
-    const size_t smem = ((size_t)G * a.hd + 2 * a.hd + tail) * sizeof(float);
+    if (G > kMaxHeadsPerWarp * (kAttnThreads / 32) || a.hd > 32 * kMaxDimPerLane) {
+        set_error("attention: %u query heads per kv head / head_dim %u not supported", G, a.hd);
+        return false;
+    }
+    const size_t hd4 = (a.hd + 3u) & ~3u;
+    // scores need G*kChunk floats; the merge reuses them for G*n_split + G floats
+    const size_t tail = (size_t)G * kChunk > (size_t)G * a.n_split + G ? (size_t)G * kChunk : (size_t)G * a.n_split + G;
+    const size_t smem = ((size_t)G * hd4 + 2 * hd4 + 2 * (size_t)kChunk * a.hd + tail) * sizeof(float);
     if (smem > 200 * 1024) { set_error("attention: shared memory %zu too large", smem); return false; }
     const dim3 grid(a.n_kv, a.n_split);
     if (a.kv_f16) return LM_CUDA(launch_k(attn_decode_kernel<__half>, grid, dim3(kAttnThreads), smem, st, a));

@@ -253,7 +253,8 @@ gemv_fused_kernel(const __grid_constant__ GemvArgs a) {
 static size_t gemv_smem(uint32_t K) { return (((size_t)K + 3) & ~size_t(3)) * sizeof(float) + 64 * sizeof(float); }
 
 bool gemv_init() {
-    return LM_CUDA(cudaFuncSetAttribute(gemv_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    return LM_CUDA(cudaFuncSetAttribute(gemv_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)) &&
+           LM_CUDA(cudaFuncSetAttribute(gemv_fused_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
 }
 
 bool launch_gemv(const GemvArgs& in, cudaStream_t st) {

@@ -34,7 +34,7 @@ constexpr int kMThreads = kMWarps * 32;
 bool mma_type(uint32_t t) { return t == T_Q4_K || t == T_Q6_K || t == T_Q8_0 || t == T_Q4_0; }
 
 struct MmaSmem {
-    float* xf;          // staged x (f32, before the final scale for RMSNorm)
+    float* xf;          // staged x before the final scale (K floats)
     uint32_t* xh;       // x * 2^E as fp16 pairs, high part   (K/2 words)
     uint32_t* xl;       // low part
     float* sx;          // per 16-element run: sum(x) * 2^(E-24)
@@ -50,29 +50,37 @@ __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uin
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// B fragment for the 4 consecutive elements e0..e0+3 (e0 % 4 == 0): k slots
-// (2t, 2t+1) take elements (e0, e0+2), slots (2t+8, 2t+9) take (e0+1, e0+3),
-// matching how the A pairs are cut from packed bytes. Column 0 = x_hi,
-// column 1 = x_lo, other columns zero.
-struct BFrag { uint32_t b0, b1; };
-
+// Lane roles. For the A operand lane (g, tig) supplies rows g and g+8 at the k
+// slots of its tig. For B, lane (g, tig) supplies column g; the column pair
+// (2s, 2s+1) of an MMA carries (x_hi, x_lo) of "slot" s (a group, scale group
+// or block, depending on the format) and is zero in every other slot's MMA.
+// Chaining the MMAs of 4 slots into one accumulator therefore leaves slot s's
+// sums in the lanes with tig == s (accumulator columns 2tig, 2tig+1), so the
+// four lanes of a quad apply the scales of four different slots in parallel.
 struct Lane {
     uint32_t g, tig;
-    bool bact;                 // provides a B column (g < 2)
-    const uint32_t* xpart;     // xh for g == 0, xl for g == 1
+    uint32_t slot;             // g >> 1: the slot whose x this lane supplies
+    const uint32_t* xpart;     // xh for even g (x_hi column), xl for odd g
 };
 
+struct BFrag { uint32_t b0, b1; };
+
+// B values of this lane for elements e0..e0+3 (e0 % 4 == 0): k slots (2t, 2t+1)
+// take elements (e0, e0+2), slots (2t+8, 2t+9) take (e0+1, e0+3), matching how
+// the A pairs are cut from packed bytes.
 __device__ __forceinline__ BFrag bfrag(const Lane& L, uint32_t e0) {
-    BFrag f{0u, 0u};
-    if (L.bact) {
-        const uint2 v = *reinterpret_cast<const uint2*>(L.xpart + (e0 >> 1));
-        f.b0 = __byte_perm(v.x, v.y, 0x5410);
-        f.b1 = __byte_perm(v.x, v.y, 0x7632);
-    }
-    return f;
+    const uint2 v = *reinterpret_cast<const uint2*>(L.xpart + (e0 >> 1));
+    return BFrag{__byte_perm(v.x, v.y, 0x5410), __byte_perm(v.x, v.y, 0x7632)};
+}
+__device__ __forceinline__ BFrag bmask(const BFrag& f, uint32_t slot, uint32_t s) {
+    const uint32_t m = slot == s ? 0xFFFFFFFFu : 0u;
+    return BFrag{f.b0 & m, f.b1 & m};
 }
 
-// acc[0] (row g) and acc[1] (row g+8) += alpha * P - beta * S, lanes tig == 0.
+// Exact small-integer to float (v < 2^23) without the conversion unit.
+__device__ __forceinline__ float u2f(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.0f; }
+
+// acc[0] (row g) and acc[1] (row g+8) += alpha * P - beta * S.
 __device__ __forceinline__ void scale_add(float* acc, const float* c, float a_g, float b_g, float a_g8, float b_g8,
                                           float sx) {
     acc[0] = fmaf(a_g, c[0] + c[1], fmaf(-b_g, sx, acc[0]));
@@ -81,11 +89,13 @@ __device__ __forceinline__ void scale_add(float* acc, const float* c, float a_g,
 
 // ------------------------------------------------------------------ formats
 // Each format: Raw (the words one lane needs for one iteration of rows g and
-// g+8), SB (elements per iteration), load(), compute().
+// g+8), SB (elements per iteration), SBB (bytes per iteration), load(),
+// compute().
 
 // Q4_K (gguf.c:504-529): 256-element super-block, 4 groups of 64; in group j
 // the low nibbles of qs[32j..32j+32) are sub-block 2j, the high nibbles 2j+1.
-// Lane tig takes bytes 8*tig..8*tig+8 of each group: two MMAs per sub-block.
+// Lane tig takes bytes 8tig..8tig+8 of each group (two MMAs per sub-block);
+// slot = group.
 struct FQ4K {
     static constexpr uint32_t SB = 256, SBB = 144;
     struct Raw { uint32_t h[4], h8[4]; uint2 q[4], q8[4]; };
@@ -98,41 +108,54 @@ struct FQ4K {
             r.q8[j] = __ldg(reinterpret_cast<const uint2*>(bg8 + 16 + 32 * j + 8 * L.tig));
         }
     }
+    // scale and min of sub-blocks 2t and 2t+1 (gguf.c:391-399), all 16 six-bit
+    // fields unpacked with word-wide masks
+    static __device__ __forceinline__ void scales(const uint32_t* h, uint32_t t, float* sl, float* ml, float* sh,
+                                                  float* mh) {
+        const uint32_t lo = t < 2;
+        const uint32_t wsc = lo ? (h[1] & 0x3F3F3F3Fu) : ((h[3] & 0x0F0F0F0Fu) | ((h[1] >> 2) & 0x30303030u));
+        const uint32_t wm = lo ? (h[2] & 0x3F3F3F3Fu) : (((h[3] >> 4) & 0x0F0F0F0Fu) | ((h[2] >> 2) & 0x30303030u));
+        const uint32_t sh16 = 16 * (t & 1);
+        *sl = u2f((wsc >> sh16) & 0xFFu);
+        *sh = u2f((wsc >> (sh16 + 8)) & 0xFFu);
+        *ml = u2f((wm >> sh16) & 0xFFu);
+        *mh = u2f((wm >> (sh16 + 8)) & 0xFFu);
+    }
     static __device__ __forceinline__ void compute(const Raw& r, uint32_t e_blk, uint32_t, const Lane& L,
                                                    const MmaSmem& sm, float* acc) {
-        const float dg = f16_bits(r.h[0] & 0xFFFFu), mg = f16_bits(r.h[0] >> 16);
-        const float dg8 = f16_bits(r.h8[0] & 0xFFFFu), mg8 = f16_bits(r.h8[0] >> 16);
+        const uint32_t eb = e_blk + 64 * L.slot + 8 * L.tig;
+        const BFrag f00 = bfrag(L, eb), f01 = bfrag(L, eb + 4), f10 = bfrag(L, eb + 32), f11 = bfrag(L, eb + 36);
+        float cl[4] = {0.f, 0.f, 0.f, 0.f}, ch[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-            const uint32_t e = e_blk + 64 * j + 8 * L.tig;
-            const BFrag lo0 = bfrag(L, e), lo1 = bfrag(L, e + 4), hi0 = bfrag(L, e + 32), hi1 = bfrag(L, e + 36);
             const uint32_t w0 = r.q[j].x, w1 = r.q[j].y, v0 = r.q8[j].x, v1 = r.q8[j].y;
             const uint32_t w0s = w0 >> 8, w1s = w1 >> 8, v0s = v0 >> 8, v1s = v1 >> 8;
-            float cl[4] = {0.f, 0.f, 0.f, 0.f}, ch[4] = {0.f, 0.f, 0.f, 0.f};
-            mma16816(cl, w0 & 0x000F000Fu, v0 & 0x000F000Fu, w0s & 0x000F000Fu, v0s & 0x000F000Fu, lo0.b0, lo0.b1);
-            mma16816(cl, w1 & 0x000F000Fu, v1 & 0x000F000Fu, w1s & 0x000F000Fu, v1s & 0x000F000Fu, lo1.b0, lo1.b1);
-            // high nibbles in place (16 q): alpha of sub-block 2j+1 scaled by 1/16
-            mma16816(ch, w0 & 0x00F000F0u, v0 & 0x00F000F0u, w0s & 0x00F000F0u, v0s & 0x00F000F0u, hi0.b0, hi0.b1);
-            mma16816(ch, w1 & 0x00F000F0u, v1 & 0x00F000F0u, w1s & 0x00F000F0u, v1s & 0x00F000F0u, hi1.b0, hi1.b1);
-            if (L.tig == 0) {
-                uint32_t s0, m0, s1, m1, t0, n0, t1, n1;
-                k4_scale_min(r.h + 1, 2 * j, &s0, &m0);
-                k4_scale_min(r.h + 1, 2 * j + 1, &s1, &m1);
-                k4_scale_min(r.h8 + 1, 2 * j, &t0, &n0);
-                k4_scale_min(r.h8 + 1, 2 * j + 1, &t1, &n1);
-                const uint32_t q = (e_blk + 64 * j) >> 4;
-                const float sxl = sm.sx[q] + sm.sx[q + 1], sxh = sm.sx[q + 2] + sm.sx[q + 3];
-                scale_add(acc, cl, dg * (float)s0, mg * (float)m0, dg8 * (float)t0, mg8 * (float)n0, sxl);
-                scale_add(acc, ch, dg * (float)s1 * 0.0625f, mg * (float)m1, dg8 * (float)t1 * 0.0625f,
-                          mg8 * (float)n1, sxh);
-            }
+            const BFrag b00 = bmask(f00, L.slot, j), b01 = bmask(f01, L.slot, j);
+            const BFrag b10 = bmask(f10, L.slot, j), b11 = bmask(f11, L.slot, j);
+            mma16816(cl, w0 & 0x000F000Fu, v0 & 0x000F000Fu, w0s & 0x000F000Fu, v0s & 0x000F000Fu, b00.b0, b00.b1);
+            mma16816(cl, w1 & 0x000F000Fu, v1 & 0x000F000Fu, w1s & 0x000F000Fu, v1s & 0x000F000Fu, b01.b0, b01.b1);
+            // high nibbles in place (16 q): alpha scaled by 1/16 below
+            mma16816(ch, w0 & 0x00F000F0u, v0 & 0x00F000F0u, w0s & 0x00F000F0u, v0s & 0x00F000F0u, b10.b0, b10.b1);
+            mma16816(ch, w1 & 0x00F000F0u, v1 & 0x00F000F0u, w1s & 0x00F000F0u, v1s & 0x00F000F0u, b11.b0, b11.b1);
         }
+        // this lane: group tig of rows g and g+8
+        float sl, ml, sh, mh, tl, nl, th, nh;
+        scales(r.h, L.tig, &sl, &ml, &sh, &mh);
+        scales(r.h8, L.tig, &tl, &nl, &th, &nh);
+        const float dg = __half2float(__ushort_as_half((unsigned short)(r.h[0] & 0xFFFFu)));
+        const float mg = __half2float(__ushort_as_half((unsigned short)(r.h[0] >> 16)));
+        const float dg8 = __half2float(__ushort_as_half((unsigned short)(r.h8[0] & 0xFFFFu)));
+        const float mg8 = __half2float(__ushort_as_half((unsigned short)(r.h8[0] >> 16)));
+        const uint32_t q = (e_blk + 64 * L.tig) >> 4;
+        const float sxl = sm.sx[q] + sm.sx[q + 1], sxh = sm.sx[q + 2] + sm.sx[q + 3];
+        scale_add(acc, cl, dg * sl, mg * ml, dg8 * tl, mg8 * nl, sxl);
+        scale_add(acc, ch, dg * sh * 0.0625f, mg * mh, dg8 * th * 0.0625f, mg8 * nh, sxh);
     }
 };
 
 // Q6_K (gguf.c:561-590): per 128-half H, byte l of ql[64H..], ql[64H+32..] and
 // qh[32H..] give elements 128H + 32c + l (c = 0..3), scale sc[8H + l/16 + 2c].
-// One MMA per 16-element scale group; lane tig takes l = 16u + 4tig .. +4.
+// For each (H, u = l/16) the four scale groups c are one MMA each, slot = c.
 // Blocks are 210 bytes, so words are read with funnel shifts (ld_u32).
 struct FQ6K {
     static constexpr uint32_t SB = 256, SBB = 210;
@@ -151,16 +174,22 @@ struct FQ6K {
                 r.h8[i] = ld_u32(bg8 + 128 + 32 * H + off);
             }
         }
-        if (L.tig == 0) {
-            ld_words<4>(bg + 192, r.sc);
-            ld_words<4>(bg8 + 192, r.sc8);
-        }
+        ld_words<4>(bg + 192, r.sc);
+        ld_words<4>(bg8 + 192, r.sc8);
         r.d = ld_u16(bg + 208) | (ld_u16(bg8 + 208) << 16);
     }
     static __device__ __forceinline__ uint32_t word(uint32_t n, uint32_t hbits) { return (n & 0x0F0F0F0Fu) | hbits; }
+    // signed scale byte i of the 16-byte field (i is lane dependent: words are
+    // picked with selects, not a dynamically indexed array)
+    static __device__ __forceinline__ float sbyte(const uint32_t* w, uint32_t i) {
+        const uint32_t q = i >> 2;
+        const uint32_t x = q == 0 ? w[0] : (q == 1 ? w[1] : (q == 2 ? w[2] : w[3]));
+        return (float)(int)(int8_t)(uint8_t)((x >> (8 * (i & 3))) & 0xFFu);
+    }
     static __device__ __forceinline__ void compute(const Raw& r, uint32_t e_blk, uint32_t, const Lane& L,
                                                    const MmaSmem& sm, float* acc) {
-        const float dg = f16_bits(r.d & 0xFFFFu), dg8 = f16_bits(r.d >> 16);
+        const float dg = __half2float(__ushort_as_half((unsigned short)(r.d & 0xFFFFu)));
+        const float dg8 = __half2float(__ushort_as_half((unsigned short)(r.d >> 16)));
 #pragma unroll
         for (int H = 0; H < 2; H++) {
 #pragma unroll
@@ -175,29 +204,26 @@ struct FQ6K {
                 wm[1] = word(r.b8[i], (r.h8[i] << 2) & 0x30303030u);
                 wm[2] = word(r.a8[i] >> 4, r.h8[i] & 0x30303030u);
                 wm[3] = word(r.b8[i] >> 4, (r.h8[i] >> 2) & 0x30303030u);
+                const BFrag f = bfrag(L, e_blk + 128 * H + 32 * L.slot + 16 * u + 4 * L.tig);
+                float cc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int c = 0; c < 4; c++) {
-                    const uint32_t e = e_blk + 128 * H + 32 * c + 16 * u + 4 * L.tig;
-                    const BFrag b = bfrag(L, e);
-                    float cc[4] = {0.f, 0.f, 0.f, 0.f};
+                    const BFrag b = bmask(f, L.slot, c);
                     mma16816(cc, __byte_perm(wq[c], 0, 0x4240), __byte_perm(wm[c], 0, 0x4240),
                              __byte_perm(wq[c], 0, 0x4341), __byte_perm(wm[c], 0, 0x4341), b.b0, b.b1);
-                    if (L.tig == 0) {
-                        const uint32_t si = 8 * H + u + 2 * c;           // scale byte index
-                        const float sg = (float)(int8_t)(uint8_t)((r.sc[si >> 2] >> (8 * (si & 3))) & 0xFFu);
-                        const float sg8 = (float)(int8_t)(uint8_t)((r.sc8[si >> 2] >> (8 * (si & 3))) & 0xFFu);
-                        const float ag = dg * sg, ag8 = dg8 * sg8;
-                        scale_add(acc, cc, ag, 32.0f * ag, ag8, 32.0f * ag8,
-                                  sm.sx[(e_blk + 128 * H + 32 * c + 16 * u) >> 4]);
-                    }
                 }
+                // this lane: scale group c = tig of rows g, g+8
+                const uint32_t si = 8 * H + u + 2 * L.tig;
+                const float ag = dg * sbyte(r.sc, si), ag8 = dg8 * sbyte(r.sc8, si);
+                scale_add(acc, cc, ag, 32.0f * ag, ag8, 32.0f * ag8,
+                          sm.sx[(e_blk + 128 * H + 32 * L.tig + 16 * u) >> 4]);
             }
         }
     }
 };
 
-// 32-element formats, 4 blocks per iteration (the last one may be partial;
-// nb32 = number of blocks in the row).
+// 32-element formats, 4 blocks per iteration (slot = block; the last iteration
+// of a row may hold fewer blocks).
 // Q8_0 (gguf.c:489-503): w = d q, q int8; with u = q ^ 0x80, w = d u - 128 d.
 struct FQ80 {
     static constexpr uint32_t SB = 128, SBB = 136, BB = 34;
@@ -219,21 +245,29 @@ struct FQ80 {
     }
     static __device__ __forceinline__ void compute(const Raw& r, uint32_t e_blk, uint32_t nvalid, const Lane& L,
                                                    const MmaSmem& sm, float* acc) {
+        const uint32_t es = e_blk + 32 * L.slot + 4 * L.tig;
+        const BFrag f0 = L.slot < nvalid ? bfrag(L, es) : BFrag{0u, 0u};
+        const BFrag f1 = L.slot < nvalid ? bfrag(L, es + 16) : BFrag{0u, 0u};
+        float cc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int k = 0; k < 4; k++) {
             if ((uint32_t)k >= nvalid) break;
-            const float dg = f16_bits(r.d[k] & 0xFFFFu), dg8 = f16_bits(r.d[k] >> 16);
+            const BFrag b0 = bmask(f0, L.slot, k), b1 = bmask(f1, L.slot, k);
+            const uint32_t w = r.w[k][0] ^ 0x80808080u, v = r.v[k][0] ^ 0x80808080u;
+            const uint32_t w2 = r.w[k][1] ^ 0x80808080u, v2 = r.v[k][1] ^ 0x80808080u;
+            mma16816(cc, __byte_perm(w, 0, 0x4240), __byte_perm(v, 0, 0x4240),
+                     __byte_perm(w, 0, 0x4341), __byte_perm(v, 0, 0x4341), b0.b0, b0.b1);
+            mma16816(cc, __byte_perm(w2, 0, 0x4240), __byte_perm(v2, 0, 0x4240),
+                     __byte_perm(w2, 0, 0x4341), __byte_perm(v2, 0, 0x4341), b1.b0, b1.b1);
+        }
+        if (L.tig < nvalid) {
+            uint32_t dd = 0;
 #pragma unroll
-            for (int u = 0; u < 2; u++) {
-                const uint32_t w = r.w[k][u] ^ 0x80808080u, v = r.v[k][u] ^ 0x80808080u;
-                const uint32_t e = e_blk + 32 * k + 16 * u + 4 * L.tig;
-                const BFrag b = bfrag(L, e);
-                float cc[4] = {0.f, 0.f, 0.f, 0.f};
-                mma16816(cc, __byte_perm(w, 0, 0x4240), __byte_perm(v, 0, 0x4240),
-                         __byte_perm(w, 0, 0x4341), __byte_perm(v, 0, 0x4341), b.b0, b.b1);
-                if (L.tig == 0)
-                    scale_add(acc, cc, dg, 128.0f * dg, dg8, 128.0f * dg8, sm.sx[(e_blk + 32 * k + 16 * u) >> 4]);
-            }
+            for (int k = 0; k < 4; k++) if ((uint32_t)k == L.tig) dd = r.d[k];
+            const float dg = __half2float(__ushort_as_half((unsigned short)(dd & 0xFFFFu)));
+            const float dg8 = __half2float(__ushort_as_half((unsigned short)(dd >> 16)));
+            const uint32_t q = (e_blk + 32 * L.tig) >> 4;
+            scale_add(acc, cc, dg, 128.0f * dg, dg8, 128.0f * dg8, sm.sx[q] + sm.sx[q + 1]);
         }
     }
 };
@@ -256,21 +290,27 @@ struct FQ40 {
     }
     static __device__ __forceinline__ void compute(const Raw& r, uint32_t e_blk, uint32_t nvalid, const Lane& L,
                                                    const MmaSmem& sm, float* acc) {
+        const uint32_t es = e_blk + 32 * L.slot + 4 * L.tig;
+        const BFrag fl = L.slot < nvalid ? bfrag(L, es) : BFrag{0u, 0u};
+        const BFrag fh = L.slot < nvalid ? bfrag(L, es + 16) : BFrag{0u, 0u};
+        float cl[4] = {0.f, 0.f, 0.f, 0.f}, ch[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int k = 0; k < 4; k++) {
             if ((uint32_t)k >= nvalid) break;
-            const float dg = f16_bits(r.d[k] & 0xFFFFu), dg8 = f16_bits(r.d[k] >> 16);
             const uint32_t w = r.w[k], v = r.v[k], ws = w >> 8, vs = v >> 8;
-            const uint32_t e = e_blk + 32 * k;
-            const BFrag lo = bfrag(L, e + 4 * L.tig), hi = bfrag(L, e + 16 + 4 * L.tig);
-            float cl[4] = {0.f, 0.f, 0.f, 0.f}, ch[4] = {0.f, 0.f, 0.f, 0.f};
-            mma16816(cl, w & 0x000F000Fu, v & 0x000F000Fu, ws & 0x000F000Fu, vs & 0x000F000Fu, lo.b0, lo.b1);
-            mma16816(ch, w & 0x00F000F0u, v & 0x00F000F0u, ws & 0x00F000F0u, vs & 0x00F000F0u, hi.b0, hi.b1);
-            if (L.tig == 0) {
-                const uint32_t q = e >> 4;
-                scale_add(acc, cl, dg, 8.0f * dg, dg8, 8.0f * dg8, sm.sx[q]);
-                scale_add(acc, ch, dg * 0.0625f, 8.0f * dg, dg8 * 0.0625f, 8.0f * dg8, sm.sx[q + 1]);
-            }
+            const BFrag bl = bmask(fl, L.slot, k), bh = bmask(fh, L.slot, k);
+            mma16816(cl, w & 0x000F000Fu, v & 0x000F000Fu, ws & 0x000F000Fu, vs & 0x000F000Fu, bl.b0, bl.b1);
+            mma16816(ch, w & 0x00F000F0u, v & 0x00F000F0u, ws & 0x00F000F0u, vs & 0x00F000F0u, bh.b0, bh.b1);
+        }
+        if (L.tig < nvalid) {
+            uint32_t dd = 0;
+#pragma unroll
+            for (int k = 0; k < 4; k++) if ((uint32_t)k == L.tig) dd = r.d[k];
+            const float dg = __half2float(__ushort_as_half((unsigned short)(dd & 0xFFFFu)));
+            const float dg8 = __half2float(__ushort_as_half((unsigned short)(dd >> 16)));
+            const uint32_t q = (e_blk + 32 * L.tig) >> 4;
+            scale_add(acc, cl, dg, 8.0f * dg, dg8, 8.0f * dg8, sm.sx[q]);
+            scale_add(acc, ch, dg * 0.0625f, 8.0f * dg, dg8 * 0.0625f, 8.0f * dg8, sm.sx[q + 1]);
         }
     }
 };
@@ -315,105 +355,98 @@ __device__ __forceinline__ unsigned long long m_key(float v, uint32_t idx) {
 
 // ------------------------------------------------------------------ prologue
 // Stage the input vector: normalise (RMSNorm model.c:4-10 / LayerNorm
-// gpt2.c:130-139), choose E with max|x| * 2^E < 2^14, write the fp16 hi/lo
-// split and the scaled 16-element sums. Threads own runs of 16 elements; the
-// loads of a run are issued together, so x costs one round trip.
+// gpt2.c:130-139), choose E with max|x| 2^E < 2^14, write the fp16 hi/lo split
+// and the scaled 16-element sums. Thread t owns float4s t, t+256, ...; all its
+// loads are issued before any is used, so x costs one round trip.
 __device__ void stage_x(const GemvArgs& a, const MmaSmem& sm, float* s_scale) {
-    const uint32_t K = a.K, nrun = K / 16;
-    float s = 0.f, m = 0.f;
-    if (a.norm == NORM_LAYER) {
-        // two-pass mean / variance like the reference
-        for (uint32_t r = threadIdx.x; r < nrun; r += blockDim.x) {
-            const float4* xp = reinterpret_cast<const float4*>(a.x + 16 * r);
-            float4 v[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) v[i] = xp[i];
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                reinterpret_cast<float4*>(sm.xf + 16 * r)[i] = v[i];
-                s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-            }
+    const uint32_t K = a.K, n4 = K / 4, tid = threadIdx.x;
+    const float4* x4 = reinterpret_cast<const float4*>(a.x);
+    float4* xf4 = reinterpret_cast<float4*>(sm.xf);
+    float s = 0.f, m = 0.f, f = 1.0f;
+    // pass 1: x (times the RMSNorm weight) into shared memory, sum of squares, max
+    if (a.norm == NORM_RMS) {
+        const float4* w4 = reinterpret_cast<const float4*>(a.norm_w);
+#pragma unroll 4
+        for (uint32_t i = tid; i < n4; i += kMThreads) {
+            const float4 v = x4[i], w = w4[i];
+            s = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, s))));
+            const float4 o = make_float4(v.x * w.x, v.y * w.y, v.z * w.z, v.w * w.w);
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w))));
+            xf4[i] = o;
         }
         block_sum_max(s, m, sm.red);
-        const float mean = s / (float)K;
+        f = 1.0f / sqrtf(s / (float)K + a.eps);    // model.c:7-8; applied to x*w below
+    } else if (a.norm == NORM_LAYER) {
+#pragma unroll 4
+        for (uint32_t i = tid; i < n4; i += kMThreads) {
+            const float4 v = x4[i];
+            s += (v.x + v.y) + (v.z + v.w);
+            xf4[i] = v;
+        }
+        block_sum_max(s, m, sm.red);
+        const float mean = s / (float)K;          // two passes like gpt2.c:131-136
         float vs = 0.f;
-        for (uint32_t r = threadIdx.x; r < nrun; r += blockDim.x)
-            for (int i = 0; i < 16; i++) { const float c = sm.xf[16 * r + i] - mean; vs = fmaf(c, c, vs); }
+        for (uint32_t i = tid; i < n4; i += kMThreads) {
+            const float4 v = xf4[i];
+            const float c0 = v.x - mean, c1 = v.y - mean, c2 = v.z - mean, c3 = v.w - mean;
+            vs = fmaf(c0, c0, fmaf(c1, c1, fmaf(c2, c2, fmaf(c3, c3, vs))));
+        }
         float dummy = 0.f;
         block_sum_max(vs, dummy, sm.red);
         const float inv = 1.0f / sqrtf(vs / (float)K + a.eps);
+        const float4* w4 = reinterpret_cast<const float4*>(a.norm_w);
+        const float4* b4 = reinterpret_cast<const float4*>(a.norm_b);
         m = 0.f;
-        for (uint32_t r = threadIdx.x; r < nrun; r += blockDim.x) {
-            for (int i = 0; i < 16; i++) {
-                const uint32_t k = 16 * r + i;
-                const float v = (sm.xf[k] - mean) * inv * a.norm_w[k] + a.norm_b[k];
-                sm.xf[k] = v;
-                m = fmaxf(m, fabsf(v));
-            }
+#pragma unroll 4
+        for (uint32_t i = tid; i < n4; i += kMThreads) {
+            const float4 v = xf4[i], w = w4[i], b = b4[i];
+            const float4 o = make_float4((v.x - mean) * inv * w.x + b.x, (v.y - mean) * inv * w.y + b.y,
+                                         (v.z - mean) * inv * w.z + b.z, (v.w - mean) * inv * w.w + b.w);
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w))));
+            xf4[i] = o;
         }
-        s = 0.f;
-        block_sum_max(s, m, sm.red);
-        s = 1.0f;                                  // xf already final
+        float ds = 0.f;
+        block_sum_max(ds, m, sm.red);
     } else {
-        const bool rms = a.norm == NORM_RMS;
-        for (uint32_t r = threadIdx.x; r < nrun; r += blockDim.x) {
-            const float4* xp = reinterpret_cast<const float4*>(a.x + 16 * r);
-            float4 v[4], w[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) v[i] = xp[i];
-            if (rms) {
-                const float4* wp = reinterpret_cast<const float4*>(a.norm_w + 16 * r);
-#pragma unroll
-                for (int i = 0; i < 4; i++) w[i] = wp[i];
-            }
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                float4 o = v[i];
-                if (rms) {
-                    s = fmaf(v[i].x, v[i].x, fmaf(v[i].y, v[i].y, fmaf(v[i].z, v[i].z, fmaf(v[i].w, v[i].w, s))));
-                    o.x *= w[i].x; o.y *= w[i].y; o.z *= w[i].z; o.w *= w[i].w;
-                }
-                m = fmaxf(m, fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w))));
-                reinterpret_cast<float4*>(sm.xf + 16 * r)[i] = o;
-            }
+#pragma unroll 4
+        for (uint32_t i = tid; i < n4; i += kMThreads) {
+            const float4 v = x4[i];
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+            xf4[i] = v;
         }
-        block_sum_max(s, m, sm.red);
-        // RMSNorm: xf holds x*w; the common factor 1/rms is applied below
-        s = rms ? 1.0f / sqrtf(s / (float)K + a.eps) : 1.0f;
+        float ds = 0.f;
+        block_sum_max(ds, m, sm.red);
     }
-    const float f = s;                             // factor still to apply to xf
+    // pass 2: x_final = xf * f, scaled by 2^E so that max|x| 2^E < 2^14
     const float mx = m * f;
     int e = 0;
     if (mx > 0.f && mx < INFINITY) frexpf(mx, &e);
-    const int E = 14 - e;
-    for (uint32_t r = threadIdx.x; r < nrun; r += blockDim.x) {
-        float v[16];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float4 t = reinterpret_cast<const float4*>(sm.xf + 16 * r)[i];
-            v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+    int E = 14 - e;
+    E = E > 100 ? 100 : (E < -100 ? -100 : E);
+    const float F = f * __int_as_float((E + 127) << 23);
+    // each lane takes whole float4s; the runs of 16 are 4 consecutive lanes
+    const uint32_t n4r = (n4 + 31u) & ~31u;            // whole warps in the loop
+    for (uint32_t i = tid; i < n4r; i += kMThreads) {
+        const float4 v = i < n4 ? xf4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float x0 = v.x * F, x1 = v.y * F, x2 = v.z * F, x3 = v.w * F;
+        const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+        const __half h2 = __float2half_rn(x2), h3 = __float2half_rn(x3);
+        const __half l0 = __float2half_rn(x0 - __half2float(h0)), l1 = __float2half_rn(x1 - __half2float(h1));
+        const __half l2 = __float2half_rn(x2 - __half2float(h2)), l3 = __float2half_rn(x3 - __half2float(h3));
+        float rs = ((x0 + x1) + (x2 + x3)) * 5.9604644775390625e-08f;     // units of 2^(E-24)
+        rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+        rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+        if (i < n4) {
+            *reinterpret_cast<uint2*>(sm.xh + 2 * i) =
+                make_uint2((uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16),
+                           (uint32_t)__half_as_ushort(h2) | ((uint32_t)__half_as_ushort(h3) << 16));
+            *reinterpret_cast<uint2*>(sm.xl + 2 * i) =
+                make_uint2((uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16),
+                           (uint32_t)__half_as_ushort(l2) | ((uint32_t)__half_as_ushort(l3) << 16));
+            if ((i & 3u) == 0) sm.sx[i >> 2] = rs;
         }
-        float sum = 0.f;
-        uint32_t hw[8], lw[8];
-#pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-            const float x0 = v[i] * f, x1 = v[i + 1] * f;
-            sum += x0 + x1;
-            const float s0 = ldexpf(x0, E), s1 = ldexpf(x1, E);
-            const __half h0 = __float2half_rn(s0), h1 = __float2half_rn(s1);
-            const __half l0 = __float2half_rn(s0 - __half2float(h0)), l1 = __float2half_rn(s1 - __half2float(h1));
-            hw[i / 2] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-            lw[i / 2] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
-        }
-        uint4* hp = reinterpret_cast<uint4*>(sm.xh + 8 * r);
-        uint4* lp = reinterpret_cast<uint4*>(sm.xl + 8 * r);
-        hp[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        hp[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
-        lp[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-        lp[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
-        sm.sx[r] = ldexpf(sum, E - 24);
     }
-    if (threadIdx.x == 0) *s_scale = ldexpf(1.0f, 24 - E);
+    if (tid == 0) *s_scale = __int_as_float((127 + 24 - E) << 23);   // 2^(24-E)
     __syncthreads();
 }
 
@@ -473,8 +506,8 @@ gemv_mma_kernel(const __grid_constant__ GemvArgs a) {
     Lane L;
     L.g = lane >> 2;
     L.tig = lane & 3u;
-    L.bact = L.g < 2;
-    L.xpart = L.g == 0 ? sm.xh : sm.xl;
+    L.slot = L.g >> 1;
+    L.xpart = (L.g & 1u) ? sm.xl : sm.xh;
     // rows past the end of the matrix read its last row; their results are dropped
     const uint32_t ra = min(row0 + L.g, G.rows - 1), rb = min(row0 + L.g + 8, G.rows - 1);
 
@@ -533,12 +566,13 @@ gemv_mma_kernel(const __grid_constant__ GemvArgs a) {
 }
 
 size_t gemv_mma_smem(uint32_t K) {
-    // xf (4K) + xh, xl (2K each) + sx (K/4) bytes, then red and part
-    return (size_t)K * 8 + (size_t)K / 16 * 4 + 2 * kMWarps * 4 + kMWarps * 2 * 16 * 4;
+    // xf (4K bytes), xh, xl (2K bytes each), sx (K/4 bytes), then red and part
+    return (size_t)K * 8 + (size_t)K / 16 * 4 + 2 * kMWarps * 4 + kMWarps * 16 * 4;
 }
 
 bool gemv_mma_init() {
-    return LM_CUDA(cudaFuncSetAttribute(gemv_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    return LM_CUDA(cudaFuncSetAttribute(gemv_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)) &&
+           LM_CUDA(cudaFuncSetAttribute(gemv_mma_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
 }
 
 // Launch when every segment is a tensor-core format (and a gated pair shares

@@ -391,7 +391,13 @@ bool attn_init();
 // Per-kernel attributes, set once when the device is selected (never during a
 // graph capture).
 bool kernels_init() {
+    // one shared-memory carveout for every kernel of the step, so consecutive
+    // kernels never wait for an SM to reconfigure its L1 / shared split
+    const int carve = cudaFuncAttributePreferredSharedMemoryCarveout;
     return gemv_init() && gemv_mma_init() && attn_init() &&
+           LM_CUDA(cudaFuncSetAttribute(embed_kernel, (cudaFuncAttribute)carve, 100)) &&
+           LM_CUDA(cudaFuncSetAttribute(finish_kernel, (cudaFuncAttribute)carve, 100)) &&
+           LM_CUDA(cudaFuncSetAttribute(copy_kernel, (cudaFuncAttribute)carve, 100)) &&
            LM_CUDA(cudaFuncSetAttribute(mha_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
 }
 
