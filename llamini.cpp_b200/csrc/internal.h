@@ -91,6 +91,7 @@ struct GemvArgs {
     GemvSeg seg[kMaxSegs];
     unsigned long long* argmax_key = nullptr;
     float* x_out = nullptr;        // optional: store the normalised x (block 0 writes it)
+    uint32_t* err = nullptr;       // error bits (a bounded wait that ran out sets kErrWaitTimeout)
 };
 
 bool launch_gemv(const GemvArgs& a, cudaStream_t st);
@@ -102,12 +103,16 @@ bool launch_gemv_mma(const GemvArgs& a, cudaStream_t st, bool* handled);
 bool launch_gemv_plain(uint32_t type, const uint8_t* w, uint32_t rows, uint32_t cols,
                        const float* x, uint32_t batch, float* y, cudaStream_t st);
 
+// Error bits written by kernels into a device word the host checks.
+constexpr uint32_t kErrWaitTimeout = 1u;   // a bounded wait on a copy gave up
+uint32_t* dev_err_word();                  // library-wide word for launches outside a session
+
 // Per-step device state shared by the kernels of one session.
 struct StepState {
     uint32_t pos;          // position of the current step
     uint32_t n_prompt;     // tokens [0, n_prompt) are given; later ones are generated
     uint32_t trace;        // 1: copy the residual stream after each layer
-    uint32_t pad;
+    uint32_t err;          // error bits set by kernels (kErrWaitTimeout, ...)
     unsigned long long argmax_key;
     double nll;            // perplexity accumulator
     uint32_t nll_count;

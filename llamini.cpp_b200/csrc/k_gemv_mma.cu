@@ -1,25 +1,26 @@
-// k_gemv_mma.cu -- dequant-GEMV on the tensor cores (Q4_K / Q6_K / Q8_0 / Q4_0).
+// k_gemv_mma.cu -- dequant-GEMV on the tensor cores, weights streamed by TMA.
 //
 // Same contract as the CUDA-core kernel in k_gemv.cu (llamini.cpp linear(),
-// model.c:66-176, with the fused prologues/epilogues), computed differently:
+// model.c:66-176, with the fused prologues/epilogues), organised for B200:
 //
+//  * Weight tiles move HBM -> shared memory with one cp.async.bulk per tile (a
+//    tile is 16 consecutive rows, contiguous in GGUF layout; a gated tile adds
+//    the 16 matching rows of the up matrix), completion tracked by an mbarrier.
+//    CTAs are persistent and keep a ring of kStages tiles in flight, so HBM
+//    sees ~100 KB of outstanding reads per SM without spending registers. The
+//    first copies are issued before the kernel waits for its predecessor (the
+//    weights do not depend on it), overlapping the previous kernel's tail.
 //  * Every block format is affine per group of 16 or 32 weights:
 //      w = alpha * q - beta     (q a small unsigned integer, gguf.c:427-590)
 //    so  sum_i w_i x_i = alpha * sum_i q_i x_i - beta * sum_i x_i.
-//  * sum_i q_i x_i for 16 rows at a time is one mma.sync.m16n8k16: the integers
-//    q (< 1024) enter the A operand as exact fp16 subnormals q * 2^-24, made
-//    with one AND (or byte permute) on the packed bytes; x enters the B operand
-//    as two fp16 columns x_hi + x_lo (22 significant bits) after the whole
-//    vector is scaled by a power of two into fp16's range. Accumulation is f32.
-//  * alpha, beta and the per-16 sums of x are applied in f32 by the lanes that
-//    hold columns 0/1 of the accumulator; the result is scaled back at the end.
-//
-// CTA = one tile of 16 output rows (16 gate + 16 up rows for the gated FFN);
-// its 8 warps split the row's blocks between them and combine partial sums in
-// shared memory. Latency is what limits a batch-1 GEMV, so each warp loads its
-// first blocks of weights into registers before anything else (before waiting
-// for the previous kernel, which produces x), and keeps one iteration of loads
-// in flight while it computes the previous one.
+//    sum_i q_i x_i for 16 rows is an mma.sync.m16n8k16: the integers enter the
+//    A operand as exact fp16 subnormals q * 2^-24 (one AND / byte permute on
+//    the packed bytes), x enters B as an fp16 hi/lo pair (22 significant bits)
+//    after scaling the vector by a power of two into fp16's range; f32
+//    accumulation. alpha, beta and the 16-element sums of x are applied in f32.
+//  * B columns 2s, 2s+1 carry x for "slot" s (a group, scale group or block);
+//    chaining four slots' MMAs into one accumulator leaves slot s's sums in the
+//    lanes with tig == s, so all 32 lanes apply scales in parallel.
 #include "internal.h"
 #include "quant.cuh"
 #include "pdl.cuh"
@@ -30,8 +31,42 @@ namespace lm {
 
 constexpr int kMWarps = 8;
 constexpr int kMThreads = kMWarps * 32;
+constexpr uint32_t kStages = 2;              // weight tiles in flight per CTA
+constexpr uint32_t kMaxWait = 1u << 26;      // polls of an mbarrier before giving up
 
 bool mma_type(uint32_t t) { return t == T_Q4_K || t == T_Q6_K || t == T_Q8_0 || t == T_Q4_0; }
+
+// ------------------------------------------------------------------ TMA / mbarrier
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" :: "r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n"
+                 :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
+// this GPU's global memory into this CTA's shared memory. No multicast.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+                 :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+// Bounded wait for the phase with the given parity; false if it never came.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    for (uint32_t i = 0; i < kMaxWait; i++) {
+        uint32_t done;
+        asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+                     " selp.u32 %0, 1, 0, p;\n}\n" : "=r"(done) : "r"(a), "r"(parity) : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+// ------------------------------------------------------------------ MMA helpers
 
 struct MmaSmem {
     float* xf;          // staged x before the final scale (K floats)
@@ -50,13 +85,9 @@ __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uin
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Lane roles. For the A operand lane (g, tig) supplies rows g and g+8 at the k
-// slots of its tig. For B, lane (g, tig) supplies column g; the column pair
-// (2s, 2s+1) of an MMA carries (x_hi, x_lo) of "slot" s (a group, scale group
-// or block, depending on the format) and is zero in every other slot's MMA.
-// Chaining the MMAs of 4 slots into one accumulator therefore leaves slot s's
-// sums in the lanes with tig == s (accumulator columns 2tig, 2tig+1), so the
-// four lanes of a quad apply the scales of four different slots in parallel.
+// Lane roles. For A, lane (g, tig) supplies rows g and g+8 at the k slots of
+// its tig. For B, lane (g, tig) supplies column g: column pair (2s, 2s+1) of
+// an MMA carries (x_hi, x_lo) of slot s and is zero in other slots' MMAs.
 struct Lane {
     uint32_t g, tig;
     uint32_t slot;             // g >> 1: the slot whose x this lane supplies
@@ -65,9 +96,9 @@ struct Lane {
 
 struct BFrag { uint32_t b0, b1; };
 
-// B values of this lane for elements e0..e0+3 (e0 % 4 == 0): k slots (2t, 2t+1)
-// take elements (e0, e0+2), slots (2t+8, 2t+9) take (e0+1, e0+3), matching how
-// the A pairs are cut from packed bytes.
+// B values for elements e0..e0+3 (e0 % 4 == 0): k slots (2t, 2t+1) take
+// elements (e0, e0+2), slots (2t+8, 2t+9) take (e0+1, e0+3), matching how the
+// A pairs are cut from packed bytes.
 __device__ __forceinline__ BFrag bfrag(const Lane& L, uint32_t e0) {
     const uint2 v = *reinterpret_cast<const uint2*>(L.xpart + (e0 >> 1));
     return BFrag{__byte_perm(v.x, v.y, 0x5410), __byte_perm(v.x, v.y, 0x7632)};
@@ -79,6 +110,7 @@ __device__ __forceinline__ BFrag bmask(const BFrag& f, uint32_t slot, uint32_t s
 
 // Exact small-integer to float (v < 2^23) without the conversion unit.
 __device__ __forceinline__ float u2f(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.0f; }
+__device__ __forceinline__ float h2f(uint32_t bits) { return __half2float(__ushort_as_half((unsigned short)bits)); }
 
 // acc[0] (row g) and acc[1] (row g+8) += alpha * P - beta * S.
 __device__ __forceinline__ void scale_add(float* acc, const float* c, float a_g, float b_g, float a_g8, float b_g8,
@@ -87,48 +119,50 @@ __device__ __forceinline__ void scale_add(float* acc, const float* c, float a_g,
     acc[1] = fmaf(a_g8, c[2] + c[3], fmaf(-b_g8, sx, acc[1]));
 }
 
+// Shared-memory word loads at any 2-byte alignment (funnel shift of the two
+// aligned words around the address; the stage buffer has slack at its end).
+__device__ __forceinline__ uint32_t lds_u32(const uint8_t* p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+    const uint32_t s = (uint32_t)(a & 3u) * 8u;
+    const uint32_t lo = w[0];
+    return s ? __funnelshift_r(lo, w[1], s) : lo;
+}
+__device__ __forceinline__ uint32_t lds_u16(const uint8_t* p) { return lds_u32(p) & 0xFFFFu; }
+
 // ------------------------------------------------------------------ formats
-// Each format: Raw (the words one lane needs for one iteration of rows g and
-// g+8), SB (elements per iteration), SBB (bytes per iteration), load(),
-// compute().
+// compute(bg, bg8, e_blk, nvalid, L, sm, acc): one iteration (SB elements) of
+// rows g (bytes at bg) and g+8 (bg8), both in shared memory.
 
 // Q4_K (gguf.c:504-529): 256-element super-block, 4 groups of 64; in group j
 // the low nibbles of qs[32j..32j+32) are sub-block 2j, the high nibbles 2j+1.
-// Lane tig takes bytes 8tig..8tig+8 of each group (two MMAs per sub-block);
-// slot = group.
+// Lane tig takes bytes 8tig..8tig+8 of each group; slot = group.
 struct FQ4K {
     static constexpr uint32_t SB = 256, SBB = 144;
-    struct Raw { uint32_t h[4], h8[4]; uint2 q[4], q8[4]; };
-    static __device__ __forceinline__ void load(Raw& r, const uint8_t* bg, const uint8_t* bg8, uint32_t, const Lane& L) {
-        ld_v4(bg, r.h);
-        ld_v4(bg8, r.h8);
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            r.q[j] = __ldg(reinterpret_cast<const uint2*>(bg + 16 + 32 * j + 8 * L.tig));
-            r.q8[j] = __ldg(reinterpret_cast<const uint2*>(bg8 + 16 + 32 * j + 8 * L.tig));
-        }
-    }
-    // scale and min of sub-blocks 2t and 2t+1 (gguf.c:391-399), all 16 six-bit
-    // fields unpacked with word-wide masks
-    static __device__ __forceinline__ void scales(const uint32_t* h, uint32_t t, float* sl, float* ml, float* sh,
-                                                  float* mh) {
-        const uint32_t lo = t < 2;
-        const uint32_t wsc = lo ? (h[1] & 0x3F3F3F3Fu) : ((h[3] & 0x0F0F0F0Fu) | ((h[1] >> 2) & 0x30303030u));
-        const uint32_t wm = lo ? (h[2] & 0x3F3F3F3Fu) : (((h[3] >> 4) & 0x0F0F0F0Fu) | ((h[2] >> 2) & 0x30303030u));
+    // scale and min of sub-blocks 2t and 2t+1 (gguf.c:391-399): all 16 six-bit
+    // fields unpacked with word-wide masks, then the pair for group t picked
+    static __device__ __forceinline__ void scales(uint32_t s0, uint32_t s1, uint32_t s2, uint32_t t, float* sl,
+                                                  float* ml, float* sh, float* mh) {
+        const bool lo = t < 2;
+        const uint32_t wsc = lo ? (s0 & 0x3F3F3F3Fu) : ((s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u));
+        const uint32_t wm = lo ? (s1 & 0x3F3F3F3Fu) : (((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u));
         const uint32_t sh16 = 16 * (t & 1);
         *sl = u2f((wsc >> sh16) & 0xFFu);
         *sh = u2f((wsc >> (sh16 + 8)) & 0xFFu);
         *ml = u2f((wm >> sh16) & 0xFFu);
         *mh = u2f((wm >> (sh16 + 8)) & 0xFFu);
     }
-    static __device__ __forceinline__ void compute(const Raw& r, uint32_t e_blk, uint32_t, const Lane& L,
-                                                   const MmaSmem& sm, float* acc) {
+    static __device__ __forceinline__ void compute(const uint8_t* bg, const uint8_t* bg8, uint32_t e_blk, uint32_t,
+                                                   const Lane& L, const MmaSmem& sm, float* acc) {
+        const uint4 h = *reinterpret_cast<const uint4*>(bg), h8 = *reinterpret_cast<const uint4*>(bg8);
         const uint32_t eb = e_blk + 64 * L.slot + 8 * L.tig;
         const BFrag f00 = bfrag(L, eb), f01 = bfrag(L, eb + 4), f10 = bfrag(L, eb + 32), f11 = bfrag(L, eb + 36);
         float cl[4] = {0.f, 0.f, 0.f, 0.f}, ch[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-            const uint32_t w0 = r.q[j].x, w1 = r.q[j].y, v0 = r.q8[j].x, v1 = r.q8[j].y;
+            const uint2 q = *reinterpret_cast<const uint2*>(bg + 16 + 32 * j + 8 * L.tig);
+            const uint2 q8 = *reinterpret_cast<const uint2*>(bg8 + 16 + 32 * j + 8 * L.tig);
+            const uint32_t w0 = q.x, w1 = q.y, v0 = q8.x, v1 = q8.y;
             const uint32_t w0s = w0 >> 8, w1s = w1 >> 8, v0s = v0 >> 8, v1s = v1 >> 8;
             const BFrag b00 = bmask(f00, L.slot, j), b01 = bmask(f01, L.slot, j);
             const BFrag b10 = bmask(f10, L.slot, j), b11 = bmask(f11, L.slot, j);
@@ -138,14 +172,11 @@ struct FQ4K {
             mma16816(ch, w0 & 0x00F000F0u, v0 & 0x00F000F0u, w0s & 0x00F000F0u, v0s & 0x00F000F0u, b10.b0, b10.b1);
             mma16816(ch, w1 & 0x00F000F0u, v1 & 0x00F000F0u, w1s & 0x00F000F0u, v1s & 0x00F000F0u, b11.b0, b11.b1);
         }
-        // this lane: group tig of rows g and g+8
         float sl, ml, sh, mh, tl, nl, th, nh;
-        scales(r.h, L.tig, &sl, &ml, &sh, &mh);
-        scales(r.h8, L.tig, &tl, &nl, &th, &nh);
-        const float dg = __half2float(__ushort_as_half((unsigned short)(r.h[0] & 0xFFFFu)));
-        const float mg = __half2float(__ushort_as_half((unsigned short)(r.h[0] >> 16)));
-        const float dg8 = __half2float(__ushort_as_half((unsigned short)(r.h8[0] & 0xFFFFu)));
-        const float mg8 = __half2float(__ushort_as_half((unsigned short)(r.h8[0] >> 16)));
+        scales(h.y, h.z, h.w, L.tig, &sl, &ml, &sh, &mh);
+        scales(h8.y, h8.z, h8.w, L.tig, &tl, &nl, &th, &nh);
+        const float dg = h2f(h.x & 0xFFFFu), mg = h2f(h.x >> 16);
+        const float dg8 = h2f(h8.x & 0xFFFFu), mg8 = h2f(h8.x >> 16);
         const uint32_t q = (e_blk + 64 * L.tig) >> 4;
         const float sxl = sm.sx[q] + sm.sx[q + 1], sxh = sm.sx[q + 2] + sm.sx[q + 3];
         scale_add(acc, cl, dg * sl, mg * ml, dg8 * tl, mg8 * nl, sxl);
@@ -156,65 +187,41 @@ struct FQ4K {
 // Q6_K (gguf.c:561-590): per 128-half H, byte l of ql[64H..], ql[64H+32..] and
 // qh[32H..] give elements 128H + 32c + l (c = 0..3), scale sc[8H + l/16 + 2c].
 // For each (H, u = l/16) the four scale groups c are one MMA each, slot = c.
-// Blocks are 210 bytes, so words are read with funnel shifts (ld_u32).
 struct FQ6K {
     static constexpr uint32_t SB = 256, SBB = 210;
-    struct Raw { uint32_t a[4], b[4], h[4], a8[4], b8[4], h8[4], sc[4], sc8[4]; uint32_t d; };
-    static __device__ __forceinline__ void load(Raw& r, const uint8_t* bg, const uint8_t* bg8, uint32_t, const Lane& L) {
-#pragma unroll
-        for (int H = 0; H < 2; H++) {
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-                const uint32_t off = 16 * u + 4 * L.tig, i = 2 * H + u;
-                r.a[i] = ld_u32(bg + 64 * H + off);
-                r.b[i] = ld_u32(bg + 64 * H + 32 + off);
-                r.h[i] = ld_u32(bg + 128 + 32 * H + off);
-                r.a8[i] = ld_u32(bg8 + 64 * H + off);
-                r.b8[i] = ld_u32(bg8 + 64 * H + 32 + off);
-                r.h8[i] = ld_u32(bg8 + 128 + 32 * H + off);
-            }
-        }
-        ld_words<4>(bg + 192, r.sc);
-        ld_words<4>(bg8 + 192, r.sc8);
-        r.d = ld_u16(bg + 208) | (ld_u16(bg8 + 208) << 16);
-    }
     static __device__ __forceinline__ uint32_t word(uint32_t n, uint32_t hbits) { return (n & 0x0F0F0F0Fu) | hbits; }
-    // signed scale byte i of the 16-byte field (i is lane dependent: words are
-    // picked with selects, not a dynamically indexed array)
-    static __device__ __forceinline__ float sbyte(const uint32_t* w, uint32_t i) {
-        const uint32_t q = i >> 2;
-        const uint32_t x = q == 0 ? w[0] : (q == 1 ? w[1] : (q == 2 ? w[2] : w[3]));
-        return (float)(int)(int8_t)(uint8_t)((x >> (8 * (i & 3))) & 0xFFu);
-    }
-    static __device__ __forceinline__ void compute(const Raw& r, uint32_t e_blk, uint32_t, const Lane& L,
-                                                   const MmaSmem& sm, float* acc) {
-        const float dg = __half2float(__ushort_as_half((unsigned short)(r.d & 0xFFFFu)));
-        const float dg8 = __half2float(__ushort_as_half((unsigned short)(r.d >> 16)));
+    static __device__ __forceinline__ void compute(const uint8_t* bg, const uint8_t* bg8, uint32_t e_blk, uint32_t,
+                                                   const Lane& L, const MmaSmem& sm, float* acc) {
+        const float dg = h2f(lds_u16(bg + 208)), dg8 = h2f(lds_u16(bg8 + 208));
 #pragma unroll
         for (int H = 0; H < 2; H++) {
 #pragma unroll
             for (int u = 0; u < 2; u++) {
-                const int i = 2 * H + u;
+                const uint32_t off = 16 * u + 4 * L.tig;
+                const uint32_t a = lds_u32(bg + 64 * H + off), b = lds_u32(bg + 64 * H + 32 + off);
+                const uint32_t hq = lds_u32(bg + 128 + 32 * H + off);
+                const uint32_t a8 = lds_u32(bg8 + 64 * H + off), b8 = lds_u32(bg8 + 64 * H + 32 + off);
+                const uint32_t h8 = lds_u32(bg8 + 128 + 32 * H + off);
                 uint32_t wq[4], wm[4];
-                wq[0] = word(r.a[i], (r.h[i] << 4) & 0x30303030u);
-                wq[1] = word(r.b[i], (r.h[i] << 2) & 0x30303030u);
-                wq[2] = word(r.a[i] >> 4, r.h[i] & 0x30303030u);
-                wq[3] = word(r.b[i] >> 4, (r.h[i] >> 2) & 0x30303030u);
-                wm[0] = word(r.a8[i], (r.h8[i] << 4) & 0x30303030u);
-                wm[1] = word(r.b8[i], (r.h8[i] << 2) & 0x30303030u);
-                wm[2] = word(r.a8[i] >> 4, r.h8[i] & 0x30303030u);
-                wm[3] = word(r.b8[i] >> 4, (r.h8[i] >> 2) & 0x30303030u);
+                wq[0] = word(a, (hq << 4) & 0x30303030u);
+                wq[1] = word(b, (hq << 2) & 0x30303030u);
+                wq[2] = word(a >> 4, hq & 0x30303030u);
+                wq[3] = word(b >> 4, (hq >> 2) & 0x30303030u);
+                wm[0] = word(a8, (h8 << 4) & 0x30303030u);
+                wm[1] = word(b8, (h8 << 2) & 0x30303030u);
+                wm[2] = word(a8 >> 4, h8 & 0x30303030u);
+                wm[3] = word(b8 >> 4, (h8 >> 2) & 0x30303030u);
                 const BFrag f = bfrag(L, e_blk + 128 * H + 32 * L.slot + 16 * u + 4 * L.tig);
                 float cc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int c = 0; c < 4; c++) {
-                    const BFrag b = bmask(f, L.slot, c);
+                    const BFrag bb = bmask(f, L.slot, c);
                     mma16816(cc, __byte_perm(wq[c], 0, 0x4240), __byte_perm(wm[c], 0, 0x4240),
-                             __byte_perm(wq[c], 0, 0x4341), __byte_perm(wm[c], 0, 0x4341), b.b0, b.b1);
+                             __byte_perm(wq[c], 0, 0x4341), __byte_perm(wm[c], 0, 0x4341), bb.b0, bb.b1);
                 }
                 // this lane: scale group c = tig of rows g, g+8
-                const uint32_t si = 8 * H + u + 2 * L.tig;
-                const float ag = dg * sbyte(r.sc, si), ag8 = dg8 * sbyte(r.sc8, si);
+                const uint32_t si = 192 + 8 * H + u + 2 * L.tig;
+                const float ag = dg * (float)(int8_t)bg[si], ag8 = dg8 * (float)(int8_t)bg8[si];
                 scale_add(acc, cc, ag, 32.0f * ag, ag8, 32.0f * ag8,
                           sm.sx[(e_blk + 128 * H + 32 * L.tig + 16 * u) >> 4]);
             }
@@ -222,29 +229,13 @@ struct FQ6K {
     }
 };
 
-// 32-element formats, 4 blocks per iteration (slot = block; the last iteration
-// of a row may hold fewer blocks).
+// 32-element formats, 4 blocks per iteration (slot = block; the last
+// iteration of a row may hold fewer blocks).
 // Q8_0 (gguf.c:489-503): w = d q, q int8; with u = q ^ 0x80, w = d u - 128 d.
 struct FQ80 {
     static constexpr uint32_t SB = 128, SBB = 136, BB = 34;
-    struct Raw { uint32_t w[4][2], v[4][2], d[4]; };
-    static __device__ __forceinline__ void load(Raw& r, const uint8_t* bg, const uint8_t* bg8, uint32_t nvalid,
-                                                const Lane& L) {
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            if ((uint32_t)k < nvalid) {
-                const uint8_t* p = bg + k * BB;
-                const uint8_t* q = bg8 + k * BB;
-                r.w[k][0] = ld_u32(p + 2 + 4 * L.tig);
-                r.w[k][1] = ld_u32(p + 18 + 4 * L.tig);
-                r.v[k][0] = ld_u32(q + 2 + 4 * L.tig);
-                r.v[k][1] = ld_u32(q + 18 + 4 * L.tig);
-                r.d[k] = ld_u16(p) | (ld_u16(q) << 16);
-            }
-        }
-    }
-    static __device__ __forceinline__ void compute(const Raw& r, uint32_t e_blk, uint32_t nvalid, const Lane& L,
-                                                   const MmaSmem& sm, float* acc) {
+    static __device__ __forceinline__ void compute(const uint8_t* bg, const uint8_t* bg8, uint32_t e_blk,
+                                                   uint32_t nvalid, const Lane& L, const MmaSmem& sm, float* acc) {
         const uint32_t es = e_blk + 32 * L.slot + 4 * L.tig;
         const BFrag f0 = L.slot < nvalid ? bfrag(L, es) : BFrag{0u, 0u};
         const BFrag f1 = L.slot < nvalid ? bfrag(L, es + 16) : BFrag{0u, 0u};
@@ -252,20 +243,18 @@ struct FQ80 {
 #pragma unroll
         for (int k = 0; k < 4; k++) {
             if ((uint32_t)k >= nvalid) break;
+            const uint8_t* p = bg + k * BB + 2 + 4 * L.tig;
+            const uint8_t* q = bg8 + k * BB + 2 + 4 * L.tig;
+            const uint32_t w = lds_u32(p) ^ 0x80808080u, v = lds_u32(q) ^ 0x80808080u;
+            const uint32_t w2 = lds_u32(p + 16) ^ 0x80808080u, v2 = lds_u32(q + 16) ^ 0x80808080u;
             const BFrag b0 = bmask(f0, L.slot, k), b1 = bmask(f1, L.slot, k);
-            const uint32_t w = r.w[k][0] ^ 0x80808080u, v = r.v[k][0] ^ 0x80808080u;
-            const uint32_t w2 = r.w[k][1] ^ 0x80808080u, v2 = r.v[k][1] ^ 0x80808080u;
             mma16816(cc, __byte_perm(w, 0, 0x4240), __byte_perm(v, 0, 0x4240),
                      __byte_perm(w, 0, 0x4341), __byte_perm(v, 0, 0x4341), b0.b0, b0.b1);
             mma16816(cc, __byte_perm(w2, 0, 0x4240), __byte_perm(v2, 0, 0x4240),
                      __byte_perm(w2, 0, 0x4341), __byte_perm(v2, 0, 0x4341), b1.b0, b1.b1);
         }
         if (L.tig < nvalid) {
-            uint32_t dd = 0;
-#pragma unroll
-            for (int k = 0; k < 4; k++) if ((uint32_t)k == L.tig) dd = r.d[k];
-            const float dg = __half2float(__ushort_as_half((unsigned short)(dd & 0xFFFFu)));
-            const float dg8 = __half2float(__ushort_as_half((unsigned short)(dd >> 16)));
+            const float dg = h2f(lds_u16(bg + L.tig * BB)), dg8 = h2f(lds_u16(bg8 + L.tig * BB));
             const uint32_t q = (e_blk + 32 * L.tig) >> 4;
             scale_add(acc, cc, dg, 128.0f * dg, dg8, 128.0f * dg8, sm.sx[q] + sm.sx[q + 1]);
         }
@@ -276,20 +265,8 @@ struct FQ80 {
 // nibbles 16..31.
 struct FQ40 {
     static constexpr uint32_t SB = 128, SBB = 72, BB = 18;
-    struct Raw { uint32_t w[4], v[4], d[4]; };
-    static __device__ __forceinline__ void load(Raw& r, const uint8_t* bg, const uint8_t* bg8, uint32_t nvalid,
-                                                const Lane& L) {
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            if ((uint32_t)k < nvalid) {
-                r.w[k] = ld_u32(bg + k * BB + 2 + 4 * L.tig);
-                r.v[k] = ld_u32(bg8 + k * BB + 2 + 4 * L.tig);
-                r.d[k] = ld_u16(bg + k * BB) | (ld_u16(bg8 + k * BB) << 16);
-            }
-        }
-    }
-    static __device__ __forceinline__ void compute(const Raw& r, uint32_t e_blk, uint32_t nvalid, const Lane& L,
-                                                   const MmaSmem& sm, float* acc) {
+    static __device__ __forceinline__ void compute(const uint8_t* bg, const uint8_t* bg8, uint32_t e_blk,
+                                                   uint32_t nvalid, const Lane& L, const MmaSmem& sm, float* acc) {
         const uint32_t es = e_blk + 32 * L.slot + 4 * L.tig;
         const BFrag fl = L.slot < nvalid ? bfrag(L, es) : BFrag{0u, 0u};
         const BFrag fh = L.slot < nvalid ? bfrag(L, es + 16) : BFrag{0u, 0u};
@@ -297,17 +274,14 @@ struct FQ40 {
 #pragma unroll
         for (int k = 0; k < 4; k++) {
             if ((uint32_t)k >= nvalid) break;
-            const uint32_t w = r.w[k], v = r.v[k], ws = w >> 8, vs = v >> 8;
+            const uint32_t w = lds_u32(bg + k * BB + 2 + 4 * L.tig), v = lds_u32(bg8 + k * BB + 2 + 4 * L.tig);
+            const uint32_t ws = w >> 8, vs = v >> 8;
             const BFrag bl = bmask(fl, L.slot, k), bh = bmask(fh, L.slot, k);
             mma16816(cl, w & 0x000F000Fu, v & 0x000F000Fu, ws & 0x000F000Fu, vs & 0x000F000Fu, bl.b0, bl.b1);
             mma16816(ch, w & 0x00F000F0u, v & 0x00F000F0u, ws & 0x00F000F0u, vs & 0x00F000F0u, bh.b0, bh.b1);
         }
         if (L.tig < nvalid) {
-            uint32_t dd = 0;
-#pragma unroll
-            for (int k = 0; k < 4; k++) if ((uint32_t)k == L.tig) dd = r.d[k];
-            const float dg = __half2float(__ushort_as_half((unsigned short)(dd & 0xFFFFu)));
-            const float dg8 = __half2float(__ushort_as_half((unsigned short)(dd >> 16)));
+            const float dg = h2f(lds_u16(bg + L.tig * BB)), dg8 = h2f(lds_u16(bg8 + L.tig * BB));
             const uint32_t q = (e_blk + 32 * L.tig) >> 4;
             scale_add(acc, cl, dg, 8.0f * dg, dg8, 8.0f * dg8, sm.sx[q]);
             scale_add(acc, ch, dg * 0.0625f, 8.0f * dg, dg8 * 0.0625f, 8.0f * dg8, sm.sx[q + 1]);
@@ -353,17 +327,14 @@ __device__ __forceinline__ unsigned long long m_key(float v, uint32_t idx) {
     return ((unsigned long long)o << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
 }
 
-// ------------------------------------------------------------------ prologue
-// Stage the input vector: normalise (RMSNorm model.c:4-10 / LayerNorm
-// gpt2.c:130-139), choose E with max|x| 2^E < 2^14, write the fp16 hi/lo split
-// and the scaled 16-element sums. Thread t owns float4s t, t+256, ...; all its
-// loads are issued before any is used, so x costs one round trip.
+// ------------------------------------------------------------------ x staging
+// Normalise (RMSNorm model.c:4-10 / LayerNorm gpt2.c:130-139), choose E with
+// max|x| 2^E < 2^14, write the fp16 hi/lo split and the scaled 16-element sums.
 __device__ void stage_x(const GemvArgs& a, const MmaSmem& sm, float* s_scale) {
     const uint32_t K = a.K, n4 = K / 4, tid = threadIdx.x;
     const float4* x4 = reinterpret_cast<const float4*>(a.x);
     float4* xf4 = reinterpret_cast<float4*>(sm.xf);
     float s = 0.f, m = 0.f, f = 1.0f;
-    // pass 1: x (times the RMSNorm weight) into shared memory, sum of squares, max
     if (a.norm == NORM_RMS) {
         const float4* w4 = reinterpret_cast<const float4*>(a.norm_w);
 #pragma unroll 4
@@ -417,15 +388,14 @@ __device__ void stage_x(const GemvArgs& a, const MmaSmem& sm, float* s_scale) {
         float ds = 0.f;
         block_sum_max(ds, m, sm.red);
     }
-    // pass 2: x_final = xf * f, scaled by 2^E so that max|x| 2^E < 2^14
     const float mx = m * f;
     int e = 0;
     if (mx > 0.f && mx < INFINITY) frexpf(mx, &e);
     int E = 14 - e;
     E = E > 100 ? 100 : (E < -100 ? -100 : E);
     const float F = f * __int_as_float((E + 127) << 23);
-    // each lane takes whole float4s; the runs of 16 are 4 consecutive lanes
-    const uint32_t n4r = (n4 + 31u) & ~31u;            // whole warps in the loop
+    // each lane takes whole float4s; a run of 16 is 4 consecutive lanes
+    const uint32_t n4r = (n4 + 31u) & ~31u;
     for (uint32_t i = tid; i < n4r; i += kMThreads) {
         const float4 v = i < n4 ? xf4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
         const float x0 = v.x * F, x1 = v.y * F, x2 = v.z * F, x3 = v.w * F;
@@ -450,157 +420,233 @@ __device__ void stage_x(const GemvArgs& a, const MmaSmem& sm, float* s_scale) {
     __syncthreads();
 }
 
-// ------------------------------------------------------------------ tile runner
+// ------------------------------------------------------------------ tiles
 
-// Rows g and g+8 of one matrix: this warp takes iterations first, first+step,
-// ... The first iteration's weights are loaded before waiting for the producer
-// of x; afterwards one iteration of loads stays in flight.
+struct TileRef {
+    uint32_t seg, row0, nrows;
+};
+
+__device__ __forceinline__ TileRef tile_of(const GemvArgs& a, uint32_t t) {
+    uint32_t s = 0;
+#pragma unroll
+    for (uint32_t i = 1; i < kMaxSegs; i++)
+        if (i < a.nseg && t >= a.seg[i].tile0) s = i;
+    const GemvSeg& G = a.seg[s];
+    const uint32_t row0 = (t - G.tile0) * 16;
+    return TileRef{s, row0, min(16u, G.rows - row0)};
+}
+
+// Offset of the up matrix's rows in a gated tile's stage buffer.
+__device__ __forceinline__ uint32_t up_offset(const GemvSeg& G) {
+    return (uint32_t)(((16 * G.row_bytes) + 15) & ~uint64_t(15));
+}
+
+// Thread 0: start the copies of tile t into stage buffer `buf`.
+__device__ __forceinline__ void issue_tile(const GemvArgs& a, uint32_t t, uint8_t* buf, uint64_t* bar) {
+    const TileRef tr = tile_of(a, t);
+    const GemvSeg& G = a.seg[tr.seg];
+    const bool glu = G.epi == EPI_GLU_SILU || G.epi == EPI_GLU_GELU;
+    const uint32_t n1 = (uint32_t)(((uint64_t)tr.nrows * G.row_bytes + 15) & ~uint64_t(15));
+    const uint32_t n2 = glu ? (uint32_t)(((uint64_t)tr.nrows * G.row_bytes2 + 15) & ~uint64_t(15)) : 0u;
+    mbar_expect_tx(bar, n1 + n2);
+    bulk_g2s(buf, G.w + (uint64_t)tr.row0 * G.row_bytes, n1, bar);
+    if (glu) bulk_g2s(buf + up_offset(G), G.w2 + (uint64_t)tr.row0 * G.row_bytes2, n2, bar);
+}
+
 template <class F>
-__device__ __forceinline__ void run_tile(const GemvArgs& a, const uint8_t* w, uint64_t row_bytes, uint32_t ra,
-                                         uint32_t rb, const Lane& L, uint32_t first, uint32_t step,
-                                         const MmaSmem& sm, float* s_scale, float* acc) {
-    const uint32_t K = a.K;
-    const uint32_t nblk32 = K / 32;                        // only used by the 32-block formats
+__device__ __forceinline__ void tile_rows(const uint8_t* base, uint64_t rb, uint32_t K, const Lane& L,
+                                          uint32_t first, uint32_t step, const MmaSmem& sm, float* acc) {
+    const uint32_t nblk32 = K / 32;
     const uint32_t nit = (K + F::SB - 1) / F::SB;
-    const uint8_t* ga = w + (uint64_t)ra * row_bytes;
-    const uint8_t* gb = w + (uint64_t)rb * row_bytes;
-    auto nvalid = [&](uint32_t it) -> uint32_t { return F::SB == 256 ? 1u : min(4u, nblk32 - it * 4); };
-    typename F::Raw r0;
-    uint32_t it = first;
-    if (it < nit) F::load(r0, ga + (uint64_t)it * F::SBB, gb + (uint64_t)it * F::SBB, nvalid(it), L);
-    pdl_wait();                                            // x comes from the previous kernel
-    stage_x(a, sm, s_scale);
-    for (; it < nit; it += step) {
-        typename F::Raw r1;
-        const uint32_t nx = it + step;
-        if (nx < nit) F::load(r1, ga + (uint64_t)nx * F::SBB, gb + (uint64_t)nx * F::SBB, nvalid(nx), L);
-        F::compute(r0, it * F::SB, nvalid(it), L, sm, acc);
-        r0 = r1;
+    const uint8_t* rg = base + (uint64_t)L.g * rb;
+    const uint8_t* rg8 = base + (uint64_t)(L.g + 8) * rb;
+    for (uint32_t it = first; it < nit; it += step) {
+        const uint32_t nvalid = F::SB == 256 ? 1u : min(4u, nblk32 - it * 4);
+        F::compute(rg + (uint64_t)it * F::SBB, rg8 + (uint64_t)it * F::SBB, it * F::SB, nvalid, L, sm, acc);
     }
 }
 
 // ------------------------------------------------------------------ kernel
 
 __global__ void __launch_bounds__(kMThreads)
-gemv_mma_kernel(const __grid_constant__ GemvArgs a) {
-    extern __shared__ __align__(16) float smem[];
+gemv_mma_kernel(const __grid_constant__ GemvArgs a, uint32_t stage_bytes) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
     __shared__ float s_scale;
+    __shared__ __align__(8) uint64_t bars[kStages];
+    __shared__ int s_fail;
     pdl_trigger();
-    const uint32_t K = a.K;
+    const uint32_t K = a.K, tid = threadIdx.x;
+    const GemvSeg& last = a.seg[a.nseg - 1];
+    const uint32_t n_tiles = last.tile0 + (last.rows + 15) / 16;
+
+    uint8_t* stages = smem_raw;                                   // kStages * stage_bytes
     MmaSmem sm;
-    sm.xf = smem;
-    sm.xh = reinterpret_cast<uint32_t*>(smem + K);
+    sm.xf = reinterpret_cast<float*>(smem_raw + kStages * stage_bytes);
+    sm.xh = reinterpret_cast<uint32_t*>(sm.xf + K);
     sm.xl = sm.xh + K / 2;
     sm.sx = reinterpret_cast<float*>(sm.xl + K / 2);
     sm.red = sm.sx + K / 16;
     sm.part = sm.red + 2 * kMWarps;
 
-    uint32_t s = 0;
-#pragma unroll
-    for (uint32_t i = 1; i < kMaxSegs; i++)
-        if (i < a.nseg && blockIdx.x >= a.seg[i].tile0) s = i;
-    const GemvSeg& G = a.seg[s];
-    const uint32_t row0 = (blockIdx.x - G.tile0) * 16;
-    const bool glu = G.epi == EPI_GLU_SILU || G.epi == EPI_GLU_GELU;
-    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    // weights first: they do not depend on the previous kernel
+    if (tid == 0) {
+        s_fail = 0;
+        for (uint32_t i = 0; i < kStages; i++) mbar_init(&bars[i], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        for (uint32_t i = 0; i < kStages; i++) {
+            const uint32_t t = blockIdx.x + i * gridDim.x;
+            if (t < n_tiles) issue_tile(a, t, stages + i * stage_bytes, &bars[i]);
+        }
+    }
+    pdl_wait();                                                   // x comes from the previous kernel
+    stage_x(a, sm, &s_scale);                                     // ends with __syncthreads
+
+    const uint32_t lane = tid & 31u, warp = tid >> 5;
     Lane L;
     L.g = lane >> 2;
     L.tig = lane & 3u;
     L.slot = L.g >> 1;
     L.xpart = (L.g & 1u) ? sm.xl : sm.xh;
-    // rows past the end of the matrix read its last row; their results are dropped
-    const uint32_t ra = min(row0 + L.g, G.rows - 1), rb = min(row0 + L.g + 8, G.rows - 1);
 
-    // A gated tile gives the gate matrix to warps 0..3 and the up matrix to
-    // warps 4..7; otherwise all 8 warps share the one matrix.
-    const uint32_t half = kMWarps / 2;
-    const bool up = glu && warp >= half;
-    const uint8_t* wm = up ? G.w2 : G.w;
-    const uint64_t rbytes = up ? G.row_bytes2 : G.row_bytes;
-    const uint32_t first = glu ? warp % half : warp, step = glu ? half : kMWarps;
-    float acc[2] = {0.f, 0.f};
-    switch (G.type) {
-    case T_Q4_K: run_tile<FQ4K>(a, wm, rbytes, ra, rb, L, first, step, sm, &s_scale, acc); break;
-    case T_Q6_K: run_tile<FQ6K>(a, wm, rbytes, ra, rb, L, first, step, sm, &s_scale, acc); break;
-    case T_Q8_0: run_tile<FQ80>(a, wm, rbytes, ra, rb, L, first, step, sm, &s_scale, acc); break;
-    default:     run_tile<FQ40>(a, wm, rbytes, ra, rb, L, first, step, sm, &s_scale, acc); break;
-    }
-
-    if (L.tig == 0) {
-        sm.part[warp * 16 + L.g] = acc[0];
-        sm.part[warp * 16 + L.g + 8] = acc[1];
-    }
-    __syncthreads();
-
-    // epilogue: thread r < 16 finishes row row0 + r
-    unsigned long long key = 0ull;
-    if (threadIdx.x < 16) {
-        const uint32_t r = threadIdx.x, row = row0 + r;
-        float v = 0.f, u = 0.f;
-#pragma unroll
-        for (uint32_t w = 0; w < kMWarps; w++) {
-            if (glu && w >= half) u += sm.part[w * 16 + r];
-            else v += sm.part[w * 16 + r];
+    uint32_t i = 0;
+    for (uint32_t t = blockIdx.x; t < n_tiles; t += gridDim.x, i++) {
+        const uint32_t st = i % kStages, parity = (i / kStages) & 1u;
+        uint8_t* buf = stages + st * stage_bytes;
+        if (!mbar_wait(&bars[st], parity)) {
+            atomicOr(a.err, kErrWaitTimeout);
+            s_fail = 1;
         }
-        v *= s_scale;
-        u *= s_scale;
-        if (row < G.rows) {
-            switch (G.epi) {
-            case EPI_STORE: if (G.bias) v += G.bias[row]; G.out[row] = v; break;
-            case EPI_RESID: if (G.bias) v += G.bias[row]; G.out[row] += v; break;
-            case EPI_GLU_SILU: v = v / (1.0f + expf(-v)) * u; G.out[row] = v; break;   // model.c:22
-            case EPI_GLU_GELU: v = m_gelu(v) * u; G.out[row] = v; break;
-            case EPI_GELU: if (G.bias) v += G.bias[row]; v = m_gelu(v); G.out[row] = v; break;
+        __syncthreads();
+        if (s_fail) return;                       // a copy never landed: the flag is set, stop
+        const TileRef tr = tile_of(a, t);
+        const GemvSeg& G = a.seg[tr.seg];
+        const bool glu = G.epi == EPI_GLU_SILU || G.epi == EPI_GLU_GELU;
+        // a gated tile: warps 0..3 take the gate rows, 4..7 the up rows
+        const uint32_t half = kMWarps / 2;
+        const bool up = glu && warp >= half;
+        const uint8_t* base = up ? buf + up_offset(G) : buf;
+        const uint64_t rb = up ? G.row_bytes2 : G.row_bytes;
+        const uint32_t first = glu ? warp % half : warp, step = glu ? half : kMWarps;
+        float acc[2] = {0.f, 0.f};
+        switch (G.type) {
+        case T_Q4_K: tile_rows<FQ4K>(base, rb, K, L, first, step, sm, acc); break;
+        case T_Q6_K: tile_rows<FQ6K>(base, rb, K, L, first, step, sm, acc); break;
+        case T_Q8_0: tile_rows<FQ80>(base, rb, K, L, first, step, sm, acc); break;
+        default:     tile_rows<FQ40>(base, rb, K, L, first, step, sm, acc); break;
+        }
+        // the lanes of a quad hold different slots' sums: combine them
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 1);
+            acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 2);
+        }
+        if (L.tig == 0) {
+            sm.part[warp * 16 + L.g] = acc[0];
+            sm.part[warp * 16 + L.g + 8] = acc[1];
+        }
+        __syncthreads();                          // stage buffer consumed, partials ready
+        if (tid == 0) {
+            const uint32_t nt = t + kStages * gridDim.x;
+            if (nt < n_tiles) issue_tile(a, nt, buf, &bars[st]);
+        }
+        // epilogue: thread r < 16 finishes row row0 + r
+        unsigned long long key = 0ull;
+        if (tid < 16) {
+            const uint32_t r = tid, row = tr.row0 + r;
+            float v = 0.f, u = 0.f;
+#pragma unroll
+            for (uint32_t w = 0; w < kMWarps; w++) {
+                if (glu && w >= half) u += sm.part[w * 16 + r];
+                else v += sm.part[w * 16 + r];
             }
-            if (G.argmax) key = m_key(v, row);
+            v *= s_scale;
+            u *= s_scale;
+            if (r < tr.nrows) {
+                switch (G.epi) {
+                case EPI_STORE: if (G.bias) v += G.bias[row]; G.out[row] = v; break;
+                case EPI_RESID: if (G.bias) v += G.bias[row]; G.out[row] += v; break;
+                case EPI_GLU_SILU: v = v / (1.0f + expf(-v)) * u; G.out[row] = v; break;   // model.c:22
+                case EPI_GLU_GELU: v = m_gelu(v) * u; G.out[row] = v; break;
+                case EPI_GELU: if (G.bias) v += G.bias[row]; v = m_gelu(v); G.out[row] = v; break;
+                }
+                if (G.argmax) key = m_key(v, row);
+            }
         }
-    }
-    if (a.argmax_key != nullptr && warp == 0) {
+        if (a.argmax_key != nullptr && warp == 0) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
-            key = k2 > key ? k2 : key;
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+                key = k2 > key ? k2 : key;
+            }
+            if (lane == 0 && key != 0ull) atomicMax(a.argmax_key, key);
         }
-        if (lane == 0 && key != 0ull) atomicMax(a.argmax_key, key);
+        __syncthreads();                          // part[] free for the next tile
     }
 }
 
-size_t gemv_mma_smem(uint32_t K) {
+static size_t x_smem(uint32_t K) {
     // xf (4K bytes), xh, xl (2K bytes each), sx (K/4 bytes), then red and part
     return (size_t)K * 8 + (size_t)K / 16 * 4 + 2 * kMWarps * 4 + kMWarps * 16 * 4;
 }
 
+constexpr size_t kSmemLimit = 220 * 1024;     // dynamic shared memory per CTA (leaves room for static)
+static int g_mma_regs = 128;
+
 bool gemv_mma_init() {
-    return LM_CUDA(cudaFuncSetAttribute(gemv_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)) &&
+    cudaFuncAttributes fa;
+    if (!LM_CUDA(cudaFuncGetAttributes(&fa, gemv_mma_kernel))) return false;
+    g_mma_regs = fa.numRegs > 0 ? fa.numRegs : 128;
+    return LM_CUDA(cudaFuncSetAttribute(gemv_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit)) &&
            LM_CUDA(cudaFuncSetAttribute(gemv_mma_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
 }
 
-// Launch when every segment is a tensor-core format (and a gated pair shares
-// one format); *handled = false otherwise, and the caller uses k_gemv.cu.
+// Launch when every segment is a tensor-core format (a gated pair sharing one
+// format) and the tiles fit in shared memory; *handled = false otherwise, and
+// the caller uses k_gemv.cu.
 bool launch_gemv_mma(const GemvArgs& in, cudaStream_t st, bool* handled) {
     *handled = false;
-    // the 32-block formats iterate in runs of 4 blocks, the last run may be partial
     if (in.K % 32 != 0) return true;
+    uint64_t stage = 0;
     for (uint32_t i = 0; i < in.nseg; i++) {
         const GemvSeg& g = in.seg[i];
         const bool glu = g.epi == EPI_GLU_SILU || g.epi == EPI_GLU_GELU;
         if (!mma_type(g.type) || (glu && g.type2 != g.type)) return true;
         if (type_bytes(g.type, in.K) == 0) return true;
+        // bulk copies need 16-byte aligned sources: the matrix base and every
+        // tile start (row multiples of 16, so 16 * row_bytes suffices)
+        if (reinterpret_cast<uintptr_t>(g.w) % 16 != 0 || (glu && reinterpret_cast<uintptr_t>(g.w2) % 16 != 0))
+            return true;
+        const uint64_t t1 = ((16 * g.row_bytes) + 15) & ~uint64_t(15);
+        const uint64_t t2 = glu ? ((16 * g.row_bytes2) + 15) & ~uint64_t(15) : 0;
+        stage = stage > t1 + t2 ? stage : t1 + t2;
     }
+    // 16 bytes of slack past each stage: funnel-shifted word reads at the tile end
+    stage = (stage + 16 + 127) & ~uint64_t(127);
     if (in.norm != NORM_NONE && (reinterpret_cast<uintptr_t>(in.norm_w) % 16 != 0 ||
                                  (in.norm == NORM_LAYER && reinterpret_cast<uintptr_t>(in.norm_b) % 16 != 0)))
         return true;
     if (reinterpret_cast<uintptr_t>(in.x) % 16 != 0) return true;
+    const size_t smem = kStages * stage + x_smem(in.K);
+    if (smem > kSmemLimit) return true;
     GemvArgs a = in;
     uint32_t tiles = 0;
     for (uint32_t i = 0; i < a.nseg; i++) {
         a.seg[i].tile0 = tiles;
         tiles += (a.seg[i].rows + 15) / 16;
     }
-    const size_t smem = gemv_mma_smem(a.K);
-    if (smem > 200 * 1024) return true;
+    if (a.err == nullptr) a.err = dev_err_word();
+    if (a.err == nullptr) return false;
+    // resident CTAs per SM from registers, threads and shared memory (computed
+    // here rather than queried: launches are also made during graph capture)
+    uint32_t per_sm = 65536u / ((uint32_t)g_mma_regs * kMThreads);
+    per_sm = per_sm < 2048u / kMThreads ? per_sm : 2048u / kMThreads;
+    const uint32_t by_smem = (uint32_t)((228u * 1024u) / (smem + 1024u));
+    per_sm = per_sm < by_smem ? per_sm : by_smem;
+    if (per_sm < 1) per_sm = 1;
+    uint32_t grid = (uint32_t)sm_count() * per_sm;
+    if (grid > tiles) grid = tiles;
     *handled = true;
-    return LM_CUDA(launch_k(gemv_mma_kernel, dim3(tiles), dim3(kMThreads), smem, st, a));
+    return LM_CUDA(launch_k(gemv_mma_kernel, dim3(grid), dim3(kMThreads), smem, st, a, (uint32_t)stage));
 }
 
 }  // namespace lm

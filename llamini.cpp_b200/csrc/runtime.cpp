@@ -80,6 +80,14 @@ bool pdl_enabled() {
 }
 int sm_count() { return g_sms; }
 
+static uint32_t* g_err_word = nullptr;
+uint32_t* dev_err_word() {
+    if (!g_err_word && ensure_device()) {
+        if (LM_CUDA(cudaMalloc(&g_err_word, 16))) LM_CUDA(cudaMemset(g_err_word, 0, 16));
+    }
+    return g_err_word;
+}
+
 void* dev_alloc(size_t bytes) {
     if (!ensure_device()) return nullptr;
     void* p = nullptr;

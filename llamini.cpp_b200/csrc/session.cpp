@@ -173,6 +173,7 @@ bool enqueue_step(llamini_session* s, cudaStream_t st, bool trace, bool nll) {
         const llamini_session::Layer& W = s->layers[l];
         // norm + QKV
         GemvArgs a;
+        a.err = &s->st->err;
         a.x = s->hidden;
         a.K = s->dim;
         a.norm = gpt2 ? NORM_LAYER : NORM_RMS;
@@ -210,6 +211,7 @@ bool enqueue_step(llamini_session* s, cudaStream_t st, bool trace, bool nll) {
         if (!launch_attention(at, st)) return false;
         // O projection + residual
         GemvArgs o;
+        o.err = &s->st->err;
         o.x = s->attn;
         o.K = s->qd;
         o.nseg = 1;
@@ -217,6 +219,7 @@ bool enqueue_step(llamini_session* s, cudaStream_t st, bool trace, bool nll) {
         if (!launch_gemv(o, st)) return false;
         // norm + FFN up (gated for LLaMA, GELU for GPT-2)
         GemvArgs f;
+        f.err = &s->st->err;
         f.x = s->hidden;
         f.K = s->dim;
         f.norm = gpt2 ? NORM_LAYER : NORM_RMS;
@@ -232,6 +235,7 @@ bool enqueue_step(llamini_session* s, cudaStream_t st, bool trace, bool nll) {
         if (!launch_gemv(f, st)) return false;
         // down + residual
         GemvArgs d;
+        d.err = &s->st->err;
         d.x = s->ffn_h;
         d.K = s->ffn;
         d.nseg = 1;
@@ -240,6 +244,7 @@ bool enqueue_step(llamini_session* s, cudaStream_t st, bool trace, bool nll) {
         if (trace && !launch_copy_f32(s->trace + (size_t)l * s->dim, s->hidden, s->dim, st)) return false;
     }
     GemvArgs h;
+    h.err = &s->st->err;
     h.x = s->hidden;
     h.K = s->dim;
     h.norm = gpt2 ? NORM_LAYER : NORM_RMS;
@@ -413,7 +418,7 @@ bool write_state(llamini_session* s, u32 pos, u32 n_prompt, bool reset_nll) {
     s->st_host->pos = pos;
     s->st_host->n_prompt = n_prompt;
     s->st_host->trace = 0;
-    s->st_host->pad = 0;
+    s->st_host->err = 0;
     s->st_host->argmax_key = 0;
     s->st_host->nll = 0.0;
     s->st_host->nll_count = 0;
@@ -443,6 +448,17 @@ bool run_steps(llamini_session* s, u32 n) {
     }
     while (left--) if (!LM_CUDA(cudaGraphLaunch(s->g_one, st))) return false;
     s->pos += n;
+    return true;
+}
+
+// Device-side error bits (bounded waits that ran out): read after a sync.
+bool check_device_errors(llamini_session* s) {
+    uint32_t e = 0;
+    if (!LM_CUDA(cudaMemcpy(&e, &s->st->err, 4, cudaMemcpyDeviceToHost))) return false;
+    if (e) {
+        set_error("a kernel reported error bits 0x%x (a bounded wait on a weight copy ran out)", e);
+        return false;
+    }
     return true;
 }
 
@@ -477,7 +493,7 @@ static void forward_one(llamini_session* s, u32 pos, u32 token, f32* logits_out)
     s->max_pos = saved;
     if (!ok) return;
     if (logits_out && !LM_CUDA(cudaMemcpyAsync(logits_out, s->logits, (size_t)s->vocab * 4, cudaMemcpyDeviceToHost, st))) return;
-    LM_CUDA(cudaStreamSynchronize(st));
+    if (!LM_CUDA(cudaStreamSynchronize(st)) || !check_device_errors(s)) return;
     set_cur_seq(s);
 }
 
@@ -539,6 +555,7 @@ static u32 generate(llamini_session* s, u32* input, u32 n_in, u32* out, u32 max_
             if (!stop) last = done;
             if (stop) break;
         }
+        check_device_errors(s);
         set_cur_seq(s, last);
     }
     clock_gettime(CLOCK_MONOTONIC, &t1);
@@ -634,7 +651,7 @@ int llamini_session_tokens(llamini_session* s, u32* out, u32 n) {
     const u32 valid = s->pos + 1 > s->n_prompt ? s->pos + 1 : s->n_prompt;
     const u32 k = n < valid ? n : valid;
     if (!LM_CUDA(cudaMemcpyAsync(out, s->tokens, (size_t)k * 4, cudaMemcpyDeviceToHost, lm::stream())) ||
-        !LM_CUDA(cudaStreamSynchronize(lm::stream())))
+        !LM_CUDA(cudaStreamSynchronize(lm::stream())) || !lm::check_device_errors(s))
         return -1;
     lm::set_cur_seq(s);
     return (int)valid;
