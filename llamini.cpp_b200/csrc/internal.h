@@ -137,7 +137,7 @@ struct AttnArgs {
     uint32_t kv_f16;       // 1: fp16 elements, 0: f32 elements
     float* out;            // [n_heads*hd]
     float* part;           // [n_heads][n_split][hd + 2] partial results
-    uint32_t* counter;     // [n_kv] completion counters (return to 0 after use)
+    uint32_t* counter;     // [n_heads] completion counters (return to 0 after use)
     uint32_t n_heads, n_kv, hd, max_seq, n_split;
     uint32_t rope;         // 0 none, 1 NORM, 2 NEOX
     const float* theta;    // [hd/2] rotation frequencies base^(-2j/hd), computed on the host

@@ -5,15 +5,18 @@
 // lives on the device in [kv_head][position][head_dim] order (f32 by default,
 // fp16 on request), so a head's keys and values are contiguous.
 //
-// Grid = (kv heads) x (position splits). A CTA takes one kv head, all query
-// heads that share it (the GQA group, model.c:220) and a contiguous slice of
-// positions 0..pos; only as many splits as the context needs (16 positions or
-// more each) do work. The CTA rotates the queries itself (angle = pos * theta_j
+// Grid = (query heads) x (position splits). A CTA takes one query head and a
+// contiguous slice of positions 0..pos; only as many splits as the context
+// needs (64 positions or more each) do work. It stages the slice's keys and
+// values of the head's kv head (the GQA group, model.c:220) in shared memory
+// 64 positions at a time, scores one position per thread and keeps an online
+// softmax across chunks. The CTA rotates its query itself (angle = pos * theta_j
 // with theta_j = base^(-2j/hd) computed on the host with the C library's powf,
 // exactly the reference's value); the CTA whose slice holds `pos` also rotates
-// the new key and stores the new key/value before reading them back. Each CTA
-// writes (running max, sum of exponentials, weighted value sum) per head; the
-// last CTA of a kv head (atomic ticket) merges them with all of its threads.
+// the new key and uses the new key/value from shared memory, and the group's
+// first head stores them into the cache. Each CTA writes (running max, sum of
+// exponentials, weighted value sum); the last CTA of a head (atomic ticket)
+// merges them with all of its threads.
 #include "internal.h"
 #include "pdl.cuh"
 
@@ -22,7 +25,6 @@
 namespace lm {
 
 constexpr int kAttnThreads = 128;
-constexpr uint32_t kMinSplitLen = 16;     // positions per split before another split is used
 
 __device__ __forceinline__ float kv_load(const float* p) { return *p; }
 __device__ __forceinline__ float kv_load(const __half* p) { return __half2float(*p); }
@@ -48,193 +50,175 @@ __device__ void rope_vecs(float* v, uint32_t nvec, uint32_t hd, uint32_t pos, ui
 }
 
 constexpr uint32_t kChunk = 64;           // positions staged in shared memory at a time
-constexpr uint32_t kMaxHeadsPerWarp = 4;  // G <= 16 query heads per kv head
-constexpr uint32_t kMaxDimPerLane = 8;    // head_dim <= 256
 
-// Stage rows [t0, t0+n) of one kv head's cache (row length hd) as f32.
-__device__ __forceinline__ void stage_rows(float* dst, const float* src, uint32_t n, uint32_t hd) {
-    if ((hd & 3u) == 0) {
-        const float4* s4 = reinterpret_cast<const float4*>(src);
-        float4* d4 = reinterpret_cast<float4*>(dst);
-        for (uint32_t i = threadIdx.x; i < n * hd / 4; i += blockDim.x) d4[i] = s4[i];
-    } else {
-        for (uint32_t i = threadIdx.x; i < n * hd; i += blockDim.x) dst[i] = src[i];
-    }
-}
-__device__ __forceinline__ void stage_rows(float* dst, const __half* src, uint32_t n, uint32_t hd) {
-    if ((hd & 3u) == 0) {
-        const uint2* s2 = reinterpret_cast<const uint2*>(src);
-        float4* d4 = reinterpret_cast<float4*>(dst);
-        for (uint32_t i = threadIdx.x; i < n * hd / 4; i += blockDim.x) {
-            const uint2 v = s2[i];
-            const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
-            const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
-            d4[i] = make_float4(lo.x, lo.y, hi.x, hi.y);
-        }
-    } else {
-        for (uint32_t i = threadIdx.x; i < n * hd; i += blockDim.x) dst[i] = __half2float(src[i]);
+// Stage rows [c0, c0+n) of one kv head's cache (row length hd) as f32 with a
+// row stride of hd+1 floats, so that "thread t reads row t" is conflict-free.
+template <typename KV>
+__device__ __forceinline__ void stage_rows(float* dst, const KV* src, uint32_t n, uint32_t hd) {
+    for (uint32_t i = threadIdx.x; i < n * hd; i += blockDim.x) {
+        const uint32_t t = i / hd, d = i - t * hd;
+        dst[t * (hd + 1) + d] = kv_load(src + i);
     }
 }
 
+// One CTA per (query head, position split). q, and for the split holding
+// `pos` the new key/value, are rotated locally; the new key/value rows are used
+// from shared memory and written to the cache by the group's first head only,
+// so no CTA reads a cache row another CTA of this launch writes.
 template <typename KV>
 __global__ void __launch_bounds__(kAttnThreads)
 attn_decode_kernel(const AttnArgs a) {
     extern __shared__ __align__(16) float sm[];
     __shared__ int is_last;
+    __shared__ float s_m, s_l;
     pdl_trigger();
     pdl_wait();                                   // q/k/v come from the QKV projection
-    const uint32_t G = a.n_heads / a.n_kv;        // query heads per kv head
-    const uint32_t hd = a.hd;
-    const uint32_t g = blockIdx.x, split = blockIdx.y;
+    const uint32_t G = a.n_heads / a.n_kv;        // query heads per kv head (model.c:220)
+    const uint32_t hd = a.hd, hp = hd + 1;
+    const uint32_t h = blockIdx.x, g = h / G, split = blockIdx.y;
     const uint32_t pos = a.st->pos;
     const uint32_t L = pos + 1;
-    // splits in use: enough that each has >= kMinSplitLen positions
-    uint32_t ns = (L + kMinSplitLen - 1) / kMinSplitLen;
+    // splits in use: each covers >= kChunk positions
+    uint32_t ns = (L + kChunk - 1) / kChunk;
     ns = ns < a.n_split ? ns : a.n_split;
     if (split >= ns) return;
     const uint32_t chunk = (L + ns - 1) / ns;
     const uint32_t t0 = min(split * chunk, L);
     const uint32_t t1 = min(t0 + chunk, L);
+    const uint32_t tid = threadIdx.x;
 
-    const uint32_t hd4 = (hd + 3u) & ~3u;
-    float* qs = sm;                      // [G][hd]
-    float* kvn = qs + G * hd4;           // [2][hd] new key, new value
-    float* ks = kvn + 2 * hd4;           // [kChunk][hd]
-    float* vs = ks + kChunk * hd;        // [kChunk][hd]
-    float* sc = vs + kChunk * hd;        // [G][kChunk] scores / probabilities (and merge scratch)
+    float* qs = sm;                  // [hd]
+    float* kn = qs + hp;             // [hd] new key
+    float* vn = kn + hp;             // [hd] new value
+    float* ks = vn + hp;             // [kChunk][hd+1]
+    float* vs = ks + kChunk * hp;    // [kChunk][hd+1]
+    float* sc = vs + kChunk * hp;    // [kChunk] probabilities (and merge weights)
 
-    const float* q = a.qkv + (uint64_t)g * G * hd;
-    for (uint32_t i = threadIdx.x; i < G * hd; i += blockDim.x) qs[(i / hd) * hd4 + i % hd] = q[i];
     const bool has_new = t0 <= pos && pos < t1;
-    if (has_new) {
-        const float* kn = a.qkv + (uint64_t)a.n_heads * hd + (uint64_t)g * hd;
-        const float* vn = kn + (uint64_t)a.n_kv * hd;
-        for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) { kvn[i] = kn[i]; kvn[hd4 + i] = vn[i]; }
+    for (uint32_t i = tid; i < hd; i += blockDim.x) {
+        qs[i] = a.qkv[(uint64_t)h * hd + i];
+        if (has_new) {
+            kn[i] = a.qkv[(uint64_t)a.n_heads * hd + (uint64_t)g * hd + i];
+            vn[i] = a.qkv[(uint64_t)(a.n_heads + a.n_kv) * hd + (uint64_t)g * hd + i];
+        }
     }
     __syncthreads();
-    for (uint32_t i = 0; i < G; i++) rope_vecs(qs + i * hd4, 1, hd, pos, a.rope, a.theta);
-    if (has_new) rope_vecs(kvn, 1, hd, pos, a.rope, a.theta);
+    rope_vecs(qs, 1, hd, pos, a.rope, a.theta);
+    if (has_new) rope_vecs(kn, 1, hd, pos, a.rope, a.theta);
     __syncthreads();
     KV* kc = reinterpret_cast<KV*>(a.kc) + (uint64_t)g * a.max_seq * hd;
     KV* vc = reinterpret_cast<KV*>(a.vc) + (uint64_t)g * a.max_seq * hd;
-    if (has_new) {
-        for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) {
-            kv_store(kc + (uint64_t)pos * hd + i, kvn[i]);
-            kv_store(vc + (uint64_t)pos * hd + i, kvn[hd4 + i]);
+    if (has_new && h == g * G) {                  // one writer per kv head
+        for (uint32_t i = tid; i < hd; i += blockDim.x) {
+            kv_store(kc + (uint64_t)pos * hd + i, kn[i]);
+            kv_store(vc + (uint64_t)pos * hd + i, vn[i]);
         }
     }
-    __syncthreads();                               // the new row is visible to the staging loads
-
-    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const float rscale = sqrtf((float)hd);        // model.c:243
-    // online softmax state of the heads this warp owns (i = warp + nw * j)
-    float mrun[kMaxHeadsPerWarp], lrun[kMaxHeadsPerWarp], o[kMaxHeadsPerWarp][kMaxDimPerLane];
-#pragma unroll
-    for (uint32_t j = 0; j < kMaxHeadsPerWarp; j++) {
-        mrun[j] = -INFINITY;
-        lrun[j] = 0.f;
-#pragma unroll
-        for (uint32_t d = 0; d < kMaxDimPerLane; d++) o[j][d] = 0.f;
-    }
+    float o[2] = {0.f, 0.f};                      // thread owns dims tid, tid + 128
+    if (tid == 0) { s_m = -INFINITY; s_l = 0.f; }
 
     for (uint32_t c0 = t0; c0 < t1; c0 += kChunk) {
         const uint32_t n = min(kChunk, t1 - c0);
-        __syncthreads();                           // previous chunk fully consumed
-        stage_rows(ks, kc + (uint64_t)c0 * hd, n, hd);
-        stage_rows(vs, vc + (uint64_t)c0 * hd, n, hd);
+        __syncthreads();                           // previous chunk consumed
+        // rows < pos come from the cache (written by earlier steps); row pos
+        // is this step's key/value, taken from shared memory
+        const uint32_t nold = (c0 + n > pos) ? pos - c0 : n;
+        stage_rows(ks, kc + (uint64_t)c0 * hd, nold, hd);
+        stage_rows(vs, vc + (uint64_t)c0 * hd, nold, hd);
+        if (nold < n)
+            for (uint32_t i = tid; i < hd; i += blockDim.x) { ks[nold * hp + i] = kn[i]; vs[nold * hp + i] = vn[i]; }
         __syncthreads();
-        // scores: warp per position, lanes over head_dim, all G heads
-        for (uint32_t t = warp; t < n; t += nw) {
-            for (uint32_t i = 0; i < G; i++) {
-                float s = 0.f;
-                for (uint32_t d = lane; d < hd; d += 32) s = fmaf(qs[i * hd4 + d], ks[t * hd + d], s);
+        // scores: thread t takes position t
+        float sv = -INFINITY;
+        if (tid < n) {
+            float s = 0.f;
+            const float* kr = ks + tid * hp;
+            for (uint32_t d = 0; d < hd; d++) s = fmaf(qs[d], kr[d], s);
+            sv = s / rscale;
+        }
+        // chunk max / sum over the first two warps (kChunk = 64 positions)
+        if (tid < 64) {
+            float m = sv;
 #pragma unroll
-                for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-                if (lane == 0) sc[i * kChunk + t] = s / rscale;
-            }
+            for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+            if ((tid & 31u) == 0) sc[kChunk + (tid >> 5)] = m;
         }
         __syncthreads();
+        const float mprev = s_m;
+        const float mnew = fmaxf(mprev, fmaxf(sc[kChunk], sc[kChunk + 1]));
+        const float p = tid < n ? expf(sv - mnew) : 0.f;
+        if (tid < kChunk) sc[tid] = p;
+        if (tid < 64) {
+            float l = p;
 #pragma unroll
-        for (uint32_t j = 0; j < kMaxHeadsPerWarp; j++) {
-            const uint32_t i = warp + nw * j;
-            if (i >= G) break;
-            float* si = sc + i * kChunk;
-            float cm = -INFINITY;
-            for (uint32_t t = lane; t < n; t += 32) cm = fmaxf(cm, si[t]);
+            for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+            if ((tid & 31u) == 0) sc[kChunk + 2 + (tid >> 5)] = l;
+        }
+        __syncthreads();
+        const float corr = expf(mprev - mnew);    // 0 on the first chunk
+        if (tid == 0) {
+            s_l = s_l * corr + sc[kChunk + 2] + sc[kChunk + 3];
+            s_m = mnew;
+        }
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, off));
-            const float mnew = fmaxf(mrun[j], cm);
-            const float corr = expf(mrun[j] - mnew);      // 0 on the first chunk
-            float cl = 0.f;
-            for (uint32_t t = lane; t < n; t += 32) {
-                const float p = expf(si[t] - mnew);
-                si[t] = p;
-                cl += p;
-            }
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) cl += __shfl_xor_sync(0xffffffffu, cl, off);
-            __syncwarp();
-            lrun[j] = lrun[j] * corr + cl;
-            mrun[j] = mnew;
-#pragma unroll
-            for (uint32_t dd = 0; dd < kMaxDimPerLane; dd++) {
-                const uint32_t d = lane + 32 * dd;
-                if (d >= hd) break;
-                float acc = o[j][dd] * corr;
-                for (uint32_t t = 0; t < n; t++) acc = fmaf(si[t], vs[t * hd + d], acc);
-                o[j][dd] = acc;
+        for (int j = 0; j < 2; j++) {
+            const uint32_t d = tid + 128 * j;
+            if (d < hd) {
+                float acc = o[j] * corr;
+                for (uint32_t t = 0; t < n; t++) acc = fmaf(sc[t], vs[t * hp + d], acc);
+                o[j] = acc;
             }
         }
     }
-
+    __syncthreads();
     const uint32_t stride = hd + 2;
+    float* dst = a.part + ((uint64_t)h * a.n_split + split) * stride;
 #pragma unroll
-    for (uint32_t j = 0; j < kMaxHeadsPerWarp; j++) {
-        const uint32_t i = warp + nw * j;
-        if (i >= G) break;
-        const uint32_t h = g * G + i;
-        float* dst = a.part + ((uint64_t)h * a.n_split + split) * stride;
-#pragma unroll
-        for (uint32_t dd = 0; dd < kMaxDimPerLane; dd++) {
-            const uint32_t d = lane + 32 * dd;
-            if (d >= hd) break;
-            if (ns == 1) a.out[(uint64_t)h * hd + d] = o[j][dd] / lrun[j];
-            else dst[2 + d] = o[j][dd];
+    for (int j = 0; j < 2; j++) {
+        const uint32_t d = tid + 128 * j;
+        if (d < hd) {
+            if (ns == 1) a.out[(uint64_t)h * hd + d] = o[j] / s_l;
+            else dst[2 + d] = o[j];
         }
-        if (ns > 1 && lane == 0) { dst[0] = mrun[j]; dst[1] = lrun[j]; }
     }
     if (ns == 1) return;
+    if (tid == 0) { dst[0] = s_m; dst[1] = s_l; }
 
-    // the last CTA of this kv head merges the partials of its G heads
+    // the last CTA of this head merges the splits (model.c:247-257 in one pass)
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) is_last = atomicAdd(&a.counter[g], 1u) == ns - 1;
+    if (tid == 0) is_last = atomicAdd(&a.counter[h], 1u) == ns - 1;
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    float* wts = sc;                               // [G][ns] merge weights, then [G] totals
-    float* tot = sc + G * ns;
-    for (uint32_t t = threadIdx.x; t < G; t += blockDim.x) {
-        const float* src = a.part + (uint64_t)(g * G + t) * a.n_split * stride;
+    const float* src = a.part + (uint64_t)h * a.n_split * stride;
+    if (tid < 32) {
         float M = -INFINITY;
-        for (uint32_t s = 0; s < ns; s++) M = fmaxf(M, __ldcg(src + s * stride));
+        for (uint32_t s = tid; s < ns; s += 32) M = fmaxf(M, __ldcg(src + s * stride));
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
         float Ls = 0.f;
-        for (uint32_t s = 0; s < ns; s++) {
+        for (uint32_t s = tid; s < ns; s += 32) {
             const float w = expf(__ldcg(src + s * stride) - M);
-            wts[t * ns + s] = w;
+            sc[s] = w;
             Ls += w * __ldcg(src + s * stride + 1);
         }
-        tot[t] = Ls;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) Ls += __shfl_xor_sync(0xffffffffu, Ls, off);
+        if (tid == 0) s_l = Ls;
     }
     __syncthreads();
-    for (uint32_t idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
-        const uint32_t t = idx / hd, d = idx % hd;
-        const float* src = a.part + (uint64_t)(g * G + t) * a.n_split * stride + 2 + d;
-        float acc = 0.f;
-        for (uint32_t s = 0; s < ns; s++) acc = fmaf(__ldcg(src + s * stride), wts[t * ns + s], acc);
-        a.out[(uint64_t)(g * G + t) * hd + d] = acc / tot[t];
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const uint32_t d = tid + 128 * j;
+        if (d < hd) {
+            float acc = 0.f;
+            for (uint32_t s = 0; s < ns; s++) acc = fmaf(__ldcg(src + s * stride + 2 + d), sc[s], acc);
+            a.out[(uint64_t)h * hd + d] = acc / s_l;
+        }
     }
-    if (threadIdx.x == 0) a.counter[g] = 0u;
+    if (tid == 0) a.counter[h] = 0u;
 }
 
 bool attn_init() {
@@ -245,21 +229,15 @@ bool attn_init() {
 }
 
 bool launch_attention(const AttnArgs& a, cudaStream_t st) {
-    if (a.n_kv == 0 || a.n_heads % a.n_kv != 0 || a.hd == 0 || a.hd % 2 != 0 || a.n_split == 0) {
+    if (a.n_kv == 0 || a.n_heads % a.n_kv != 0 || a.hd == 0 || a.hd % 2 != 0 || a.n_split == 0 || a.hd > 256) {
         set_error("attention: bad shape heads=%u kv=%u hd=%u", a.n_heads, a.n_kv, a.hd);
         return false;
     }
-    const uint32_t G = a.n_heads / a.n_kv;
-    if (G > kMaxHeadsPerWarp * (kAttnThreads / 32) || a.hd > 32 * kMaxDimPerLane) {
-        set_error("attention: %u query heads per kv head / head_dim %u not supported", G, a.hd);
-        return false;
-    }
-    const size_t hd4 = (a.hd + 3u) & ~3u;
-    // scores need G*kChunk floats; the merge reuses them for G*n_split + G floats
-    const size_t tail = (size_t)G * kChunk > (size_t)G * a.n_split + G ? (size_t)G * kChunk : (size_t)G * a.n_split + G;
-    const size_t smem = ((size_t)G * hd4 + 2 * hd4 + 2 * (size_t)kChunk * a.hd + tail) * sizeof(float);
+    const size_t hp = a.hd + 1;
+    const size_t tail = kChunk + 4 > a.n_split ? kChunk + 4 : a.n_split;
+    const size_t smem = (3 * hp + 2 * (size_t)kChunk * hp + tail) * sizeof(float);
     if (smem > 200 * 1024) { set_error("attention: shared memory %zu too large", smem); return false; }
-    const dim3 grid(a.n_kv, a.n_split);
+    const dim3 grid(a.n_heads, a.n_split);
     if (a.kv_f16) return LM_CUDA(launch_k(attn_decode_kernel<__half>, grid, dim3(kAttnThreads), smem, st, a));
     return LM_CUDA(launch_k(attn_decode_kernel<float>, grid, dim3(kAttnThreads), smem, st, a));
 }

@@ -131,7 +131,7 @@ bool alloc_buffers(llamini_session* s) {
     s->logits = (float*)own(s, (size_t)s->vocab * 4);
     s->part = (float*)own(s, (size_t)s->n_heads * s->n_split * (s->hd + 2) * 4);
     s->trace = (float*)own(s, (size_t)L * s->dim * 4);
-    s->counters = (u32*)own(s, (size_t)s->n_kv * 4);
+    s->counters = (u32*)own(s, (size_t)s->n_heads * 4);
     s->tokens = (u32*)own(s, ((size_t)s->max_seq + 1) * 4);
     const size_t kv_bytes = (size_t)L * s->n_kv * s->max_seq * s->hd * (s->kv_f16 ? 2 : 4);
     s->kc = own(s, kv_bytes);
@@ -142,18 +142,21 @@ bool alloc_buffers(llamini_session* s) {
         return false;
     if (!LM_CUDA(cudaMallocHost((void**)&s->st_host, sizeof(StepState)))) return false;
     memset(s->st_host, 0, sizeof(StepState));
-    return LM_CUDA(cudaMemset(s->counters, 0, (size_t)s->n_kv * 4)) &&
+    return LM_CUDA(cudaMemset(s->counters, 0, (size_t)s->n_heads * 4)) &&
            LM_CUDA(cudaMemset(s->st, 0, sizeof(StepState))) &&
            LM_CUDA(cudaMemset(s->tokens, 0, ((size_t)s->max_seq + 1) * 4)) &&
            LM_CUDA(cudaMemset(s->kc, 0, kv_bytes)) && LM_CUDA(cudaMemset(s->vc, 0, kv_bytes));
 }
 
-u32 choose_splits(u32 n_kv, u32 max_seq) {
-    u32 s = 256 / (n_kv ? n_kv : 1);
+// Position splits per query head: enough CTAs to cover the SMs at long
+// contexts (each split takes >= 64 positions, so short contexts use fewer).
+u32 choose_splits(u32 n_heads, u32 max_seq) {
+    u32 s = (2 * 148 + n_heads - 1) / (n_heads ? n_heads : 1);
     if (s < 1) s = 1;
     if (s > 32) s = 32;
-    if (s > max_seq) s = max_seq;
-    return s;
+    const u32 by_len = (max_seq + 63) / 64;
+    if (s > by_len) s = by_len;
+    return s ? s : 1;
 }
 
 // ---------------------------------------------------------------- the step
@@ -297,7 +300,7 @@ bool finish_build(llamini_session* s) {
     s->theta = upload_f32(s, th.data(), th.size());
     if (!s->theta) return false;
     s->kv_f16 = g_kv_f16 ? 1u : 0u;
-    s->n_split = choose_splits(s->n_kv, s->max_seq);
+    s->n_split = choose_splits(s->n_heads, s->max_seq);
     if (!alloc_buffers(s)) return false;
     if (!capture(s, 1, false, false, &s->g_one)) return false;
     if (!capture(s, kStepsPerGraph, false, false, &s->g_many)) return false;
