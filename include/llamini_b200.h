@@ -67,6 +67,26 @@ int llamini_gemv_host(u32 type, const void* w, u32 rows, u32 cols,
 int llamini_gemv_device(u32 type, const void* d_w, u32 rows, u32 cols,
                         const f32* d_x, u32 batch, f32* d_y);
 
+/* Decode attention for one query position over caller-owned DEVICE buffers,
+ * with no device allocation. No counterpart in the reference: it computes what
+ * causal_mha (model.c:217-260) computes after the cache already holds position
+ * pos (the reference stores k/v first, model.c:222-224). d_q and d_out are
+ * n_heads x head_dim f32; d_key/d_val are f32 caches laid out like KVCache
+ * (row p = position p, n_heads_kv x head_dim) holding rows 0..pos. The work is
+ * enqueued on `stream` (a cudaStream_t; NULL = the legacy default stream) of the
+ * calling thread's current device.
+ * For callers that may not allocate on their path (an engine whose page pool
+ * already holds nearly all of HBM, a loop that cannot take cudaFree's implicit
+ * device synchronisation): split partials and completion counters live in a
+ * fixed 1 MiB (+1 KiB) array in the library's device memory. Limits: n_heads
+ * <= 256, head_dim <= 256; larger requests fail with -1 and a message. The
+ * counters start at zero and every call returns them to zero. The first call
+ * on a device does the set-up (scratch address, kernel attribute) and should
+ * come before any stream capture. Calls that overlap in time on one device
+ * (two streams, or unordered host threads) share the scratch and race. */
+int llamini_causal_mha_noalloc(const f32* d_q, const f32* d_key, const f32* d_val, f32* d_out,
+                               u32 pos, u32 n_heads, u32 n_heads_kv, u32 head_dim, void* stream);
+
 /* ---- device-resident decoding sessions (generate.c:122-167 without host
  *      round trips) --------------------------------------------------------- */
 

@@ -155,6 +155,7 @@ SIGNATURES = {
     "llamini_session_weight_bytes": (u64, [P]),
     "llamini_session_kv_bytes_per_pos": (u64, [P]),
     "llamini_set_kv_f16": (C.c_int, [C.c_int]),
+    "llamini_causal_mha_noalloc": (C.c_int, [P, P, P, P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, P]),
     "llamini_session_trace": (C.c_int, [P, C.c_int]),
     "llamini_session_trace_read": (C.c_int, [P, P]),
 }
