@@ -152,6 +152,7 @@ SIGNATURES = {
     "llamini_session_tokens": (C.c_int, [P, P, u32]),
     "llamini_session_logits": (C.c_int, [P, P]),
     "llamini_session_pos": (u32, [P]),
+    "llamini_session_kernel": (C.c_int, [P]),
     "llamini_session_weight_bytes": (u64, [P]),
     "llamini_session_kv_bytes_per_pos": (u64, [P]),
     "llamini_set_kv_f16": (C.c_int, [C.c_int]),

@@ -136,7 +136,7 @@ struct AttnArgs {
     void* vc;
     uint32_t kv_f16;       // 1: fp16 elements, 0: f32 elements
     float* out;            // [n_heads*hd]
-    float* part;           // [n_heads][n_split][hd + 2] partial results
+    float* part;           // [n_heads][n_split][hd + 4] partial results (m, l, -, -, o[hd])
     uint32_t* counter;     // [n_heads] completion counters (return to 0 after use)
     uint32_t n_heads, n_kv, hd, max_seq, n_split;
     uint32_t rope;         // 0 none, 1 NORM, 2 NEOX
@@ -153,6 +153,65 @@ struct FinishArgs {
     uint32_t nll;          // 1: accumulate -log p(tokens[pos+1])
 };
 bool launch_finish(const FinishArgs& a, cudaStream_t st);
+
+// ---------------------------------------------------------------- persistent decode step
+// One launch runs whole token steps: every CTA (one per SM) works through a
+// fixed list of tasks -- 16-row tiles of the step's matrices and (head, split)
+// pieces of attention -- while its producer warp streams the weight tiles of
+// its upcoming tasks into shared memory. Ops wait for their predecessor through
+// per-op completion counters instead of kernel boundaries (k_decode.cu).
+enum DecKind : uint32_t { DEC_GEMV = 0, DEC_ATTN = 1 };
+constexpr uint32_t kDecNoWait = 0xFFFFFFFFu;   // waits for the previous step's finish
+
+struct DecOp {
+    uint32_t kind = DEC_GEMV;
+    uint32_t ntasks = 0;         // tasks in the schedule
+    uint32_t ndone = 0;          // completions signalled per step (tiles; heads for attention)
+    uint32_t wait = kDecNoWait;  // op whose completion this op needs
+    uint32_t trace_off = 0xFFFFFFFFu;   // residual-add ops that end a layer: offset in the trace buffer
+    uint32_t n_split = 1;        // attention (and x_merge): position splits per head
+    uint32_t x_merge = 0;        // DEC_GEMV: the input is the merge of `at`'s split partials
+    GemvArgs g;                  // DEC_GEMV (segment tile0 filled)
+    AttnArgs at = {};            // DEC_ATTN, and the partials an x_merge op reads
+};
+
+struct DecSync {
+    uint32_t epoch;              // steps finished by earlier launches
+    uint32_t exit_ticket;        // CTAs done with the current launch
+    uint32_t step_done;          // steps finished so far (set by each step's finisher)
+    uint32_t abort;              // set by a CTA whose bounded wait ran out
+};
+
+struct DecArgs {
+    const DecOp* ops = nullptr;
+    uint32_t n_ops = 0;
+    const uint32_t* sched = nullptr;      // CTA c: sched_len[c] entries at sched + c * sched_stride
+    const uint32_t* sched_len = nullptr;  // entry = (op << 16) | task
+    uint32_t sched_stride = 0;
+    uint32_t n_cta = 0;
+    DecSync* sync = nullptr;
+    uint32_t* done = nullptr;             // [n_ops] completions (monotonic)
+    StepState* st = nullptr;
+    uint32_t* tokens = nullptr;
+    uint32_t max_tokens = 0;
+    DevMat tok, pos;                      // embedding tables for the next step's input
+    float emb_scale = 1.f;
+    float* hidden = nullptr;
+    float* trace = nullptr;               // per-layer residual stream, or null
+    uint32_t n_steps = 1;
+    uint32_t ring_bytes = 0;              // weight ring in shared memory
+    uint32_t kmax = 0;                    // largest GEMV input length (multiple of 128)
+    uint32_t hd = 0;                      // attention head size (for the shared-memory plan)
+};
+constexpr uint32_t kDecMaxOps = 1u << 16;
+bool decode_init();
+bool decode_supported_type(uint32_t type);
+// Shared memory for a ring of `ring` bytes, inputs up to kmax and head size hd;
+// 0 when it does not fit.
+size_t decode_smem(uint32_t ring, uint32_t kmax, uint32_t hd);
+uint32_t decode_ring_bytes(uint32_t kmax, uint32_t hd);
+uint32_t decode_tile_alloc(const GemvSeg& G);    // ring bytes of one tile of G
+bool launch_decode(const DecArgs& a, cudaStream_t st);
 
 // Host-pointer op kernels (model.h per-op exports), device buffers in/out.
 bool launch_rms_norm(float* out, const float* x, const float* w, uint32_t dim, float eps, cudaStream_t st);

@@ -11,6 +11,7 @@
 //             generate.h host-pointer entry points.
 #include "internal.h"
 #include "quant.cuh"
+#include "rows.cuh"
 #include "pdl.cuh"
 
 #include <cuda_fp16.h>
@@ -79,39 +80,7 @@ bool launch_dequant(uint32_t type, const uint8_t* raw, uint64_t n, float* out, c
 
 // Decode row `row` of a table (rows of `cols` elements) into out, scaled.
 __device__ void decode_row(const DevMat& m, uint32_t row, float* out, float scale, bool add) {
-    const uint8_t* r = m.ptr + (uint64_t)row * m.row_bytes;
-    if (m.type == T_F32 || m.type == T_F16) {
-        for (uint32_t i = threadIdx.x; i < m.cols; i += blockDim.x) {
-            float v = m.type == T_F32 ? reinterpret_cast<const float*>(r)[i]
-                                      : f16_bits(reinterpret_cast<const unsigned short*>(r)[i]);
-            v = v * scale;
-            out[i] = add ? out[i] + v : v;
-        }
-        return;
-    }
-    const uint32_t units = m.cols / 32;
-    for (uint32_t u = threadIdx.x; u < units; u += blockDim.x) {
-        float y[32];
-        uint32_t blk = 0, v = 0, base = 0;
-#define LM_DEC(T)                                                    \
-        case T: {                                                    \
-            blk = u / Fmt<T>::UPB; v = u % Fmt<T>::UPB;              \
-            Fmt<T>::decode(r + (uint64_t)blk * Fmt<T>::BB, v, y);    \
-            base = blk * Fmt<T>::BE;                                 \
-            for (uint32_t i = 0; i < 32; i++) {                      \
-                float t = y[i] * scale;                              \
-                float* o = out + base + Fmt<T>::elem(v, i);          \
-                *o = add ? *o + t : t;                               \
-            }                                                        \
-            break;                                                   \
-        }
-        switch (m.type) {
-            LM_DEC(T_Q4_0) LM_DEC(T_Q4_1) LM_DEC(T_Q5_0) LM_DEC(T_Q8_0)
-            LM_DEC(T_Q4_K) LM_DEC(T_Q5_K) LM_DEC(T_Q6_K)
-            default: break;
-        }
-#undef LM_DEC
-    }
+    decode_row_part(m, row, out, scale, add, threadIdx.x, blockDim.x);
 }
 
 __global__ void embed_kernel(const EmbedArgs a) {
@@ -387,6 +356,7 @@ bool launch_mha_f32(const float* q, float* kc, float* vc, float* out, uint32_t p
 bool gemv_init();
 bool gemv_mma_init();
 bool attn_init();
+bool decode_init();
 
 // Per-kernel attributes, set once when the device is selected (never during a
 // graph capture).
@@ -394,7 +364,7 @@ bool kernels_init() {
     // one shared-memory carveout for every kernel of the step, so consecutive
     // kernels never wait for an SM to reconfigure its L1 / shared split
     const int carve = cudaFuncAttributePreferredSharedMemoryCarveout;
-    return gemv_init() && gemv_mma_init() && attn_init() &&
+    return gemv_init() && gemv_mma_init() && attn_init() && decode_init() &&
            LM_CUDA(cudaFuncSetAttribute(embed_kernel, (cudaFuncAttribute)carve, 100)) &&
            LM_CUDA(cudaFuncSetAttribute(finish_kernel, (cudaFuncAttribute)carve, 100)) &&
            LM_CUDA(cudaFuncSetAttribute(copy_kernel, (cudaFuncAttribute)carve, 100)) &&

@@ -63,6 +63,12 @@ struct llamini_session {
     cudaGraphExec_t g_one = nullptr, g_many = nullptr, g_trace = nullptr, g_nll = nullptr;
     bool trace_on = false;
 
+    // persistent decode kernel (k_decode.cu): op table, schedule and counters
+    bool dec_on = false;
+    lm::DecArgs dec;
+    u32* dec_counters = nullptr;          // DecSync | done[n_ops] | tickets[n_layers][n_heads]
+    size_t dec_counter_bytes = 0;
+
     // host mirror of the device position / prompt length
     u32 pos = 0, n_prompt = 0;
 };
@@ -71,6 +77,7 @@ namespace lm {
 namespace {
 
 constexpr u32 kStepsPerGraph = 8;
+constexpr u32 kDecStepsPerLaunch = 64;    // decode-kernel steps per launch
 std::vector<llamini_session*> g_sessions;
 
 void* own(llamini_session* s, size_t bytes) {
@@ -129,7 +136,7 @@ bool alloc_buffers(llamini_session* s) {
     s->attn = (float*)own(s, (size_t)s->qd * 4);
     s->ffn_h = (float*)own(s, (size_t)s->ffn * 4);
     s->logits = (float*)own(s, (size_t)s->vocab * 4);
-    s->part = (float*)own(s, (size_t)s->n_heads * s->n_split * (s->hd + 2) * 4);
+    s->part = (float*)own(s, (size_t)s->n_heads * s->n_split * (s->hd + 4) * 4);
     s->trace = (float*)own(s, (size_t)L * s->dim * 4);
     s->counters = (u32*)own(s, (size_t)s->n_heads * 4);
     s->tokens = (u32*)own(s, ((size_t)s->max_seq + 1) * 4);
@@ -148,10 +155,12 @@ bool alloc_buffers(llamini_session* s) {
            LM_CUDA(cudaMemset(s->kc, 0, kv_bytes)) && LM_CUDA(cudaMemset(s->vc, 0, kv_bytes));
 }
 
-// Position splits per query head: enough CTAs to cover the SMs at long
-// contexts (each split takes >= 64 positions, so short contexts use fewer).
+// Position splits per query head: at most one (head, split) task per SM, so
+// the decode kernel runs its attention in one wave (each split takes >= 64
+// positions, so short contexts use fewer).
 u32 choose_splits(u32 n_heads, u32 max_seq) {
-    u32 s = (2 * 148 + n_heads - 1) / (n_heads ? n_heads : 1);
+    const u32 sms = (u32)sm_count();
+    u32 s = n_heads ? sms / n_heads : 1;
     if (s < 1) s = 1;
     if (s > 32) s = 32;
     const u32 by_len = (max_seq + 63) / 64;
@@ -161,7 +170,10 @@ u32 choose_splits(u32 n_heads, u32 max_seq) {
 
 // ---------------------------------------------------------------- the step
 
-bool enqueue_step(llamini_session* s, cudaStream_t st, bool trace, bool nll) {
+// ---- the arguments of each op of a step (shared by the per-op launches and
+//      the persistent decode kernel)
+
+EmbedArgs embed_args(llamini_session* s) {
     EmbedArgs e;
     e.st = s->st;
     e.tokens = s->tokens;
@@ -170,82 +182,102 @@ bool enqueue_step(llamini_session* s, cudaStream_t st, bool trace, bool nll) {
     e.scale = s->emb_scale;
     e.hidden = s->hidden;
     e.dim = s->dim;
-    if (!launch_embed(e, st)) return false;
+    return e;
+}
+
+// norm + QKV (LLaMA: three matrices; GPT-2: the fused qkv matrix)
+GemvArgs qkv_args(llamini_session* s, u32 l) {
+    const llamini_session::Layer& W = s->layers[l];
     const bool gpt2 = s->kind == 1;
-    for (u32 l = 0; l < s->n_layers; l++) {
-        const llamini_session::Layer& W = s->layers[l];
-        // norm + QKV
-        GemvArgs a;
-        a.err = &s->st->err;
-        a.x = s->hidden;
-        a.K = s->dim;
-        a.norm = gpt2 ? NORM_LAYER : NORM_RMS;
-        a.norm_w = W.n1w;
-        a.norm_b = W.n1b;
-        a.eps = s->eps;
-        if (gpt2) {
-            a.nseg = 1;
-            a.seg[0] = {W.q.ptr, nullptr, W.q.row_bytes, 0, W.q.type, 0, W.q.rows, EPI_STORE, s->qkv, W.bq, 0, 0};
-        } else {
-            a.nseg = 3;
-            a.seg[0] = {W.q.ptr, nullptr, W.q.row_bytes, 0, W.q.type, 0, W.q.rows, EPI_STORE, s->qkv, W.bq, 0, 0};
-            a.seg[1] = {W.k.ptr, nullptr, W.k.row_bytes, 0, W.k.type, 0, W.k.rows, EPI_STORE, s->qkv + s->qd, W.bk, 0, 0};
-            a.seg[2] = {W.v.ptr, nullptr, W.v.row_bytes, 0, W.v.type, 0, W.v.rows, EPI_STORE, s->qkv + s->qd + s->kvd, W.bv, 0, 0};
-        }
-        if (!launch_gemv(a, st)) return false;
-        // attention
-        AttnArgs at;
-        at.st = s->st;
-        at.qkv = s->qkv;
-        const size_t per_layer = (size_t)s->n_kv * s->max_seq * s->hd * (s->kv_f16 ? 2 : 4);
-        at.kc = (uint8_t*)s->kc + l * per_layer;
-        at.vc = (uint8_t*)s->vc + l * per_layer;
-        at.kv_f16 = s->kv_f16;
-        at.out = s->attn;
-        at.part = s->part;
-        at.counter = s->counters;
-        at.n_heads = s->n_heads;
-        at.n_kv = s->n_kv;
-        at.hd = s->hd;
-        at.max_seq = s->max_seq;
-        at.n_split = s->n_split;
-        at.rope = s->rope_mode;
-        at.theta = s->theta;
-        if (!launch_attention(at, st)) return false;
-        // O projection + residual
-        GemvArgs o;
-        o.err = &s->st->err;
-        o.x = s->attn;
-        o.K = s->qd;
-        o.nseg = 1;
-        o.seg[0] = {W.o.ptr, nullptr, W.o.row_bytes, 0, W.o.type, 0, W.o.rows, EPI_RESID, s->hidden, W.bo, 0, 0};
-        if (!launch_gemv(o, st)) return false;
-        // norm + FFN up (gated for LLaMA, GELU for GPT-2)
-        GemvArgs f;
-        f.err = &s->st->err;
-        f.x = s->hidden;
-        f.K = s->dim;
-        f.norm = gpt2 ? NORM_LAYER : NORM_RMS;
-        f.norm_w = W.n2w;
-        f.norm_b = W.n2b;
-        f.eps = s->eps;
-        f.nseg = 1;
-        if (gpt2)
-            f.seg[0] = {W.up.ptr, nullptr, W.up.row_bytes, 0, W.up.type, 0, W.up.rows, EPI_GELU, s->ffn_h, W.bup, 0, 0};
-        else
-            f.seg[0] = {W.gate.ptr, W.up.ptr, W.gate.row_bytes, W.up.row_bytes, W.gate.type, W.up.type, W.gate.rows,
-                        s->act_gelu ? (u32)EPI_GLU_GELU : (u32)EPI_GLU_SILU, s->ffn_h, nullptr, 0, 0};
-        if (!launch_gemv(f, st)) return false;
-        // down + residual
-        GemvArgs d;
-        d.err = &s->st->err;
-        d.x = s->ffn_h;
-        d.K = s->ffn;
-        d.nseg = 1;
-        d.seg[0] = {W.down.ptr, nullptr, W.down.row_bytes, 0, W.down.type, 0, W.down.rows, EPI_RESID, s->hidden, W.bdown, 0, 0};
-        if (!launch_gemv(d, st)) return false;
-        if (trace && !launch_copy_f32(s->trace + (size_t)l * s->dim, s->hidden, s->dim, st)) return false;
+    GemvArgs a;
+    a.err = &s->st->err;
+    a.x = s->hidden;
+    a.K = s->dim;
+    a.norm = gpt2 ? NORM_LAYER : NORM_RMS;
+    a.norm_w = W.n1w;
+    a.norm_b = W.n1b;
+    a.eps = s->eps;
+    if (gpt2) {
+        a.nseg = 1;
+        a.seg[0] = {W.q.ptr, nullptr, W.q.row_bytes, 0, W.q.type, 0, W.q.rows, EPI_STORE, s->qkv, W.bq, 0, 0};
+    } else {
+        a.nseg = 3;
+        a.seg[0] = {W.q.ptr, nullptr, W.q.row_bytes, 0, W.q.type, 0, W.q.rows, EPI_STORE, s->qkv, W.bq, 0, 0};
+        a.seg[1] = {W.k.ptr, nullptr, W.k.row_bytes, 0, W.k.type, 0, W.k.rows, EPI_STORE, s->qkv + s->qd, W.bk, 0, 0};
+        a.seg[2] = {W.v.ptr, nullptr, W.v.row_bytes, 0, W.v.type, 0, W.v.rows, EPI_STORE, s->qkv + s->qd + s->kvd, W.bv, 0, 0};
     }
+    return a;
+}
+
+AttnArgs attn_args(llamini_session* s, u32 l) {
+    AttnArgs at;
+    at.st = s->st;
+    at.qkv = s->qkv;
+    const size_t per_layer = (size_t)s->n_kv * s->max_seq * s->hd * (s->kv_f16 ? 2 : 4);
+    at.kc = (uint8_t*)s->kc + l * per_layer;
+    at.vc = (uint8_t*)s->vc + l * per_layer;
+    at.kv_f16 = s->kv_f16;
+    at.out = s->attn;
+    at.part = s->part;
+    at.counter = s->counters;
+    at.n_heads = s->n_heads;
+    at.n_kv = s->n_kv;
+    at.hd = s->hd;
+    at.max_seq = s->max_seq;
+    at.n_split = s->n_split;
+    at.rope = s->rope_mode;
+    at.theta = s->theta;
+    return at;
+}
+
+// O projection + residual
+GemvArgs o_args(llamini_session* s, u32 l) {
+    const llamini_session::Layer& W = s->layers[l];
+    GemvArgs o;
+    o.err = &s->st->err;
+    o.x = s->attn;
+    o.K = s->qd;
+    o.nseg = 1;
+    o.seg[0] = {W.o.ptr, nullptr, W.o.row_bytes, 0, W.o.type, 0, W.o.rows, EPI_RESID, s->hidden, W.bo, 0, 0};
+    return o;
+}
+
+// norm + FFN up (gated for LLaMA, GELU for GPT-2)
+GemvArgs ffn_args(llamini_session* s, u32 l) {
+    const llamini_session::Layer& W = s->layers[l];
+    const bool gpt2 = s->kind == 1;
+    GemvArgs f;
+    f.err = &s->st->err;
+    f.x = s->hidden;
+    f.K = s->dim;
+    f.norm = gpt2 ? NORM_LAYER : NORM_RMS;
+    f.norm_w = W.n2w;
+    f.norm_b = W.n2b;
+    f.eps = s->eps;
+    f.nseg = 1;
+    if (gpt2)
+        f.seg[0] = {W.up.ptr, nullptr, W.up.row_bytes, 0, W.up.type, 0, W.up.rows, EPI_GELU, s->ffn_h, W.bup, 0, 0};
+    else
+        f.seg[0] = {W.gate.ptr, W.up.ptr, W.gate.row_bytes, W.up.row_bytes, W.gate.type, W.up.type, W.gate.rows,
+                    s->act_gelu ? (u32)EPI_GLU_GELU : (u32)EPI_GLU_SILU, s->ffn_h, nullptr, 0, 0};
+    return f;
+}
+
+// down + residual
+GemvArgs down_args(llamini_session* s, u32 l) {
+    const llamini_session::Layer& W = s->layers[l];
+    GemvArgs d;
+    d.err = &s->st->err;
+    d.x = s->ffn_h;
+    d.K = s->ffn;
+    d.nseg = 1;
+    d.seg[0] = {W.down.ptr, nullptr, W.down.row_bytes, 0, W.down.type, 0, W.down.rows, EPI_RESID, s->hidden, W.bdown, 0, 0};
+    return d;
+}
+
+// final norm + lm_head + argmax
+GemvArgs head_args(llamini_session* s) {
+    const bool gpt2 = s->kind == 1;
     GemvArgs h;
     h.err = &s->st->err;
     h.x = s->hidden;
@@ -257,7 +289,20 @@ bool enqueue_step(llamini_session* s, cudaStream_t st, bool trace, bool nll) {
     h.nseg = 1;
     h.seg[0] = {s->head.ptr, nullptr, s->head.row_bytes, 0, s->head.type, 0, s->head.rows, EPI_STORE, s->logits, nullptr, 0, 1};
     h.argmax_key = &s->st->argmax_key;
-    if (!launch_gemv(h, st)) return false;
+    return h;
+}
+
+bool enqueue_step(llamini_session* s, cudaStream_t st, bool trace, bool nll) {
+    if (!launch_embed(embed_args(s), st)) return false;
+    for (u32 l = 0; l < s->n_layers; l++) {
+        if (!launch_gemv(qkv_args(s, l), st)) return false;
+        if (!launch_attention(attn_args(s, l), st)) return false;
+        if (!launch_gemv(o_args(s, l), st)) return false;
+        if (!launch_gemv(ffn_args(s, l), st)) return false;
+        if (!launch_gemv(down_args(s, l), st)) return false;
+        if (trace && !launch_copy_f32(s->trace + (size_t)l * s->dim, s->hidden, s->dim, st)) return false;
+    }
+    if (!launch_gemv(head_args(s), st)) return false;
     FinishArgs fa;
     fa.st = s->st;
     fa.tokens = s->tokens;
@@ -293,6 +338,134 @@ void destroy(llamini_session* s) {
 
 bool g_kv_f16 = false;
 
+// Op table and per-CTA schedule of the persistent decode kernel. Returns true
+// with dec_on = false when the model has a matrix format or shape the kernel
+// does not take (the per-op graphs run those models), or when
+// LLAMINI_DECODE_KERNEL=0.
+bool build_decode(llamini_session* s) {
+    s->dec_on = false;
+    const char* env = getenv("LLAMINI_DECODE_KERNEL");
+    if (env && env[0] == '0') return true;
+    if (s->hd > 256 || s->hd == 0 || s->hd % 4 != 0 || s->n_split > 32) return true;
+    if ((size_t)s->n_heads * (s->n_split + 1) > 1024) return true;      // merge weights in shared memory
+    std::vector<DecOp> ops;
+    u32 kmax = 0;
+    bool ok = true;
+    auto add_gemv = [&](GemvArgs g, u32 trace_off) {
+        DecOp op;
+        op.kind = DEC_GEMV;
+        u32 tiles = 0;
+        for (u32 i = 0; i < g.nseg; i++) {
+            GemvSeg& G = g.seg[i];
+            const bool glu = G.epi == EPI_GLU_SILU || G.epi == EPI_GLU_GELU;
+            if (!decode_supported_type(G.type) || (glu && G.type2 != G.type)) ok = false;
+            if (reinterpret_cast<uintptr_t>(G.w) % 16 != 0 || (glu && reinterpret_cast<uintptr_t>(G.w2) % 16 != 0))
+                ok = false;
+            G.tile0 = tiles;
+            tiles += (G.rows + 15) / 16;
+        }
+        if (g.K % 32 != 0 || reinterpret_cast<uintptr_t>(g.x) % 16 != 0) ok = false;
+        const u32 kr = (g.K + 127) & ~127u;
+        kmax = kmax > kr ? kmax : kr;
+        op.g = g;
+        op.ntasks = op.ndone = tiles;
+        op.trace_off = trace_off;
+        op.wait = ops.empty() ? kDecNoWait : (u32)ops.size() - 1;
+        ops.push_back(op);
+    };
+    const u32 L = s->n_layers;
+    const size_t n_ops = (size_t)L * 5 + 1;
+    const size_t counter_words = 4 + n_ops;
+    s->dec_counters = (u32*)own(s, counter_words * 4);
+    if (!s->dec_counters) return false;
+    s->dec_counter_bytes = counter_words * 4;
+    for (u32 l = 0; l < L && ok; l++) {
+        add_gemv(qkv_args(s, l), 0xFFFFFFFFu);
+        // attention: one task per (head, split), each leaving a partial
+        DecOp at;
+        at.kind = DEC_ATTN;
+        at.at = attn_args(s, l);
+        at.at.counter = nullptr;
+        at.n_split = s->n_split;
+        at.ntasks = at.ndone = s->n_heads * s->n_split;
+        at.wait = (u32)ops.size() - 1;
+        ops.push_back(at);
+        // the O projection merges the partials while staging its input
+        add_gemv(o_args(s, l), 0xFFFFFFFFu);
+        ops.back().x_merge = 1;
+        ops.back().at = at.at;
+        ops.back().n_split = s->n_split;
+        add_gemv(ffn_args(s, l), 0xFFFFFFFFu);
+        add_gemv(down_args(s, l), l * s->dim);
+    }
+    if (ok) add_gemv(head_args(s), 0xFFFFFFFFu);
+    if (!ok || ops.size() != n_ops || n_ops >= kDecMaxOps) return true;
+    // shared memory: the ring must hold at least two of the largest tiles
+    const u32 ring = decode_ring_bytes(kmax, s->hd);
+    u32 max_tile = 0;
+    for (const DecOp& op : ops)
+        if (op.kind == DEC_GEMV)
+            for (u32 i = 0; i < op.g.nseg; i++) {
+                const u32 t = decode_tile_alloc(op.g.seg[i]);
+                max_tile = max_tile > t ? max_tile : t;
+            }
+    if (ring == 0 || 2 * (u64)max_tile > ring) return true;
+    for (const DecOp& op : ops)
+        if (op.ntasks > 0xFFFFu) return true;
+    // schedule: the tasks of each op in turn, dealt round-robin over the CTAs
+    // with the dealing position carried from op to op, so every CTA gets an
+    // equal share of the step's tiles
+    const u32 n_cta = (u32)sm_count();
+    std::vector<std::vector<u32>> per(n_cta);
+    u32 cursor = 0;
+    for (u32 i = 0; i < (u32)ops.size(); i++)
+        for (u32 t = 0; t < ops[i].ntasks; t++) {
+            per[cursor].push_back((i << 16) | t);
+            cursor = (cursor + 1) % n_cta;
+        }
+    u32 stride = 1;
+    for (auto& v : per) stride = stride > v.size() ? stride : (u32)v.size();
+    std::vector<u32> sched((size_t)n_cta * stride, 0u), len(n_cta);
+    for (u32 c = 0; c < n_cta; c++) {
+        len[c] = (u32)per[c].size();
+        for (size_t k = 0; k < per[c].size(); k++) sched[(size_t)c * stride + k] = per[c][k];
+    }
+    DecOp* d_ops = (DecOp*)own(s, ops.size() * sizeof(DecOp));
+    u32* d_sched = (u32*)own(s, sched.size() * 4);
+    u32* d_len = (u32*)own(s, len.size() * 4);
+    if (!d_ops || !d_sched || !d_len) return false;
+    if (!LM_CUDA(cudaMemcpy(d_ops, ops.data(), ops.size() * sizeof(DecOp), cudaMemcpyHostToDevice)) ||
+        !LM_CUDA(cudaMemcpy(d_sched, sched.data(), sched.size() * 4, cudaMemcpyHostToDevice)) ||
+        !LM_CUDA(cudaMemcpy(d_len, len.data(), len.size() * 4, cudaMemcpyHostToDevice)) ||
+        !LM_CUDA(cudaMemset(s->dec_counters, 0, s->dec_counter_bytes)))
+        return false;
+    DecArgs& a = s->dec;
+    a.ops = d_ops;
+    a.n_ops = (u32)ops.size();
+    a.sched = d_sched;
+    a.sched_len = d_len;
+    a.sched_stride = stride;
+    a.n_cta = n_cta;
+    a.sync = reinterpret_cast<DecSync*>(s->dec_counters);
+    a.done = s->dec_counters + 4;
+    a.st = s->st;
+    a.tokens = s->tokens;
+    a.max_tokens = s->max_seq + 1;
+    a.tok = s->tok;
+    a.pos = s->pos_tab;
+    a.emb_scale = s->emb_scale;
+    a.hidden = s->hidden;
+    a.trace = nullptr;
+    a.n_steps = 1;
+    a.ring_bytes = ring;
+    a.kmax = kmax;
+    a.hd = s->hd;
+    s->dec_on = true;
+    return true;
+}
+
+
+
 bool finish_build(llamini_session* s) {
     // theta_j = base^(-2j/hd), evaluated exactly as model.c:38 / model.c:50 do
     std::vector<f32> th(s->hd / 2 ? s->hd / 2 : 1);
@@ -304,7 +477,7 @@ bool finish_build(llamini_session* s) {
     if (!alloc_buffers(s)) return false;
     if (!capture(s, 1, false, false, &s->g_one)) return false;
     if (!capture(s, kStepsPerGraph, false, false, &s->g_many)) return false;
-    return true;
+    return build_decode(s);
 }
 
 llamini_session* find(const void* model, KVCache* caches) {
@@ -427,6 +600,7 @@ bool write_state(llamini_session* s, u32 pos, u32 n_prompt, bool reset_nll) {
     s->st_host->nll_count = 0;
     const size_t n = reset_nll ? sizeof(StepState) : offsetof(StepState, nll);
     if (!LM_CUDA(cudaMemcpyAsync(s->st, s->st_host, n, cudaMemcpyHostToDevice, st))) return false;
+    if (s->dec_on && !LM_CUDA(cudaMemsetAsync(s->dec_counters, 0, s->dec_counter_bytes, st))) return false;
     s->pos = pos;
     s->n_prompt = n_prompt;
     return true;
@@ -438,6 +612,20 @@ bool run_steps(llamini_session* s, u32 n) {
         return false;
     }
     cudaStream_t st = stream();
+    if (s->dec_on && n > 0) {
+        // the kernel embeds the input of each following step itself; the first
+        // step's input is embedded here
+        if (!launch_embed(embed_args(s), st)) return false;
+        DecArgs a = s->dec;
+        a.trace = s->trace_on ? s->trace : nullptr;
+        for (u32 left = n; left > 0;) {
+            a.n_steps = left < kDecStepsPerLaunch ? left : kDecStepsPerLaunch;
+            if (!launch_decode(a, st)) return false;
+            left -= a.n_steps;
+        }
+        s->pos += n;
+        return true;
+    }
     if (s->trace_on) {
         if (!s->g_trace && !capture(s, 1, true, false, &s->g_trace)) return false;
         for (u32 i = 0; i < n; i++) if (!LM_CUDA(cudaGraphLaunch(s->g_trace, st))) return false;
@@ -668,6 +856,7 @@ int llamini_session_logits(llamini_session* s, f32* out) {
 }
 
 u32 llamini_session_pos(llamini_session* s) { return s ? s->pos : 0; }
+int llamini_session_kernel(llamini_session* s) { return s ? (s->dec_on ? 1 : 0) : -1; }
 u64 llamini_session_weight_bytes(llamini_session* s) { return s ? s->weight_bytes : 0; }
 u64 llamini_session_kv_bytes_per_pos(llamini_session* s) {
     return s ? (u64)s->n_layers * 2 * s->n_kv * s->hd * (s->kv_f16 ? 2 : 4) : 0;
