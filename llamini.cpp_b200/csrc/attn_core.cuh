@@ -276,6 +276,55 @@ __device__ __forceinline__ float4 merged_value4(const float* src, uint32_t ns, u
     }
     return make_float4(acc.x / Ls, acc.y / Ls, acc.z / Ls, acc.w / Ls);
 }
+// merged_value4 with the weights computed in place (same operations in the
+// same order as merge_weights + merged_value4); for ns <= 4 every load is
+// issued before the first use, so the merge costs one round trip to L2.
+__device__ __forceinline__ float4 merge_head4(const float* src, uint32_t ns, uint32_t stride, uint32_t d) {
+    if (ns <= 4) {
+        float2 ml[4];
+        float4 v[4];
+#pragma unroll
+        for (uint32_t s = 0; s < 4; s++) {
+            if (s < ns) {
+                ml[s] = __ldcg(reinterpret_cast<const float2*>(src + s * stride));
+                v[s] = __ldcg(reinterpret_cast<const float4*>(src + s * stride + 4 + d));
+            }
+        }
+        float M = -INFINITY;
+#pragma unroll
+        for (uint32_t s = 0; s < 4; s++)
+            if (s < ns) M = fmaxf(M, ml[s].x);
+        float Ls = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (uint32_t s = 0; s < 4; s++) {
+            if (s < ns) {
+                const float ws = expf(ml[s].x - M);
+                Ls = fmaf(ws, ml[s].y, Ls);
+                acc.x = fmaf(v[s].x, ws, acc.x);
+                acc.y = fmaf(v[s].y, ws, acc.y);
+                acc.z = fmaf(v[s].z, ws, acc.z);
+                acc.w = fmaf(v[s].w, ws, acc.w);
+            }
+        }
+        return make_float4(acc.x / Ls, acc.y / Ls, acc.z / Ls, acc.w / Ls);
+    }
+    float M = -INFINITY;
+    for (uint32_t s = 0; s < ns; s++) M = fmaxf(M, __ldcg(src + s * stride));
+    float Ls = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (uint32_t s = 0; s < ns; s++) {
+        const float2 ml = __ldcg(reinterpret_cast<const float2*>(src + s * stride));
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(src + s * stride + 4 + d));
+        const float ws = expf(ml.x - M);
+        Ls = fmaf(ws, ml.y, Ls);
+        acc.x = fmaf(v.x, ws, acc.x);
+        acc.y = fmaf(v.y, ws, acc.y);
+        acc.z = fmaf(v.z, ws, acc.z);
+        acc.w = fmaf(v.w, ws, acc.w);
+    }
+    return make_float4(acc.x / Ls, acc.y / Ls, acc.z / Ls, acc.w / Ls);
+}
 // The same merge for a single split held in registers.
 __device__ __forceinline__ float merged_single(float o, float m, float l) {
     const float M = fmaxf(-INFINITY, m);

@@ -204,6 +204,8 @@ struct DecArgs {
     uint32_t hd = 0;                      // attention head size (for the shared-memory plan)
 };
 constexpr uint32_t kDecMaxOps = 1u << 16;
+constexpr uint32_t kDecMaxOpsSmem = 256;      // ops of one step (per-op tables live in shared memory)
+constexpr uint32_t kDecMaxTasks = 512;        // tasks of one CTA per step (its list lives in shared memory)
 bool decode_init();
 bool decode_supported_type(uint32_t type);
 // Shared memory for a ring of `ring` bytes, inputs up to kmax and head size hd;

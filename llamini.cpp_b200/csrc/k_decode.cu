@@ -43,10 +43,14 @@ constexpr uint32_t kDCons = kDWarps * 32;           // consumer threads (named b
 constexpr uint32_t kDThreads = kDCons + 32;         // + the producer warp
 constexpr uint32_t kQ = 16;                         // queued weight tiles per CTA (one mbarrier each)
 constexpr uint64_t kWaitNs = 2000000000ull;         // longest wait on a counter, ring slot or copy (2 s)
-constexpr uint32_t kMergeFloats = 1024;             // merge weights of an x_merge op: n_heads * (splits + 1)
-constexpr size_t kDecSmem = 220 * 1024;             // dynamic shared memory per CTA
+constexpr size_t kDecSmem = 218 * 1024;             // dynamic shared memory per CTA
 
 struct DecShared {
+    DecOp op;                // the consumers' current op (copied from global memory)
+    uint32_t tasks[kDecMaxTasks];        // this CTA's task list
+    uint32_t wait_ctr[kDecMaxOpsSmem];   // per op: counter index it waits on (kDecNoWait: step start)
+    uint32_t wait_n[kDecMaxOpsSmem];     // per op: completions per step of that counter
+    uint8_t kind[kDecMaxOpsSmem];        // per op: DEC_GEMV or DEC_ATTN
     uint64_t bar[kQ];
     uint64_t vend[kQ];       // producer only: virtual ring end of each queued tile
     uint32_t off[kQ];        // ring offset of each queued tile
@@ -135,15 +139,13 @@ __host__ __device__ __forceinline__ uint32_t stage_floats(uint32_t kmax, uint32_
     const uint32_t a = xs_floats(kmax), b = attn_floats(hd);
     return ((a > b ? a : b) + 3) & ~3u;
 }
-constexpr uint32_t kTailFloats = 2 * kDWarps + kDWarps * 16 + kMergeFloats;   // red, part, merge weights
-
-__host__ __device__ __forceinline__ uint32_t align16(uint64_t v) { return (uint32_t)((v + 15) & ~uint64_t(15)); }
+constexpr uint32_t kTailFloats = 2 * kDWarps + kDWarps * 16;   // red + part
 
 // Ring bytes of a tile (always sized for 16 rows so reads past a short last
 // tile stay inside its own allocation; 16 bytes of slack for the word reads).
 __host__ __device__ __forceinline__ uint32_t tile_alloc(const GemvSeg& G) {
     const bool glu = G.epi == EPI_GLU_SILU || G.epi == EPI_GLU_GELU;
-    const uint32_t body = glu ? align16(16 * G.row_bytes) + align16(16 * G.row_bytes2) : align16(16 * G.row_bytes);
+    const uint32_t body = glu ? up_offset(G) + tile_bytes(G.row_bytes2) : tile_bytes(G.row_bytes);
     return (body + 16 + 127) & ~127u;
 }
 
@@ -165,8 +167,7 @@ __device__ void dsum_max(float& s, float& m, float* red, uint32_t tid) {
     m = tm;
 }
 
-__device__ void stage_x_dec(const DecArgs& da, const DecOp& op, const MmaSmem& sm, float* mw, float* s_scale,
-                            uint32_t tid) {
+__device__ void stage_x_dec(const DecArgs& da, const DecOp& op, const MmaSmem& sm, float* s_scale, uint32_t tid) {
     const GemvArgs& a = op.g;
     const uint32_t K = a.K, n4 = K / 4;
     const float4* x4 = reinterpret_cast<const float4*>(a.x);
@@ -178,13 +179,9 @@ __device__ void stage_x_dec(const DecArgs& da, const DecOp& op, const MmaSmem& s
         const AttnArgs& at = op.at;
         const uint32_t NS = op.n_split, hd = at.hd, stride = attn_part_stride(hd);
         const uint32_t ns = split_range(vload(&da.st->pos), NS, 0).ns;
-        float* ls = mw + at.n_heads * NS;
-        for (uint32_t h = tid; h < at.n_heads; h += kDCons)
-            ls[h] = merge_weights(at.part + (uint64_t)h * NS * stride, ns, stride, mw + h * NS);
-        csync();
         for (uint32_t i = tid; i < n4; i += kDCons) {
             const uint32_t h = (4 * i) / hd, d = 4 * i - h * hd;
-            const float4 v = merged_value4(at.part + (uint64_t)h * NS * stride, ns, stride, mw + h * NS, ls[h], d);
+            const float4 v = merge_head4(at.part + (uint64_t)h * NS * stride, ns, stride, d);
             m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
             xf4[i] = v;
         }
@@ -293,8 +290,14 @@ __device__ void gemv_tile(const DecArgs& a, const DecOp& op, uint32_t t, const u
     const uint32_t half = kDWarps / 2;
     const bool up = glu && warp >= half;
     const uint8_t* base = up ? buf + up_offset(G) : buf;
-    const uint64_t rb = up ? G.row_bytes2 : G.row_bytes;
+    const uint64_t rb = smem_rs(up ? G.row_bytes2 : G.row_bytes);
     const uint32_t first = glu ? warp % half : warp, step = glu ? half : kDWarps;
+    // epilogue inputs from global memory, loaded before the MMA loop
+    float res = 0.f, bias = 0.f;
+    if (tid < 16 && tid < tr.nrows) {
+        if (G.epi == EPI_RESID) res = __ldcg(G.out + tr.row0 + tid);
+        if (G.bias) bias = G.bias[tr.row0 + tid];
+    }
     float acc[2] = {0.f, 0.f};
     switch (G.type) {
     case T_Q4_K: tile_rows<FQ4K>(base, rb, g.K, L, first, step, sm, acc); break;
@@ -326,17 +329,17 @@ __device__ void gemv_tile(const DecArgs& a, const DecOp& op, uint32_t t, const u
         u *= S.scale;
         if (r < tr.nrows) {
             switch (G.epi) {
-            case EPI_STORE: if (G.bias) v += G.bias[row]; G.out[row] = v; break;
+            case EPI_STORE: if (G.bias) v += bias; G.out[row] = v; break;
             case EPI_RESID: {
-                if (G.bias) v += G.bias[row];
-                const float o = __ldcg(G.out + row) + v;
+                if (G.bias) v += bias;
+                const float o = res + v;
                 G.out[row] = o;
                 if (a.trace != nullptr && op.trace_off != 0xFFFFFFFFu) a.trace[op.trace_off + row] = o;
                 break;
             }
             case EPI_GLU_SILU: v = v / (1.0f + expf(-v)) * u; G.out[row] = v; break;   // model.c:22
             case EPI_GLU_GELU: v = m_gelu(v) * u; G.out[row] = v; break;
-            case EPI_GELU: if (G.bias) v += G.bias[row]; v = m_gelu(v); G.out[row] = v; break;
+            case EPI_GELU: if (G.bias) v += bias; v = m_gelu(v); G.out[row] = v; break;
             }
             if (G.argmax) key = m_key(v, row);
         }
@@ -460,7 +463,7 @@ __device__ void finish_step(const DecArgs& a, DecShared& S, uint32_t tid) {
 // ------------------------------------------------------------------ roles
 
 __device__ void producer(const DecArgs& a, DecShared& S, uint8_t* ring) {
-    const uint32_t* my = a.sched + (uint64_t)blockIdx.x * a.sched_stride;
+    const uint32_t* my = S.tasks;
     const uint32_t n_my = a.sched_len[blockIdx.x];
     const uint64_t R = a.ring_bytes;
     uint64_t head = 0;
@@ -473,8 +476,8 @@ __device__ void producer(const DecArgs& a, DecShared& S, uint8_t* ring) {
             const TileRef tr = tile_of(op.g, ent & 0xFFFFu);
             const GemvSeg& G = op.g.seg[tr.seg];
             const bool glu = G.epi == EPI_GLU_SILU || G.epi == EPI_GLU_GELU;
-            const uint32_t n1 = align16((uint64_t)tr.nrows * G.row_bytes);
-            const uint32_t n2 = glu ? align16((uint64_t)tr.nrows * G.row_bytes2) : 0u;
+            const uint32_t n1 = rows_tx(G.row_bytes, tr.nrows);
+            const uint32_t n2 = glu ? rows_tx(G.row_bytes2, tr.nrows) : 0u;
             const uint32_t alloc = tile_alloc(G);
             uint64_t off = head % R;
             if (off + alloc > R) { head += R - off; off = 0; }
@@ -498,8 +501,9 @@ __device__ void producer(const DecArgs& a, DecShared& S, uint8_t* ring) {
             // released it; order them before the async-proxy writes
             asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
             mbar_expect_tx(&S.bar[q], n1 + n2);
-            bulk_g2s(ring + off, G.w + (uint64_t)tr.row0 * G.row_bytes, n1, &S.bar[q]);
-            if (glu) bulk_g2s(ring + off + up_offset(G), G.w2 + (uint64_t)tr.row0 * G.row_bytes2, n2, &S.bar[q]);
+            copy_rows(ring + off, G.w + (uint64_t)tr.row0 * G.row_bytes, G.row_bytes, tr.nrows, &S.bar[q]);
+            if (glu) copy_rows(ring + off + up_offset(G), G.w2 + (uint64_t)tr.row0 * G.row_bytes2, G.row_bytes2, tr.nrows,
+                               &S.bar[q]);
             head += alloc;
             seq++;
             vstore(&S.issued, seq);
@@ -513,26 +517,34 @@ __device__ __forceinline__ void signal(uint32_t* ctr, uint32_t n) {
 }
 
 __device__ void consumer(const DecArgs& a, DecShared& S, uint8_t* ring, const MmaSmem& sm, float* stage,
-                         float* mw, uint32_t tid) {
-    const uint32_t* my = a.sched + (uint64_t)blockIdx.x * a.sched_stride;
+                         uint32_t tid) {
+    const uint32_t* my = S.tasks;
     const uint32_t n_my = a.sched_len[blockIdx.x];
+    const DecOp& op = S.op;
     uint32_t cseq = 0;
     for (uint32_t j = 0; j < a.n_steps; j++) {
         const uint32_t E = S.epoch + j;
         uint32_t staged = 0xFFFFFFFFu, run_op = 0xFFFFFFFFu, run_n = 0;
         for (uint32_t i = 0; i < n_my; i++) {
             const uint32_t ent = my[i], op_i = ent >> 16, task = ent & 0xFFFFu;
-            const DecOp& op = a.ops[op_i];
             bool prefetched = false;
             if (op_i != run_op) {              // first task of this op here: wait for its input
-                if (op.kind == DEC_ATTN) {
+                // the op's descriptor into shared memory (read-only, so this
+                // runs while the input may still be on its way)
+                {
+                    const uint32_t* src = reinterpret_cast<const uint32_t*>(a.ops + op_i);
+                    uint32_t* dst = reinterpret_cast<uint32_t*>(&S.op);
+                    csync();                   // every thread is done with the previous op
+                    // warps 1..7 copy; warp 0 goes straight on to poll the input
+                    for (uint32_t w = tid - 32; tid >= 32 && w < (uint32_t)(sizeof(DecOp) / 4); w += kDCons - 32)
+                        dst[w] = __ldg(src + w);
+                }
+                if (S.kind[op_i] == DEC_ATTN) {
                     // the cached K/V rows do not depend on this op's input, only on
                     // the step having started (its position, the earlier steps' rows)
-                    if (run_op == 0xFFFFFFFFu) {
-                        bool ok = true;
-                        if (tid == 0) ok = dep_wait(a, S, &a.sync->step_done, E);
-                        if (csync_or(!ok)) return;
-                    }
+                    bool ok = true;
+                    if (run_op == 0xFFFFFFFFu && tid == 0) ok = dep_wait(a, S, &a.sync->step_done, E);
+                    if (csync_or(!ok)) return;     // also publishes the descriptor copy
                     if (op.at.kv_f16) attn_prefetch<__half>(a, op, task, stage, tid);
                     else attn_prefetch<float>(a, op, task, stage, tid);
                     prefetched = true;
@@ -540,16 +552,17 @@ __device__ void consumer(const DecArgs& a, DecShared& S, uint8_t* ring, const Mm
                 }
                 bool ok = true;
                 if (tid == 0) {
-                    if (op.wait == kDecNoWait) ok = dep_wait(a, S, &a.sync->step_done, E);
-                    else ok = dep_wait(a, S, &a.done[op.wait], (E + 1) * a.ops[op.wait].ndone);
+                    const uint32_t w = S.wait_ctr[op_i];
+                    if (w == kDecNoWait) ok = dep_wait(a, S, &a.sync->step_done, E);
+                    else ok = dep_wait(a, S, &a.done[w], (E + 1) * S.wait_n[op_i]);
                 }
                 if (csync_or(!ok)) return;
                 run_op = op_i;
                 run_n = 0;
             }
-            if (op.kind == DEC_GEMV) {
+            if (S.kind[op_i] == DEC_GEMV) {
                 if (staged != op_i) {
-                    stage_x_dec(a, op, sm, mw, &S.scale, tid);
+                    stage_x_dec(a, op, sm, &S.scale, tid);
                     staged = op_i;
                 }
                 const uint32_t q = cseq % kQ;
@@ -605,12 +618,23 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         S.abort = vload(&a.sync->abort);
         S.epoch = ld_acq(&a.sync->epoch);
     }
+    {
+        const uint32_t* my = a.sched + (uint64_t)blockIdx.x * a.sched_stride;
+        const uint32_t n_my = a.sched_len[blockIdx.x];
+        for (uint32_t i = tid; i < n_my; i += kDThreads) S.tasks[i] = my[i];
+        for (uint32_t o = tid; o < a.n_ops; o += kDThreads) {
+            const uint32_t w = a.ops[o].wait;
+            S.wait_ctr[o] = w;
+            S.wait_n[o] = w == kDecNoWait ? 0u : a.ops[w].ndone;
+            S.kind[o] = (uint8_t)a.ops[o].kind;
+        }
+    }
     __syncthreads();
     if (warp == (uint32_t)kDWarps) {
         if (lane == 0) producer(a, S, ring);
         __syncwarp();
     } else {
-        consumer(a, S, ring, sm, stage, sm.part + kDWarps * 16, tid);
+        consumer(a, S, ring, sm, stage, tid);
     }
     __syncthreads();
     if (tid == 0) {

@@ -150,11 +150,11 @@ __device__ __forceinline__ void issue_tile(const GemvArgs& a, uint32_t t, uint8_
     const TileRef tr = tile_of(a, t);
     const GemvSeg& G = a.seg[tr.seg];
     const bool glu = G.epi == EPI_GLU_SILU || G.epi == EPI_GLU_GELU;
-    const uint32_t n1 = (uint32_t)(((uint64_t)tr.nrows * G.row_bytes + 15) & ~uint64_t(15));
-    const uint32_t n2 = glu ? (uint32_t)(((uint64_t)tr.nrows * G.row_bytes2 + 15) & ~uint64_t(15)) : 0u;
+    const uint32_t n1 = rows_tx(G.row_bytes, tr.nrows);
+    const uint32_t n2 = glu ? rows_tx(G.row_bytes2, tr.nrows) : 0u;
     mbar_expect_tx(bar, n1 + n2);
-    bulk_g2s(buf, G.w + (uint64_t)tr.row0 * G.row_bytes, n1, bar);
-    if (glu) bulk_g2s(buf + up_offset(G), G.w2 + (uint64_t)tr.row0 * G.row_bytes2, n2, bar);
+    copy_rows(buf, G.w + (uint64_t)tr.row0 * G.row_bytes, G.row_bytes, tr.nrows, bar);
+    if (glu) copy_rows(buf + up_offset(G), G.w2 + (uint64_t)tr.row0 * G.row_bytes2, G.row_bytes2, tr.nrows, bar);
 }
 
 // ------------------------------------------------------------------ kernel
@@ -216,7 +216,7 @@ gemv_mma_kernel(const __grid_constant__ GemvArgs a, uint32_t stage_bytes) {
         const uint32_t half = kMWarps / 2;
         const bool up = glu && warp >= half;
         const uint8_t* base = up ? buf + up_offset(G) : buf;
-        const uint64_t rb = up ? G.row_bytes2 : G.row_bytes;
+        const uint64_t rb = smem_rs(up ? G.row_bytes2 : G.row_bytes);
         const uint32_t first = glu ? warp % half : warp, step = glu ? half : kMWarps;
         float acc[2] = {0.f, 0.f};
         switch (G.type) {
@@ -307,8 +307,8 @@ bool launch_gemv_mma(const GemvArgs& in, cudaStream_t st, bool* handled) {
         // tile start (row multiples of 16, so 16 * row_bytes suffices)
         if (reinterpret_cast<uintptr_t>(g.w) % 16 != 0 || (glu && reinterpret_cast<uintptr_t>(g.w2) % 16 != 0))
             return true;
-        const uint64_t t1 = ((16 * g.row_bytes) + 15) & ~uint64_t(15);
-        const uint64_t t2 = glu ? ((16 * g.row_bytes2) + 15) & ~uint64_t(15) : 0;
+        const uint64_t t1 = tile_bytes(g.row_bytes);
+        const uint64_t t2 = glu ? tile_bytes(g.row_bytes2) : 0;
         stage = stage > t1 + t2 ? stage : t1 + t2;
     }
     // 16 bytes of slack past each stage: funnel-shifted word reads at the tile end

@@ -326,9 +326,33 @@ __device__ __forceinline__ TileRef tile_of(const GemvArgs& a, uint32_t t) {
     return TileRef{s, row0, min(16u, G.rows - row0)};
 }
 
-// Offset of the up matrix's rows in a gated tile's stage buffer.
-__device__ __forceinline__ uint32_t up_offset(const GemvSeg& G) {
-    return (uint32_t)(((16 * G.row_bytes) + 15) & ~uint64_t(15));
+__host__ __device__ __forceinline__ uint32_t align16(uint64_t v) { return (uint32_t)((v + 15) & ~uint64_t(15)); }
+
+// Row stride of a tile in shared memory. Rows that are an even number of
+// 16-byte units long would all start in the same bank group, so the 8 rows an
+// MMA fragment reads at once would conflict 8 ways; such rows are copied one
+// by one to a stride of one more unit. Other row sizes stay contiguous and
+// move in one copy.
+__host__ __device__ __forceinline__ uint64_t smem_rs(uint64_t rb) {
+    return (rb % 16 == 0 && (rb / 16) % 2 == 0) ? rb + 16 : rb;
+}
+// Shared-memory bytes of one 16-row tile.
+__host__ __device__ __forceinline__ uint32_t tile_bytes(uint64_t rb) { return align16(16 * smem_rs(rb)); }
+// Offset of the up matrix's rows in a gated tile.
+__host__ __device__ __forceinline__ uint32_t up_offset(const GemvSeg& G) { return tile_bytes(G.row_bytes); }
+// Bytes the copies of `nrows` rows deliver (what the mbarrier expects).
+__host__ __device__ __forceinline__ uint32_t rows_tx(uint64_t rb, uint32_t nrows) {
+    return smem_rs(rb) == rb ? align16((uint64_t)nrows * rb) : (uint32_t)(nrows * rb);
+}
+// One thread: copy rows [0, nrows) at src (row size rb) into dst at stride smem_rs(rb).
+__device__ __forceinline__ void copy_rows(uint8_t* dst, const uint8_t* src, uint64_t rb, uint32_t nrows,
+                                          uint64_t* bar) {
+    const uint64_t rs = smem_rs(rb);
+    if (rs == rb) {
+        bulk_g2s(dst, src, align16((uint64_t)nrows * rb), bar);
+        return;
+    }
+    for (uint32_t r = 0; r < nrows; r++) bulk_g2s(dst + r * rs, src + (uint64_t)r * rb, (uint32_t)rb, bar);
 }
 
 }  // namespace lm

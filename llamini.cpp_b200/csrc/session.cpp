@@ -347,7 +347,6 @@ bool build_decode(llamini_session* s) {
     const char* env = getenv("LLAMINI_DECODE_KERNEL");
     if (env && env[0] == '0') return true;
     if (s->hd > 256 || s->hd == 0 || s->hd % 4 != 0 || s->n_split > 32) return true;
-    if ((size_t)s->n_heads * (s->n_split + 1) > 1024) return true;      // merge weights in shared memory
     std::vector<DecOp> ops;
     u32 kmax = 0;
     bool ok = true;
@@ -425,6 +424,7 @@ bool build_decode(llamini_session* s) {
         }
     u32 stride = 1;
     for (auto& v : per) stride = stride > v.size() ? stride : (u32)v.size();
+    if (stride > kDecMaxTasks || ops.size() > kDecMaxOpsSmem) return true;
     std::vector<u32> sched((size_t)n_cta * stride, 0u), len(n_cta);
     for (u32 c = 0; c < n_cta; c++) {
         len[c] = (u32)per[c].size();
