@@ -130,6 +130,24 @@ def init_dist(ws, local, backend):
     return dist if ws > 1 else None
 
 
+def max_over_ranks(dist, values):
+    """Element-wise max over ranks of per-rank numbers (device times, wall
+    times); the numbers themselves when there is one rank. NaN stays NaN."""
+    if not dist:
+        return [float(v) for v in values]
+    import torch
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.tolist()]
+
+
+def whole_job_rate(ws, steps_per_rank, t_max_ms):
+    """Tokens per second of the whole job: every rank decodes its own sequence
+    for steps_per_rank steps; the job takes as long as the slowest rank."""
+    return ws * steps_per_rank / (t_max_ms / 1e3)
+
+
 def workload_path(rank, dist):
     S = synthetic()
     directory = os.environ.get("LLAMINI_WORKDIR", "/tmp/llamini_b200")
@@ -141,6 +159,9 @@ def workload_path(rank, dist):
 
 
 # --------------------------------------------------------------------------- ours
+
+GEMV_GATE_UP_TRAFFIC = 13059584
+
 
 def kernel_roofline(lm, torch, stream, hbm_peak, peak_kind):
     """Dominant kernel: the fused GEMV at the gate+up launch shape of a layer."""
@@ -174,7 +195,10 @@ def kernel_roofline(lm, torch, stream, hbm_peak, peak_kind):
     return {"kernel": "gemv_mma_kernel (Q4_K, 11264x2048, gate+up shape)", "bound": "hbm",
             "achieved": round(achieved, 1), "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
             "frac": round(achieved / hbm_peak, 4), "algorithmic_bytes_per_launch": algo,
-            "us_per_launch": round(per_launch_s * 1e6, 2), "traffic": None}
+            "us_per_launch": round(per_launch_s * 1e6, 2),
+            # dram__bytes_read.sum + dram__bytes_write.sum of this launch shape in one ncu
+            # capture (profiles/gemv_mma_llama_1b_ncu.md): equal to the algorithmic bytes
+            "traffic": GEMV_GATE_UP_TRAFFIC}
 
 
 def step_kernel_roofline(decode_kernel, step_bytes, t_ms, steps, hbm_peak, peak_kind, gemv_roof):
@@ -239,15 +263,10 @@ def run_ours(args, ws, rank, local):
         gemv_roof = None
         if rank == 0 and not args.no_kernel_roofline:
             gemv_roof = kernel_roofline(lm, torch, stream, hbm_peak, peak_kind)
-    t_max = ms
-    e2e_max = e2e_s
-    if dist:
-        tt = torch.tensor([ms, e2e_s], device="cuda", dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_max, e2e_max = float(tt[0]), float(tt[1])
+    t_max, e2e_max = max_over_ranks(dist, [ms, e2e_s])
     if rank == 0:
         steps = args.steps
-        value = ws * steps / (t_max / 1e3)
+        value = whole_job_rate(ws, steps, t_max)
         ctx_mean = pos0 + (steps - 1) / 2 + 1
         step_bytes = weight_bytes + kv_per_pos * ctx_mean
         step_s = t_max / 1e3 / steps

@@ -338,14 +338,15 @@ void destroy(llamini_session* s) {
 
 bool g_kv_f16 = false;
 
-// Op table and per-CTA schedule of the persistent decode kernel. Returns true
-// with dec_on = false when the model has a matrix format or shape the kernel
-// does not take (the per-op graphs run those models), or when
-// LLAMINI_DECODE_KERNEL=0.
+// Op table and per-CTA schedule of the persistent decode kernel, built when
+// LLAMINI_DECODE_KERNEL=1 at session creation (the per-op graphs are the
+// default while they are the faster path). Returns true with dec_on = false
+// when the kernel is not asked for, or the model has a matrix format or shape
+// it does not take.
 bool build_decode(llamini_session* s) {
     s->dec_on = false;
     const char* env = getenv("LLAMINI_DECODE_KERNEL");
-    if (env && env[0] == '0') return true;
+    if (!env || env[0] != '1') return true;
     if (s->hd > 256 || s->hd == 0 || s->hd % 4 != 0 || s->n_split > 32) return true;
     std::vector<DecOp> ops;
     u32 kmax = 0;

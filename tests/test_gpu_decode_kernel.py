@@ -3,8 +3,8 @@
 Both paths compute every matrix tile, norm, attention split and merge with the
 same arithmetic in the same order, so the greedy tokens, the logits and the
 per-layer residual stream must be bit-identical -- not just within the 1e-3
-bar the oracle comparisons use. The per-op path is selected by creating the
-session with LLAMINI_DECODE_KERNEL=0.
+bar the oracle comparisons use. A session uses the decode kernel when it is
+created with LLAMINI_DECODE_KERNEL=1 and the per-op graphs with =0.
 """
 from __future__ import annotations
 
@@ -18,23 +18,27 @@ from conftest import same_bits
 pytestmark = pytest.mark.gpu
 
 
-def _pair(gpu, path):
-    """Two independent loads of one file: decode kernel, then per-op graphs."""
-    a = gpu.Model(path)
-    sa = a.session()
+def _session_with(gpu, path, flag):
     old = os.environ.get("LLAMINI_DECODE_KERNEL")
-    os.environ["LLAMINI_DECODE_KERNEL"] = "0"
+    os.environ["LLAMINI_DECODE_KERNEL"] = flag
     try:
-        b = gpu.Model(path)
-        sb = b.session()
+        m = gpu.Model(path)
+        m.session()
     finally:
         if old is None:
             del os.environ["LLAMINI_DECODE_KERNEL"]
         else:
             os.environ["LLAMINI_DECODE_KERNEL"] = old
+    return m
+
+
+def _pair(gpu, path):
+    """Two independent loads of one file: decode kernel, then per-op graphs."""
+    a = _session_with(gpu, path, "1")
+    b = _session_with(gpu, path, "0")
     L = gpu.lib()
-    assert L.llamini_session_kernel(sa) == 1, gpu.last_error()
-    assert L.llamini_session_kernel(sb) == 0
+    assert L.llamini_session_kernel(a.session()) == 1, gpu.last_error()
+    assert L.llamini_session_kernel(b.session()) == 0
     return a, b
 
 
