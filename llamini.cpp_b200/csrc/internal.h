@@ -215,6 +215,56 @@ uint32_t decode_ring_bytes(uint32_t kmax, uint32_t hd);
 uint32_t decode_tile_alloc(const GemvSeg& G);    // ring bytes of one tile of G
 bool launch_decode(const DecArgs& a, cudaStream_t st);
 
+// ---------------------------------------------------------------- batched GEMM
+// Up to 64 input vectors per weight pass (k_bgemm.cu): staging per sequence,
+// split-K dequant GEMM into raw partials, per-(sequence, row) finish.
+struct BStageArgs {
+    const float* x = nullptr;      // [B][ldx]
+    uint32_t ldx = 0, K = 0, B = 0;
+    uint32_t norm = NORM_NONE;
+    const float* norm_w = nullptr;
+    const float* norm_b = nullptr;
+    float eps = 0.f;
+    uint16_t* xh = nullptr;        // [B][K] fp16 bits of x * 2^E_b, high part
+    uint16_t* xl = nullptr;        // low part
+    float* sx = nullptr;           // [B][K/16] 16-element sums * 2^(E_b - 24)
+    float* oscale = nullptr;       // [B] 2^(24 - E_b)
+};
+struct BSeg {
+    const uint8_t* w = nullptr;
+    uint64_t row_bytes = 0;
+    uint32_t type = 0, rows = 0;
+    uint32_t rb0 = 0;              // first row block (filled by bgemm_plan)
+    float* part = nullptr;         // [ksplit][B][rows] raw sums
+};
+struct BGemmArgs {
+    const uint16_t* xh = nullptr;
+    const uint16_t* xl = nullptr;
+    const float* sx = nullptr;
+    uint32_t B = 0, K = 0;
+    uint32_t nseg = 0;
+    BSeg seg[3];
+    // filled by bgemm_plan
+    uint32_t ue = 0, ub = 0, ups = 0, ksplit = 0, rblocks = 0, wrs = 0, xs = 0, bpad = 0;
+};
+struct BFinishArgs {
+    const float* part = nullptr;   // [ksplit][B][rows]
+    const float* part2 = nullptr;  // up-matrix sums for EPI_GLU_*
+    uint32_t ksplit = 1, B = 0, rows = 0;
+    const float* oscale = nullptr;
+    const float* bias = nullptr;
+    uint32_t epi = EPI_STORE;
+    float* out = nullptr;          // out[b * ldo + r]
+    uint32_t ldo = 0;
+    unsigned long long* keys = nullptr;   // [B] argmax keys (or null)
+};
+bool bgemm_init();
+bool bgemm_type(uint32_t type);
+bool bgemm_plan(BGemmArgs& a, uint32_t target_ctas);
+bool launch_bgemm(const BGemmArgs& a, cudaStream_t st);
+bool launch_bstage(const BStageArgs& a, cudaStream_t st);
+bool launch_bfinish(const BFinishArgs& a, cudaStream_t st);
+
 // Host-pointer op kernels (model.h per-op exports), device buffers in/out.
 bool launch_rms_norm(float* out, const float* x, const float* w, uint32_t dim, float eps, cudaStream_t st);
 bool launch_layer_norm(float* out, const float* x, const float* w, const float* b, uint32_t dim, float eps, cudaStream_t st);

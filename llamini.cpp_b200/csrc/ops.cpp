@@ -29,7 +29,7 @@ struct Scratch {
         return p;
     }
 };
-Scratch g_s[6];
+Scratch g_s[10];
 
 bool h2d(void* d, const void* h, size_t n) {
     return n == 0 || LM_CUDA(cudaMemcpyAsync(d, h, n, cudaMemcpyHostToDevice, lm::stream()));
@@ -39,6 +39,61 @@ bool d2h(void* h, const void* d, size_t n) {
     return LM_CUDA(cudaStreamSynchronize(lm::stream()));
 }
 float* fbuf(int slot, size_t n) { return (float*)g_s[slot].get(n * sizeof(float)); }
+
+// y[b] = W x[b] for b < batch through the batched dequant-GEMM (per-sequence
+// staging, split-K partials, finish); scratch in slots 6..9. *handled is false
+// when the format or shape has no batched path (the caller loops columns).
+bool gemv_batch(uint32_t type, const uint8_t* w, uint32_t rows, uint32_t cols, const float* x, uint32_t batch,
+                float* y, bool* handled) {
+    *handled = false;
+    lm::BGemmArgs g;
+    g.B = batch;
+    g.K = cols;
+    g.nseg = 1;
+    g.seg[0].w = w;
+    g.seg[0].row_bytes = lm::type_bytes(type, cols);
+    g.seg[0].type = type;
+    g.seg[0].rows = rows;
+    if (g.seg[0].row_bytes == 0 || !lm::bgemm_plan(g, 2u * (uint32_t)lm::sm_count())) return true;
+    *handled = true;
+    uint16_t* xh = (uint16_t*)g_s[6].get((size_t)batch * cols * 2);
+    uint16_t* xl = (uint16_t*)g_s[7].get((size_t)batch * cols * 2);
+    float* sx = fbuf(8, (size_t)batch * (cols / 16) + batch);
+    float* part = fbuf(9, (size_t)g.ksplit * batch * rows);
+    if (!xh || !xl || !sx || !part) return false;
+    lm::BStageArgs st;
+    st.x = x;
+    st.ldx = cols;
+    st.K = cols;
+    st.B = batch;
+    st.xh = xh;
+    st.xl = xl;
+    st.sx = sx;
+    st.oscale = sx + (size_t)batch * (cols / 16);
+    g.xh = xh;
+    g.xl = xl;
+    g.sx = sx;
+    g.seg[0].part = part;
+    lm::BFinishArgs f;
+    f.part = part;
+    f.ksplit = g.ksplit;
+    f.B = batch;
+    f.rows = rows;
+    f.oscale = st.oscale;
+    f.epi = lm::EPI_STORE;
+    f.out = y;
+    f.ldo = rows;
+    return lm::launch_bstage(st, lm::stream()) && lm::launch_bgemm(g, lm::stream()) && lm::launch_bfinish(f, lm::stream());
+}
+
+bool gemv_any(uint32_t type, const uint8_t* w, uint32_t rows, uint32_t cols, const float* x, uint32_t batch, float* y) {
+    if (batch > 1 && batch <= 64 && cols % 32 == 0) {
+        bool handled = false;
+        const bool ok = gemv_batch(type, w, rows, cols, x, batch, y, &handled);
+        if (handled) return ok;
+    }
+    return lm::launch_gemv_plain(type, w, rows, cols, x, batch, y, lm::stream());
+}
 
 }  // namespace
 
@@ -66,7 +121,7 @@ int llamini_dequant_host(u32 type, const void* blocks, u64 n, f32* out) {
 
 int llamini_gemv_device(u32 type, const void* d_w, u32 rows, u32 cols, const f32* d_x, u32 batch, f32* d_y) {
     if (!lm::ensure_device()) return -1;
-    return lm::launch_gemv_plain(type, (const uint8_t*)d_w, rows, cols, d_x, batch, d_y, lm::stream()) ? 0 : -1;
+    return gemv_any(type, (const uint8_t*)d_w, rows, cols, d_x, batch, d_y) ? 0 : -1;
 }
 
 int llamini_gemv_host(u32 type, const void* w, u32 rows, u32 cols, const f32* x, u32 batch, f32* y) {
@@ -78,7 +133,7 @@ int llamini_gemv_host(u32 type, const void* w, u32 rows, u32 cols, const f32* x,
     float* dy = fbuf(2, (size_t)batch * rows);
     if (!dw || !dx || !dy) return -1;
     if (!h2d(dw, w, rb * rows) || !h2d(dx, x, (size_t)batch * cols * 4)) return -1;
-    if (!lm::launch_gemv_plain(type, dw, rows, cols, dx, batch, dy, lm::stream())) return -1;
+    if (!gemv_any(type, dw, rows, cols, dx, batch, dy)) return -1;
     return d2h(y, dy, (size_t)batch * rows * 4) ? 0 : -1;
 }
 

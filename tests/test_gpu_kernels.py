@@ -72,16 +72,33 @@ def test_gemv_sweep_vs_oracle(gpu, orc, synth, t, shape):
     assert rel_l2(y, want) < GEMV_TOL, rel_l2(y, want)
 
 
-@pytest.mark.parametrize("batch", [8, 64])
-def test_gemv_batch_columns(gpu, orc, synth, batch):
-    rows, cols = 2048, 2048
+@pytest.mark.parametrize("t", QTYPES + [1])
+@pytest.mark.parametrize("batch", [3, 8, 64])
+def test_gemv_batch_columns(gpu, orc, synth, t, batch):
+    """Batch columns (the config's 1, 8 and 64, plus a batch that is not a
+    multiple of 4): every column within the GEMV tolerance of the oracle."""
+    rows, cols = (2048, 2048) if batch != 64 else (1000, 2048)
     rng = np.random.default_rng(1)
-    raw = synth.random_blocks(rng, 12, rows * cols)
+    raw = synth.random_blocks(rng, t, rows * cols) if t != 1 else \
+        rng.normal(0, 0.05, rows * cols).astype(np.float16).view(np.uint8)
     x = rng.normal(0, 1, (batch, cols)).astype(np.float32)
-    y = np.zeros((batch, rows), np.float32)
-    assert gpu.lib().llamini_gemv_host(12, gpu.ptr(raw), rows, cols, gpu.ptr(x), batch, gpu.ptr(y)) == 0
-    for b in (0, batch // 2, batch - 1):
-        assert rel_l2(y[b], _orc_linear(orc, 12, raw, rows, cols, x[b])) < GEMV_TOL
+    y = np.full((batch, rows), np.nan, np.float32)
+    assert gpu.lib().llamini_gemv_host(t, gpu.ptr(raw), rows, cols, gpu.ptr(x), batch, gpu.ptr(y)) == 0, gpu.last_error()
+    for b in range(batch):
+        assert rel_l2(y[b], _orc_linear(orc, t, raw, rows, cols, x[b])) < GEMV_TOL, (b, rel_l2(y[b], _orc_linear(orc, t, raw, rows, cols, x[b])))
+
+
+@pytest.mark.parametrize("t", [12, 14, 8])
+def test_gemv_batch_wide(gpu, orc, synth, t):
+    """Batch 64 on the down-projection shape (K = 5632, split over CTAs)."""
+    rows, cols, batch = 2048, 5632, 64
+    rng = np.random.default_rng(2)
+    raw = synth.random_blocks(rng, t, rows * cols)
+    x = rng.normal(0, 1, (batch, cols)).astype(np.float32)
+    y = np.full((batch, rows), np.nan, np.float32)
+    assert gpu.lib().llamini_gemv_host(t, gpu.ptr(raw), rows, cols, gpu.ptr(x), batch, gpu.ptr(y)) == 0, gpu.last_error()
+    for b in (0, 17, 63):
+        assert rel_l2(y[b], _orc_linear(orc, t, raw, rows, cols, x[b])) < GEMV_TOL
 
 
 @pytest.mark.parametrize("t", [0, 1])
