@@ -138,6 +138,39 @@ u64 llamini_session_kv_bytes_per_pos(llamini_session* s);
  * the synthetic models its rounding moves logits by ~2e-3 relative L2). */
 int llamini_set_kv_f16(int enable);
 
+/* ---- batched decode (no counterpart in the reference, which decodes one
+ *      sequence at a time: generate.c:122-167 run for each sequence) ---------- */
+
+typedef struct llamini_batch llamini_batch;
+
+/* A batch of up to max_batch (<= 64) independent sequences of at most max_seq
+ * positions over a loaded model. Every weight matrix is read once per step for
+ * the whole batch; the device KV cache holds max_batch x max_seq positions. All
+ * matrices must be Q4_K, Q6_K, Q8_0, Q4_0 or F16 (NULL and a message otherwise).
+ * Free it with llamini_batch_free before the model and its GGUF file. */
+llamini_batch* llamini_llama_batch(LLaMAModel* model, u32 max_batch, u32 max_seq);
+llamini_batch* llamini_gpt2_batch(GPT2Model* model, u32 max_batch, u32 max_seq);
+
+/* Start n_seq sequences at position 0: prompts holds the n_seq prompts back to
+ * back, prompt_lens their lengths (each >= 1). */
+int llamini_batch_begin(llamini_batch* b, u32 n_seq, const u32* prompts, const u32* prompt_lens);
+
+/* Enqueue n_steps positions of every sequence. At position p sequence s embeds
+ * token[s][p]; once p + 1 is past its prompt its greedy token becomes
+ * token[s][p + 1] -- per sequence exactly generate_autoregressive with temp 0
+ * and no EOS (an EOS is for the caller to cut at). */
+int llamini_batch_step(llamini_batch* b, u32 n_steps);
+
+/* Wait, copy token[seq][0..n) to out; returns the number of valid tokens. */
+int llamini_batch_tokens(llamini_batch* b, u32 seq, u32* out, u32 n);
+
+/* Wait, copy the logits of sequence seq at the most recent step. */
+int llamini_batch_logits(llamini_batch* b, u32 seq, f32* out);
+
+u32 llamini_batch_pos(llamini_batch* b);
+u64 llamini_batch_weight_bytes(llamini_batch* b);
+void llamini_batch_free(llamini_batch* b);
+
 /* Per-layer residual stream of the most recent step: n_layers x dim floats,
  * captured when `enable` was set before the step ran. For parity tests. */
 int llamini_session_trace(llamini_session* s, int enable);

@@ -152,6 +152,15 @@ SIGNATURES = {
     "llamini_session_tokens": (C.c_int, [P, P, u32]),
     "llamini_session_logits": (C.c_int, [P, P]),
     "llamini_session_pos": (u32, [P]),
+    "llamini_llama_batch": (P, [P, u32, u32]),
+    "llamini_gpt2_batch": (P, [P, u32, u32]),
+    "llamini_batch_begin": (C.c_int, [P, u32, P, P]),
+    "llamini_batch_step": (C.c_int, [P, u32]),
+    "llamini_batch_tokens": (C.c_int, [P, u32, P, u32]),
+    "llamini_batch_logits": (C.c_int, [P, u32, P]),
+    "llamini_batch_pos": (u32, [P]),
+    "llamini_batch_weight_bytes": (u64, [P]),
+    "llamini_batch_free": (None, [P]),
     "llamini_session_kernel": (C.c_int, [P]),
     "llamini_session_weight_bytes": (u64, [P]),
     "llamini_session_kv_bytes_per_pos": (u64, [P]),

@@ -143,6 +143,14 @@ struct AttnArgs {
     const float* theta;    // [hd/2] rotation frequencies base^(-2j/hd), computed on the host
 };
 bool launch_attention(const AttnArgs& a, cudaStream_t st);
+// Per-sequence strides of batched decode attention (elements / bytes).
+struct AttnBatch {
+    uint64_t qkv_stride;   // floats between sequences' q|k|v rows
+    uint64_t cache_stride; // bytes between sequences' caches of one layer
+    uint64_t out_stride;   // floats between output rows
+    uint64_t part_stride;  // floats between sequences' split partials
+};
+bool launch_attention_batch(const AttnArgs& a, const AttnBatch& bt, uint32_t B, cudaStream_t st);
 
 struct FinishArgs {
     StepState* st;
@@ -258,6 +266,25 @@ struct BFinishArgs {
     uint32_t ldo = 0;
     unsigned long long* keys = nullptr;   // [B] argmax keys (or null)
 };
+struct BEmbedArgs {
+    const StepState* st;           // pos (shared by the batch)
+    const uint32_t* tokens;        // [B][tok_stride]
+    uint32_t tok_stride;
+    DevMat tok, pos;               // token table, learned positions (or ptr == nullptr)
+    float scale;
+    float* hidden;                 // [B][dim]
+    uint32_t dim;
+};
+struct BTokenArgs {
+    StepState* st;
+    uint32_t* tokens;
+    uint32_t tok_stride;
+    const uint32_t* n_prompt;      // [B]
+    unsigned long long* keys;      // [B] argmax keys of the step (reset here)
+    uint32_t B, max_tokens;
+};
+bool launch_bembed(const BEmbedArgs& a, uint32_t B, cudaStream_t st);
+bool launch_btoken(const BTokenArgs& a, cudaStream_t st);
 bool bgemm_init();
 bool bgemm_type(uint32_t type);
 bool bgemm_plan(BGemmArgs& a, uint32_t target_ctas);

@@ -23,17 +23,13 @@ namespace lm {
 
 constexpr int kAttnThreads = 128;
 
+// Split `split` of head h for the sequence whose buffers `a` points at.
 template <typename KV>
-__global__ void __launch_bounds__(kAttnThreads)
-attn_decode_kernel(const AttnArgs a) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ int is_last;
-    __shared__ float s_ls;
-    pdl_trigger();
-    pdl_wait();                                   // q/k/v come from the QKV projection
+__device__ __forceinline__ void attn_one(const AttnArgs& a, uint32_t h, uint32_t split, uint8_t* smem, int& is_last,
+                                         float& s_ls) {
     const uint32_t G = a.n_heads / a.n_kv;        // query heads per kv head (model.c:220)
     const uint32_t hd = a.hd;
-    const uint32_t h = blockIdx.x, g = h / G, split = blockIdx.y;
+    const uint32_t g = h / G;
     const uint32_t pos = a.st->pos;
     const SplitRange r = split_range(pos, a.n_split, split);
     if (split >= r.ns) return;
@@ -87,8 +83,40 @@ attn_decode_kernel(const AttnArgs a) {
     if (tid == 0) a.counter[h] = 0u;
 }
 
+template <typename KV>
+__global__ void __launch_bounds__(kAttnThreads)
+attn_decode_kernel(const AttnArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ int is_last;
+    __shared__ float s_ls;
+    pdl_trigger();
+    pdl_wait();                                   // q/k/v come from the QKV projection
+    attn_one<KV>(a, blockIdx.x, blockIdx.y, smem, is_last, s_ls);
+}
+
+// Batched decode: blockIdx.z = sequence; each sequence has its own q/k/v row,
+// cache, output row, split partials and tickets, all at fixed strides.
+template <typename KV>
+__global__ void __launch_bounds__(kAttnThreads)
+attn_batch_kernel(const AttnArgs a, const AttnBatch bt) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ int is_last;
+    __shared__ float s_ls;
+    const uint32_t b = blockIdx.z;
+    AttnArgs s = a;
+    s.qkv = a.qkv + (uint64_t)b * bt.qkv_stride;
+    s.kc = reinterpret_cast<uint8_t*>(a.kc) + (uint64_t)b * bt.cache_stride;
+    s.vc = reinterpret_cast<uint8_t*>(a.vc) + (uint64_t)b * bt.cache_stride;
+    s.out = a.out + (uint64_t)b * bt.out_stride;
+    s.part = a.part + (uint64_t)b * bt.part_stride;
+    s.counter = a.counter + (uint64_t)b * a.n_heads;
+    attn_one<KV>(s, blockIdx.x, blockIdx.y, smem, is_last, s_ls);
+}
+
 bool attn_init() {
-    return LM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)) &&
+    return LM_CUDA(cudaFuncSetAttribute(attn_batch_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)) &&
+           LM_CUDA(cudaFuncSetAttribute(attn_batch_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)) &&
+           LM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)) &&
            LM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)) &&
            LM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<float>, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) &&
            LM_CUDA(cudaFuncSetAttribute(attn_decode_kernel<__half>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
@@ -104,6 +132,18 @@ bool launch_attention(const AttnArgs& a, cudaStream_t st) {
     const dim3 grid(a.n_heads, a.n_split);
     if (a.kv_f16) return LM_CUDA(launch_k(attn_decode_kernel<__half>, grid, dim3(kAttnThreads), smem, st, a));
     return LM_CUDA(launch_k(attn_decode_kernel<float>, grid, dim3(kAttnThreads), smem, st, a));
+}
+
+bool launch_attention_batch(const AttnArgs& a, const AttnBatch& bt, uint32_t B, cudaStream_t st) {
+    if (a.n_kv == 0 || a.n_heads % a.n_kv != 0 || a.hd == 0 || a.hd % 2 != 0 || a.n_split == 0 || a.hd > 256) {
+        set_error("attention: bad shape heads=%u kv=%u hd=%u", a.n_heads, a.n_kv, a.hd);
+        return false;
+    }
+    const size_t smem = attn_core_bytes(a.hd, a.kv_f16 != 0) + (size_t)a.n_split * 4;
+    const dim3 grid(a.n_heads, a.n_split, B);
+    if (a.kv_f16) attn_batch_kernel<__half><<<grid, kAttnThreads, smem, st>>>(a, bt);
+    else attn_batch_kernel<float><<<grid, kAttnThreads, smem, st>>>(a, bt);
+    return LM_CUDA(cudaGetLastError());
 }
 
 }  // namespace lm

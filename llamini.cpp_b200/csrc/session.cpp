@@ -467,12 +467,15 @@ bool build_decode(llamini_session* s) {
 
 
 
-bool finish_build(llamini_session* s) {
-    // theta_j = base^(-2j/hd), evaluated exactly as model.c:38 / model.c:50 do
+// theta_j = base^(-2j/hd), evaluated exactly as model.c:38 / model.c:50 do
+bool upload_theta(llamini_session* s) {
     std::vector<f32> th(s->hd / 2 ? s->hd / 2 : 1);
     for (u32 j = 0; j < s->hd / 2; j++) th[j] = powf(s->rope_base, -(f32)(2 * j) / (f32)s->hd);
     s->theta = upload_f32(s, th.data(), th.size());
-    if (!s->theta) return false;
+    return s->theta != nullptr;
+}
+
+bool finish_build(llamini_session* s) {
     s->kv_f16 = g_kv_f16 ? 1u : 0u;
     s->n_split = choose_splits(s->n_heads, s->max_seq);
     if (!alloc_buffers(s)) return false;
@@ -496,26 +499,22 @@ void drop_where(bool (*pred)(const llamini_session*, const void*), const void* k
     }
 }
 
-llamini_session* build_llama(LLaMAModel* m, KVCache* caches) {
-    if (!ensure_device()) return nullptr;
+// Shape and device weights of a LLaMA-family model (everything a step reads
+// that does not depend on the caches).
+bool bind_llama(llamini_session* s, LLaMAModel* m, u32 max_seq) {
     const LLaMAConfig& c = m->cfg;
-    auto* s = new llamini_session();
     s->kind = 0;
     s->model = m;
-    s->caches = caches;
-    s->cache_max_seq = caches[0].max_seq;
-    s->cache_dim = caches[0].dim;
     s->n_layers = c.n_layers; s->dim = c.dim; s->n_heads = c.n_heads; s->n_kv = c.n_heads_kv;
     s->hd = c.head_dim; s->ffn = c.ffn_dim; s->vocab = c.vocab_size;
     s->qd = c.n_heads * c.head_dim; s->kvd = c.n_heads_kv * c.head_dim;
-    s->max_seq = caches[0].max_seq;
-    s->max_pos = caches[0].max_seq;                   // generate.c:142
+    s->max_seq = max_seq;
+    s->max_pos = max_seq;                             // generate.c:142
     s->eps = c.rms_eps; s->rope_base = c.rope_freq_base; s->emb_scale = c.embedding_scale;
     s->rope_mode = c.rope_type == ROPE_NEOX ? 2u : 1u;
     s->act_gelu = c.ffn_act == ACT_GELU;
-    bool ok = s->n_kv > 0 && s->n_heads % s->n_kv == 0 && s->hd > 0 && caches[0].dim == s->kvd;
-    if (!ok) set_error("llama session: inconsistent heads/cache (heads %u kv %u hd %u cache dim %u)",
-                       s->n_heads, s->n_kv, s->hd, caches[0].dim);
+    bool ok = s->n_kv > 0 && s->n_heads % s->n_kv == 0 && s->hd > 0;
+    if (!ok) set_error("llama session: inconsistent heads (heads %u kv %u hd %u)", s->n_heads, s->n_kv, s->hd);
     ok = ok && weight(s, m->embeddings, c.vocab_size, c.dim, &s->tok);
     ok = ok && weight(s, m->lm_head, c.vocab_size, c.dim, &s->head);
     s->fnw = ok ? vec(s, m->final_norm, c.dim) : nullptr;
@@ -536,29 +535,21 @@ llamini_session* build_llama(LLaMAModel* m, KVCache* caches) {
     }
     // the tok table is read one row per step, not whole
     if (ok) s->weight_bytes -= s->tok.row_bytes * (s->tok.rows - 1);
-    ok = ok && finish_build(s);
-    if (!ok) { destroy(s); return nullptr; }
-    g_sessions.push_back(s);
-    return s;
+    return ok && upload_theta(s);
 }
 
-llamini_session* build_gpt2(GPT2Model* m, KVCache* caches) {
-    if (!ensure_device()) return nullptr;
+bool bind_gpt2(llamini_session* s, GPT2Model* m, u32 max_seq) {
     const GPT2Config& c = m->cfg;
-    auto* s = new llamini_session();
     s->kind = 1;
     s->model = m;
-    s->caches = caches;
-    s->cache_max_seq = caches[0].max_seq;
-    s->cache_dim = caches[0].dim;
     s->n_layers = c.n_layers; s->dim = c.dim; s->n_heads = c.n_heads; s->n_kv = c.n_heads;
     s->hd = c.n_heads ? c.dim / c.n_heads : 0; s->ffn = c.ffn_dim; s->vocab = c.vocab_size;
     s->qd = c.dim; s->kvd = c.dim;
-    s->max_seq = caches[0].max_seq;
-    s->max_pos = caches[0].max_seq < c.n_ctx ? caches[0].max_seq : c.n_ctx;   // gpt2.c:205
+    s->max_seq = max_seq;
+    s->max_pos = max_seq < c.n_ctx ? max_seq : c.n_ctx;   // gpt2.c:205
     s->eps = c.ln_eps; s->rope_mode = 0; s->emb_scale = 1.0f;
-    bool ok = s->hd > 0 && caches[0].dim == c.dim;
-    if (!ok) set_error("gpt2 session: cache dim %u != model dim %u", caches[0].dim, c.dim);
+    bool ok = s->hd > 0;
+    if (!ok) set_error("gpt2 session: no heads");
     ok = ok && weight(s, m->token_embd, c.vocab_size, c.dim, &s->tok);
     ok = ok && weight(s, m->pos_embd, c.n_ctx, c.dim, &s->pos_tab);
     ok = ok && weight(s, m->lm_head, c.vocab_size, c.dim, &s->head);
@@ -580,6 +571,37 @@ llamini_session* build_gpt2(GPT2Model* m, KVCache* caches) {
     if (ok) {
         s->weight_bytes -= s->tok.row_bytes * (s->tok.rows - 1);
         s->weight_bytes -= s->pos_tab.row_bytes * (s->pos_tab.rows - 1);
+    }
+    return ok && upload_theta(s);
+}
+
+llamini_session* build_llama(LLaMAModel* m, KVCache* caches) {
+    if (!ensure_device()) return nullptr;
+    auto* s = new llamini_session();
+    s->caches = caches;
+    s->cache_max_seq = caches[0].max_seq;
+    s->cache_dim = caches[0].dim;
+    bool ok = bind_llama(s, m, caches[0].max_seq);
+    if (ok && caches[0].dim != s->kvd) {
+        set_error("llama session: cache dim %u != kv dim %u", caches[0].dim, s->kvd);
+        ok = false;
+    }
+    ok = ok && finish_build(s);
+    if (!ok) { destroy(s); return nullptr; }
+    g_sessions.push_back(s);
+    return s;
+}
+
+llamini_session* build_gpt2(GPT2Model* m, KVCache* caches) {
+    if (!ensure_device()) return nullptr;
+    auto* s = new llamini_session();
+    s->caches = caches;
+    s->cache_max_seq = caches[0].max_seq;
+    s->cache_dim = caches[0].dim;
+    bool ok = bind_gpt2(s, m, caches[0].max_seq);
+    if (ok && caches[0].dim != m->cfg.dim) {
+        set_error("gpt2 session: cache dim %u != model dim %u", caches[0].dim, m->cfg.dim);
+        ok = false;
     }
     ok = ok && finish_build(s);
     if (!ok) { destroy(s); return nullptr; }
@@ -792,6 +814,318 @@ static llamini_session* gpt2_session(GPT2Model* m, KVCache* c) {
 
 }  // namespace lm
 
+// ================================================================ batched decode
+//
+// Up to max_batch sequences in lockstep: every step runs position p of every
+// sequence; a sequence reads its prompt until p passes it, then its own greedy
+// tokens (the semantics of generate_autoregressive per sequence). Each weight
+// matrix is read once per step for the whole batch (k_bgemm.cu); norms, RoPE,
+// attention and the argmax are per sequence.
+
+struct llamini_batch {
+    llamini_session* w = nullptr;     // shape and device weights (no single-sequence buffers)
+    u32 max_batch = 0, max_seq = 0, B = 0;
+    u32 n_split = 1, kv_f16 = 0, kmax = 0;
+    float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *ffn_h = nullptr, *logits = nullptr;
+    float *sx = nullptr, *part = nullptr, *part2 = nullptr, *apart = nullptr;
+    uint16_t *xh = nullptr, *xl = nullptr;
+    u32 *counters = nullptr, *tokens = nullptr, *n_prompt = nullptr;
+    unsigned long long* keys = nullptr;
+    void *kc = nullptr, *vc = nullptr;
+    lm::StepState* st = nullptr;
+    size_t part_floats = 0;
+    u32 plan_B = 0;                   // B the graphs were captured for
+    cudaGraphExec_t g_one = nullptr, g_many = nullptr;
+    u32 pos = 0;
+    std::vector<u32> lens;
+};
+
+namespace lm {
+namespace {
+
+constexpr u32 kBatchStepsPerGraph = 8;
+
+size_t batch_cache_bytes_per_seq(const llamini_batch* b) {
+    return (size_t)b->w->n_kv * b->max_seq * b->w->hd * (b->kv_f16 ? 2 : 4);
+}
+
+// GEMM plan of one matrix for the current batch (false: format not supported)
+bool batch_gemm(const llamini_batch* b, const DevMat& m, u32 K, float* part, BGemmArgs* out) {
+    BGemmArgs g;
+    g.xh = b->xh;
+    g.xl = b->xl;
+    g.sx = b->sx;
+    g.B = b->B;
+    g.K = K;
+    g.nseg = 1;
+    g.seg[0].w = m.ptr;
+    g.seg[0].row_bytes = m.row_bytes;
+    g.seg[0].type = m.type;
+    g.seg[0].rows = m.rows;
+    g.seg[0].part = part;
+    if (m.cols != K || !bgemm_plan(g, 2u * (u32)sm_count())) return false;
+    *out = g;
+    return true;
+}
+
+bool batch_stage(llamini_batch* b, const float* x, u32 K, u32 norm, const float* w, const float* bias, cudaStream_t st) {
+    BStageArgs a;
+    a.x = x;
+    a.ldx = K;
+    a.K = K;
+    a.B = b->B;
+    a.norm = norm;
+    a.norm_w = w;
+    a.norm_b = bias;
+    a.eps = b->w->eps;
+    a.xh = b->xh;
+    a.xl = b->xl;
+    a.sx = b->sx;
+    a.oscale = b->sx + (size_t)b->max_batch * (b->kmax / 16);
+    return launch_bstage(a, st);
+}
+
+bool batch_linear(llamini_batch* b, const DevMat& m, u32 K, float* part, const float* part2_src, uint32_t epi,
+                  const float* bias, float* out, u32 ldo, unsigned long long* keys, cudaStream_t st) {
+    BGemmArgs g;
+    if (!batch_gemm(b, m, K, part, &g)) {
+        set_error("batched decode: matrix format %u (%u x %u) has no batched kernel", m.type, m.rows, m.cols);
+        return false;
+    }
+    if (!launch_bgemm(g, st)) return false;
+    BFinishArgs f;
+    f.part = part;
+    f.part2 = part2_src;
+    f.ksplit = g.ksplit;
+    f.B = b->B;
+    f.rows = m.rows;
+    f.oscale = b->sx + (size_t)b->max_batch * (b->kmax / 16);
+    f.bias = bias;
+    f.epi = epi;
+    f.out = out;
+    f.ldo = ldo;
+    f.keys = keys;
+    return launch_bfinish(f, st);
+}
+
+bool batch_enqueue_step(llamini_batch* b, cudaStream_t st) {
+    llamini_session* s = b->w;
+    const bool gpt2 = s->kind == 1;
+    const u32 qkvd = s->qd + 2 * s->kvd;
+    BEmbedArgs e;
+    e.st = b->st;
+    e.tokens = b->tokens;
+    e.tok_stride = b->max_seq + 1;
+    e.tok = s->tok;
+    e.pos = s->pos_tab;
+    e.scale = s->emb_scale;
+    e.hidden = b->hidden;
+    e.dim = s->dim;
+    if (!launch_bembed(e, b->B, st)) return false;
+    const size_t per_seq = batch_cache_bytes_per_seq(b);
+    for (u32 l = 0; l < s->n_layers; l++) {
+        const llamini_session::Layer& W = s->layers[l];
+        if (!batch_stage(b, b->hidden, s->dim, gpt2 ? NORM_LAYER : NORM_RMS, W.n1w, W.n1b, st)) return false;
+        if (gpt2) {
+            if (!batch_linear(b, W.q, s->dim, b->part, nullptr, EPI_STORE, W.bq, b->qkv, qkvd, nullptr, st)) return false;
+        } else {
+            if (!batch_linear(b, W.q, s->dim, b->part, nullptr, EPI_STORE, W.bq, b->qkv, qkvd, nullptr, st) ||
+                !batch_linear(b, W.k, s->dim, b->part, nullptr, EPI_STORE, W.bk, b->qkv + s->qd, qkvd, nullptr, st) ||
+                !batch_linear(b, W.v, s->dim, b->part, nullptr, EPI_STORE, W.bv, b->qkv + s->qd + s->kvd, qkvd, nullptr, st))
+                return false;
+        }
+        AttnArgs at;
+        at.st = b->st;
+        at.qkv = b->qkv;
+        at.kc = (uint8_t*)b->kc + (size_t)l * b->max_batch * per_seq;
+        at.vc = (uint8_t*)b->vc + (size_t)l * b->max_batch * per_seq;
+        at.kv_f16 = b->kv_f16;
+        at.out = b->attn;
+        at.part = b->apart;
+        at.counter = b->counters;
+        at.n_heads = s->n_heads;
+        at.n_kv = s->n_kv;
+        at.hd = s->hd;
+        at.max_seq = b->max_seq;
+        at.n_split = b->n_split;
+        at.rope = s->rope_mode;
+        at.theta = s->theta;
+        AttnBatch ab;
+        ab.qkv_stride = qkvd;
+        ab.cache_stride = per_seq;
+        ab.out_stride = s->qd;
+        ab.part_stride = (uint64_t)s->n_heads * b->n_split * (s->hd + 4);
+        if (!launch_attention_batch(at, ab, b->B, st)) return false;
+        if (!batch_stage(b, b->attn, s->qd, NORM_NONE, nullptr, nullptr, st) ||
+            !batch_linear(b, W.o, s->qd, b->part, nullptr, EPI_RESID, W.bo, b->hidden, s->dim, nullptr, st))
+            return false;
+        if (!batch_stage(b, b->hidden, s->dim, gpt2 ? NORM_LAYER : NORM_RMS, W.n2w, W.n2b, st)) return false;
+        if (gpt2) {
+            if (!batch_linear(b, W.up, s->dim, b->part, nullptr, EPI_GELU, W.bup, b->ffn_h, s->ffn, nullptr, st))
+                return false;
+        } else {
+            BGemmArgs gu;
+            if (!batch_gemm(b, W.up, s->dim, b->part2, &gu)) {
+                set_error("batched decode: matrix format %u has no batched kernel", W.up.type);
+                return false;
+            }
+            if (!launch_bgemm(gu, st)) return false;
+            // the gate GEMM's finish combines both: act(gate) * up (model.c:14-25)
+            BGemmArgs gg;
+            if (!batch_gemm(b, W.gate, s->dim, b->part, &gg) || gg.ksplit != gu.ksplit) {
+                set_error("batched decode: gate/up plans differ");
+                return false;
+            }
+            if (!batch_linear(b, W.gate, s->dim, b->part, b->part2,
+                              s->act_gelu ? (u32)EPI_GLU_GELU : (u32)EPI_GLU_SILU, nullptr, b->ffn_h, s->ffn, nullptr, st))
+                return false;
+        }
+        if (!batch_stage(b, b->ffn_h, s->ffn, NORM_NONE, nullptr, nullptr, st) ||
+            !batch_linear(b, W.down, s->ffn, b->part, nullptr, EPI_RESID, W.bdown, b->hidden, s->dim, nullptr, st))
+            return false;
+    }
+    if (!batch_stage(b, b->hidden, s->dim, gpt2 ? NORM_LAYER : NORM_RMS, s->fnw, s->fnb, st) ||
+        !batch_linear(b, s->head, s->dim, b->part, nullptr, EPI_STORE, nullptr, b->logits, s->vocab, b->keys, st))
+        return false;
+    BTokenArgs t;
+    t.st = b->st;
+    t.tokens = b->tokens;
+    t.tok_stride = b->max_seq + 1;
+    t.n_prompt = b->n_prompt;
+    t.keys = b->keys;
+    t.B = b->B;
+    t.max_tokens = b->max_seq + 1;
+    return launch_btoken(t, st);
+}
+
+bool batch_capture(llamini_batch* b, u32 steps, cudaGraphExec_t* out) {
+    cudaStream_t st = stream();
+    cudaGraph_t g = nullptr;
+    if (!LM_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal))) return false;
+    bool ok = true;
+    for (u32 i = 0; i < steps && ok; i++) ok = batch_enqueue_step(b, st);
+    cudaError_t e = cudaStreamEndCapture(st, &g);
+    if (!ok || !LM_CUDA(e)) { if (g) cudaGraphDestroy(g); return false; }
+    ok = LM_CUDA(cudaGraphInstantiate(out, g, 0));
+    cudaGraphDestroy(g);
+    return ok;
+}
+
+void batch_destroy(llamini_batch* b) {
+    if (!b) return;
+    cudaStreamSynchronize(stream());
+    if (b->g_one) cudaGraphExecDestroy(b->g_one);
+    if (b->g_many) cudaGraphExecDestroy(b->g_many);
+    destroy(b->w);
+    delete b;
+}
+
+// Buffers for max_batch sequences; the GEMM plans (and so the partial-sum
+// buffer) are sized for the largest batch.
+bool batch_alloc(llamini_batch* b) {
+    llamini_session* s = b->w;
+    const u32 MB = b->max_batch;
+    b->kmax = s->dim;
+    if (s->qd > b->kmax) b->kmax = s->qd;
+    if (s->ffn > b->kmax) b->kmax = s->ffn;
+    b->kmax = (b->kmax + 255) & ~255u;
+    b->kv_f16 = g_kv_f16 ? 1u : 0u;
+    const u32 hb = s->n_heads * MB;
+    u32 ns = (u32)(2 * sm_count()) / (hb ? hb : 1);
+    if (ns < 1) ns = 1;
+    if (ns > 32) ns = 32;
+    const u32 by_len = (b->max_seq + 63) / 64;
+    if (ns > by_len) ns = by_len;
+    b->n_split = ns ? ns : 1;
+    // partial sums: the largest plan over the step's matrices at the full batch
+    b->B = MB;
+    size_t pmax = 0;
+    auto need = [&](const DevMat& m, u32 K) -> bool {
+        BGemmArgs g;
+        if (!batch_gemm(b, m, K, nullptr, &g)) {
+            set_error("batched decode: matrix format %u (%u x %u) has no batched kernel", m.type, m.rows, m.cols);
+            return false;
+        }
+        const size_t n = (size_t)g.ksplit * MB * m.rows;
+        pmax = pmax > n ? pmax : n;
+        return true;
+    };
+    bool ok = need(s->head, s->dim);
+    for (u32 l = 0; ok && l < s->n_layers; l++) {
+        const auto& W = s->layers[l];
+        ok = need(W.q, s->dim) && need(W.o, s->qd) && need(W.up, s->dim) && need(W.down, s->ffn) &&
+             (s->kind == 1 || (need(W.k, s->dim) && need(W.v, s->dim) && need(W.gate, s->dim)));
+    }
+    if (!ok) return false;
+    b->part_floats = pmax;
+    const size_t per_seq = batch_cache_bytes_per_seq(b);
+    const size_t cache = (size_t)s->n_layers * MB * per_seq;
+    b->hidden = (float*)own(s, (size_t)MB * s->dim * 4);
+    b->qkv = (float*)own(s, (size_t)MB * (s->qd + 2 * s->kvd) * 4);
+    b->attn = (float*)own(s, (size_t)MB * s->qd * 4);
+    b->ffn_h = (float*)own(s, (size_t)MB * s->ffn * 4);
+    b->logits = (float*)own(s, (size_t)MB * s->vocab * 4);
+    b->xh = (uint16_t*)own(s, (size_t)MB * b->kmax * 2);
+    b->xl = (uint16_t*)own(s, (size_t)MB * b->kmax * 2);
+    b->sx = (float*)own(s, ((size_t)MB * (b->kmax / 16) + MB) * 4);
+    b->part = (float*)own(s, pmax * 4);
+    b->part2 = (float*)own(s, pmax * 4);
+    b->apart = (float*)own(s, (size_t)MB * s->n_heads * b->n_split * (s->hd + 4) * 4);
+    b->counters = (u32*)own(s, (size_t)MB * s->n_heads * 4);
+    b->tokens = (u32*)own(s, (size_t)MB * (b->max_seq + 1) * 4);
+    b->n_prompt = (u32*)own(s, (size_t)MB * 4);
+    b->keys = (unsigned long long*)own(s, (size_t)MB * 8);
+    b->kc = own(s, cache);
+    b->vc = own(s, cache);
+    b->st = (StepState*)own(s, sizeof(StepState));
+    if (!b->hidden || !b->qkv || !b->attn || !b->ffn_h || !b->logits || !b->xh || !b->xl || !b->sx || !b->part ||
+        !b->part2 || !b->apart || !b->counters || !b->tokens || !b->n_prompt || !b->keys || !b->kc || !b->vc || !b->st)
+        return false;
+    return LM_CUDA(cudaMemset(b->counters, 0, (size_t)MB * s->n_heads * 4)) &&
+           LM_CUDA(cudaMemset(b->keys, 0, (size_t)MB * 8)) && LM_CUDA(cudaMemset(b->st, 0, sizeof(StepState))) &&
+           LM_CUDA(cudaMemset(b->tokens, 0, (size_t)MB * (b->max_seq + 1) * 4)) &&
+           LM_CUDA(cudaMemset(b->kc, 0, cache)) && LM_CUDA(cudaMemset(b->vc, 0, cache));
+}
+
+template <class M, class Bind>
+llamini_batch* batch_create(M* model, u32 max_batch, u32 max_seq, Bind bind) {
+    if (!ensure_device()) return nullptr;
+    if (max_batch == 0 || max_batch > 64) { set_error("batched decode: batch %u outside 1..64", max_batch); return nullptr; }
+    if (max_seq == 0) { set_error("batched decode: max_seq 0"); return nullptr; }
+    auto* b = new llamini_batch();
+    b->w = new llamini_session();
+    b->max_batch = max_batch;
+    b->max_seq = max_seq;
+    if (!bind(b->w, model, max_seq) || !batch_alloc(b)) { batch_destroy(b); return nullptr; }
+    b->B = 0;
+    return b;
+}
+
+bool batch_run(llamini_batch* b, u32 n) {
+    if ((u64)b->pos + n > b->w->max_pos) {
+        set_error("batched decode: position %u + %u steps passes the capacity %u", b->pos, n, b->w->max_pos);
+        return false;
+    }
+    cudaStream_t st = stream();
+    if (b->plan_B != b->B) {
+        if (b->g_one) { cudaGraphExecDestroy(b->g_one); b->g_one = nullptr; }
+        if (b->g_many) { cudaGraphExecDestroy(b->g_many); b->g_many = nullptr; }
+        if (!batch_capture(b, 1, &b->g_one) || !batch_capture(b, kBatchStepsPerGraph, &b->g_many)) return false;
+        b->plan_B = b->B;
+    }
+    u32 left = n;
+    while (left >= kBatchStepsPerGraph) {
+        if (!LM_CUDA(cudaGraphLaunch(b->g_many, st))) return false;
+        left -= kBatchStepsPerGraph;
+    }
+    while (left--) if (!LM_CUDA(cudaGraphLaunch(b->g_one, st))) return false;
+    b->pos += n;
+    return true;
+}
+
+}  // namespace
+}  // namespace lm
+
 extern "C" {
 
 void forward_step(LLaMAModel* model, KVCache* caches, u32 pos, u32 token_id, f32* logits_out) {
@@ -880,5 +1214,77 @@ int llamini_session_trace_read(llamini_session* s, f32* out) {
                    LM_CUDA(cudaStreamSynchronize(lm::stream()))
                ? 0 : -1;
 }
+
+
+// ---------------------------------------------------------------- batched decode
+
+llamini_batch* llamini_llama_batch(LLaMAModel* model, u32 max_batch, u32 max_seq) {
+    if (!model) { lm::set_error("batched decode: null model"); return nullptr; }
+    return lm::batch_create(model, max_batch, max_seq, lm::bind_llama);
+}
+
+llamini_batch* llamini_gpt2_batch(GPT2Model* model, u32 max_batch, u32 max_seq) {
+    if (!model) { lm::set_error("batched decode: null model"); return nullptr; }
+    return lm::batch_create(model, max_batch, max_seq, lm::bind_gpt2);
+}
+
+int llamini_batch_begin(llamini_batch* b, u32 n_seq, const u32* prompts, const u32* prompt_lens) {
+    if (!b || !prompts || !prompt_lens) { lm::set_error("batched decode: null argument"); return -1; }
+    if (n_seq == 0 || n_seq > b->max_batch) {
+        lm::set_error("batched decode: %u sequences, created for 1..%u", n_seq, b->max_batch);
+        return -1;
+    }
+    cudaStream_t st = lm::stream();
+    if (!LM_CUDA(cudaStreamSynchronize(st))) return -1;
+    const u32 stride = b->max_seq + 1;
+    std::vector<u32> toks((size_t)n_seq * stride, 0u), lens(n_seq);
+    size_t off = 0;
+    for (u32 i = 0; i < n_seq; i++) {
+        const u32 L = prompt_lens[i];
+        if (L == 0 || L > b->max_seq) { lm::set_error("batched decode: prompt %u has length %u", i, L); return -1; }
+        memcpy(&toks[(size_t)i * stride], prompts + off, (size_t)L * 4);
+        off += L;
+        lens[i] = L;
+    }
+    b->B = n_seq;
+    b->lens = lens;
+    b->pos = 0;
+    lm::StepState z;
+    memset(&z, 0, sizeof(z));
+    if (!LM_CUDA(cudaMemcpy(b->tokens, toks.data(), toks.size() * 4, cudaMemcpyHostToDevice)) ||
+        !LM_CUDA(cudaMemcpy(b->n_prompt, lens.data(), (size_t)n_seq * 4, cudaMemcpyHostToDevice)) ||
+        !LM_CUDA(cudaMemcpy(b->st, &z, sizeof(z), cudaMemcpyHostToDevice)) ||
+        !LM_CUDA(cudaMemset(b->keys, 0, (size_t)b->max_batch * 8)))
+        return -1;
+    return 0;
+}
+
+int llamini_batch_step(llamini_batch* b, u32 n_steps) {
+    if (!b || b->B == 0) { lm::set_error("batched decode: no batch begun"); return -1; }
+    return lm::batch_run(b, n_steps) ? 0 : -1;
+}
+
+int llamini_batch_tokens(llamini_batch* b, u32 seq, u32* out, u32 n) {
+    if (!b || !out || seq >= b->B) { lm::set_error("batched decode: bad sequence index"); return -1; }
+    if (!LM_CUDA(cudaStreamSynchronize(lm::stream()))) return -1;
+    const u32 have = b->pos + 1 > b->lens[seq] ? b->pos + 1 : b->lens[seq];
+    const u32 k = n < have ? n : have;
+    if (!LM_CUDA(cudaMemcpy(out, b->tokens + (size_t)seq * (b->max_seq + 1), (size_t)k * 4, cudaMemcpyDeviceToHost)))
+        return -1;
+    return (int)have;
+}
+
+int llamini_batch_logits(llamini_batch* b, u32 seq, f32* out) {
+    if (!b || !out || seq >= b->B) { lm::set_error("batched decode: bad sequence index"); return -1; }
+    if (!LM_CUDA(cudaStreamSynchronize(lm::stream()))) return -1;
+    return LM_CUDA(cudaMemcpy(out, b->logits + (size_t)seq * b->w->vocab, (size_t)b->w->vocab * 4,
+                              cudaMemcpyDeviceToHost)) ? 0 : -1;
+}
+
+u32 llamini_batch_pos(llamini_batch* b) { return b ? b->pos : 0; }
+
+u64 llamini_batch_weight_bytes(llamini_batch* b) { return b ? b->w->weight_bytes : 0; }
+
+void llamini_batch_free(llamini_batch* b) { lm::batch_destroy(b); }
 
 }  // extern "C"

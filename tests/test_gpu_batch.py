@@ -1,0 +1,115 @@
+"""Batched decode (llamini_*_batch) on the GPU.
+
+Every sequence of a batch must decode exactly as it would alone: its greedy
+token stream equals the single-sequence path's (and, for the golden prompts, the
+reference's own stream), and its logits stay within the 1e-3 bar of the CPU
+oracle. Prompts are ragged, so sequences switch from prompt to generated tokens
+at different steps of the lockstep batch.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+
+
+def _batch(gpu, m, max_batch, max_seq):
+    L = gpu.lib()
+    fn = L.llamini_gpt2_batch if m.is_gpt2 else L.llamini_llama_batch
+    b = fn(C.byref(m.model), max_batch, max_seq)
+    assert b, gpu.last_error()
+    return b
+
+
+def _begin(gpu, b, prompts):
+    flat = np.concatenate([np.asarray(p, np.uint32) for p in prompts])
+    lens = np.array([len(p) for p in prompts], np.uint32)
+    assert gpu.lib().llamini_batch_begin(b, len(prompts), gpu.ptr(flat), gpu.ptr(lens)) == 0, gpu.last_error()
+
+
+def _tokens(gpu, b, seq, n):
+    out = np.zeros(n, np.uint32)
+    k = gpu.lib().llamini_batch_tokens(b, seq, gpu.ptr(out), n)
+    assert k >= 0, gpu.last_error()
+    return out[:min(k, n)].tolist()
+
+
+@pytest.mark.parametrize("name", ["tiny_llama", "tiny_tied", "tiny_gpt2"])
+def test_batch_streams_equal_single_sequence(gpu, orc, tiny, golden, name):
+    path = tiny.ensure(name)
+    m = gpu.Model(path)
+    L = gpu.lib()
+    g = golden["tokens"][name]
+    rng = np.random.default_rng(7)
+    vocab = m.vocab
+    prompts = [g["prompt"], rng.integers(3, vocab, 3).tolist(), rng.integers(3, vocab, 9).tolist(),
+               [1], rng.integers(3, vocab, 16).tolist()]
+    steps = min(m.max_seq, 48) - 1
+    b = _batch(gpu, m, 8, m.max_seq)
+    try:
+        _begin(gpu, b, prompts)
+        assert L.llamini_batch_step(b, steps) == 0, gpu.last_error()
+        assert L.llamini_batch_pos(b) == steps
+        for s, p in enumerate(prompts):
+            got = _tokens(gpu, b, s, steps + 1)
+            assert len(got) == steps + 1
+            alone = m.generate(np.array(p, np.uint32), steps + 1 - len(p)).tolist()
+            assert got == alone[:steps + 1], (s, got, alone)
+        ref = g["tokens"]
+        n = min(len(ref), steps + 1)
+        assert _tokens(gpu, b, 0, n) == ref[:n]
+        # logits of the last step against the oracle, teacher-forced on the stream
+        o = orc.oracle_model(path)
+        for s in (0, 3):
+            toks = _tokens(gpu, b, s, steps + 1)
+            want = None
+            for pos in range(steps):
+                want = o.forward(pos, toks[pos])
+            lg = np.zeros(vocab, np.float32)
+            assert L.llamini_batch_logits(b, s, gpu.ptr(lg)) == 0
+            assert rel_l2(lg, want) < TOL, (s, rel_l2(lg, want))
+    finally:
+        L.llamini_batch_free(b)
+        m.close()
+
+
+def test_batch_rejects_unsupported_formats(gpu, tiny):
+    m = gpu.Model(tiny.ensure("tiny_mixed"))       # Q4_1, Q5_0, Q5_K matrices
+    try:
+        assert not gpu.lib().llamini_llama_batch(C.byref(m.model), 4, 32)
+        assert "batched" in gpu.last_error()
+        gpu.lib().llamini_clear_error()
+    finally:
+        m.close()
+
+
+@pytest.mark.parametrize("name", ["llama_1b", "gpt2_124m"])
+def test_batch_workload_golden_stream(gpu, synth, golden, name):
+    """Full-size workloads, 4 sequences: the golden prompt's stream equals the
+    reference's for 24 generated tokens; the others equal the single path."""
+    g = golden["tokens"][name]
+    m = gpu.Model(synth.ensure_workload(name), max_seq=512)
+    L = gpu.lib()
+    rng = np.random.default_rng(3)
+    prompts = [g["prompt"], rng.integers(3, m.vocab, 40).tolist(), rng.integers(3, m.vocab, len(g["prompt"])).tolist(),
+               rng.integers(3, m.vocab, 5).tolist()]
+    steps = len(g["prompt"]) - 1 + 24
+    b = _batch(gpu, m, 4, 512)
+    try:
+        _begin(gpu, b, prompts)
+        assert L.llamini_batch_step(b, steps) == 0, gpu.last_error()
+        assert _tokens(gpu, b, 0, steps + 1) == g["tokens"][:steps + 1]
+        for s in (1, 3):
+            got = _tokens(gpu, b, s, steps + 1)
+            alone = m.generate(np.array(prompts[s], np.uint32), steps + 1 - len(prompts[s])).tolist()
+            assert got == alone[:steps + 1], s
+    finally:
+        L.llamini_batch_free(b)
+        m.close()
