@@ -16,6 +16,9 @@ quantized blocks) exceed the 126 MB L2, so every step streams them from HBM.
           bandwidth in MEASURED_PEAKS.json
   cpu_baseline  the reference's own C (oracle/_ref) on the host cores, a bounded
           sample of the same decode loop
+  batch64 the batch-64 side of the metric: 64 independent llama_1b sequences
+          (64 / N per GPU) after 128-token prompts, every weight matrix read once
+          per step for the whole batch; tok/s of all sequences over K' timed steps
 
 With --gpus N (torchrun) every rank decodes its own sequence (independent
 replicas; the path has no cross-sequence exchange) and value sums the ranks.
@@ -215,6 +218,44 @@ def step_kernel_roofline(decode_kernel, step_bytes, t_ms, steps, hbm_peak, peak_
             "us_per_step": round(t_ms * 1e3 / steps, 2), "traffic": None}
 
 
+GLOBAL_BATCH = 64
+
+
+def run_batch(args, lm, L, model, torch, stream, ws, rank, dist, hbm_peak):
+    """Batched decode: 64 sequences in all (64 / N per rank, independent), each
+    after its own 128-token prompt; K timed steps of every sequence. Returns this
+    rank's device time and the per-step byte count, or None when skipped."""
+    B = max(1, GLOBAL_BATCH // ws)
+    max_seq = 512
+    b = L.llamini_llama_batch(C.byref(model.model), B, max_seq)
+    if not b:
+        raise RuntimeError("batch: " + lm.last_error())
+    try:
+        rng = np.random.default_rng(1000 + rank)
+        prompts = rng.integers(3, model.vocab, (B, args.prompt)).astype(np.uint32)
+        lens = np.full(B, args.prompt, np.uint32)
+        assert L.llamini_batch_begin(b, B, lm.ptr(prompts), lm.ptr(lens)) == 0, lm.last_error()
+        assert L.llamini_batch_step(b, args.prompt - 1 + args.warmup) == 0, lm.last_error()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        pos0 = L.llamini_batch_pos(b)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        assert L.llamini_batch_step(b, args.batch_steps) == 0, lm.last_error()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        out = np.zeros(4, np.uint32)
+        assert L.llamini_batch_tokens(b, 0, lm.ptr(out), 4) > 0
+        weight_bytes = L.llamini_batch_weight_bytes(b)
+    finally:
+        L.llamini_batch_free(b)
+    kv_per_pos = L.llamini_session_kv_bytes_per_pos(model.session())
+    ctx_mean = pos0 + (args.batch_steps - 1) / 2 + 1
+    return ms, weight_bytes + B * kv_per_pos * ctx_mean, B
+
+
 def run_ours(args, ws, rank, local):
     import torch
     dist = init_dist(ws, local, "nccl")
@@ -263,7 +304,9 @@ def run_ours(args, ws, rank, local):
         gemv_roof = None
         if rank == 0 and not args.no_kernel_roofline:
             gemv_roof = kernel_roofline(lm, torch, stream, hbm_peak, peak_kind)
+        bt = None if args.no_batch else run_batch(args, lm, L, model, torch, stream, ws, rank, dist, hbm_peak)
     t_max, e2e_max = max_over_ranks(dist, [ms, e2e_s])
+    b_max = max_over_ranks(dist, [bt[0]])[0] if bt else None
     if rank == 0:
         steps = args.steps
         value = whole_job_rate(ws, steps, t_max)
@@ -296,6 +339,18 @@ def run_ours(args, ws, rank, local):
             "step_kernel": "decode_kernel (persistent, whole step)" if decode_kernel else "per-op graph",
             "clocks": clk.summary(),
         }
+        if bt:
+            b_ms, b_bytes, b_per = bt[0], bt[1], bt[2]
+            b_step_s = b_max / 1e3 / args.batch_steps
+            line["batch64"] = {
+                "value": round(whole_job_rate(ws * b_per, args.batch_steps, b_max), 1), "unit": "tok/s",
+                "global_batch": ws * b_per, "per_gpu_batch": b_per, "steps": args.batch_steps,
+                "ms_per_step": round(b_max / args.batch_steps, 4), "scaling": "strong",
+                "workload": "llama_1b, %d independent sequences per GPU, %d-token prompts (seeded uniform ids), "
+                            "timed decode steps after the prompt" % (b_per, args.prompt),
+                "weight_stream_gbs": round(b_bytes / b_step_s / 1e9, 1),
+                "frac_of_hbm": round(b_bytes / b_step_s / 1e9 / hbm_peak, 4),
+                "gpu_launches": args.batch_steps * (1 + 22 * 18 + 3 + 1)}
         if ws == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(path)
         print(json.dumps(line), flush=True)
@@ -388,6 +443,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the generate_autoregressive timing")
     ap.add_argument("--no-kernel-roofline", action="store_true", help="skip the isolated GEMV timing")
     ap.add_argument("--prompt", type=int, default=N_PROMPT, help="prompt length before the timed steps")
+    ap.add_argument("--no-batch", action="store_true", help="skip the batch-64 decode timing")
+    ap.add_argument("--batch-steps", type=int, default=32, help="timed steps of the batch-64 leg")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
