@@ -350,7 +350,9 @@ def run_ours(args, ws, rank, local):
                             "timed decode steps after the prompt" % (b_per, args.prompt),
                 "weight_stream_gbs": round(b_bytes / b_step_s / 1e9, 1),
                 "frac_of_hbm": round(b_bytes / b_step_s / 1e9 / hbm_peak, 4),
-                "gpu_launches": args.batch_steps * (1 + 22 * 18 + 3 + 1)}
+                # per step: embed; per layer 4 stagings, 4 GEMMs (qkv, o, gate+up, down),
+                # 6 finishes, attention; lm_head staging + GEMM + finish; token update
+                "gpu_launches": args.batch_steps * (1 + 22 * 15 + 3 + 1)}
         if ws == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(path)
         print(json.dumps(line), flush=True)

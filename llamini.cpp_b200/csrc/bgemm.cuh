@@ -18,6 +18,8 @@ constexpr uint32_t kBMaxQuads = 16;       // 64 input vectors
 
 // Staged input of the CTA's current K unit in shared memory: fp16 hi and lo of
 // x * 2^E per sequence (row stride xs halves) and 16-element sums (stride sxs).
+// Within every aligned group of 4 elements the halves are stored in fragment
+// order (e, e+2, e+1, e+3), so a lane's 8-byte load is its B fragment as is.
 struct BX {
     const uint16_t* h;
     const uint16_t* l;
@@ -34,7 +36,14 @@ struct BLane {
 __device__ __forceinline__ BFrag bq(const BX& X, const BLane& L, uint32_t q, uint32_t e0) {
     const uint16_t* p = ((L.g & 1u) ? X.l : X.h) + (4 * q + (L.g >> 1)) * X.xs + e0;
     const uint2 v = *reinterpret_cast<const uint2*>(p);
-    return BFrag{__byte_perm(v.x, v.y, 0x5410), __byte_perm(v.x, v.y, 0x7632)};
+    return BFrag{v.x, v.y};
+}
+// Both fragments of elements e0..e0+7 (e0 % 8 == 0) in one 16-byte load.
+__device__ __forceinline__ void bq2(const BX& X, const BLane& L, uint32_t q, uint32_t e0, BFrag& f0, BFrag& f1) {
+    const uint16_t* p = ((L.g & 1u) ? X.l : X.h) + (4 * q + (L.g >> 1)) * X.xs + e0;
+    const uint4 v = *reinterpret_cast<const uint4*>(p);
+    f0 = BFrag{v.x, v.y};
+    f1 = BFrag{v.z, v.w};
 }
 __device__ __forceinline__ float bsx(const BX& X, const BLane& L, uint32_t q, uint32_t i16) {
     return X.sx[(4 * q + L.tig) * X.sxs + i16];
@@ -68,8 +77,9 @@ __device__ __forceinline__ void bq4k(const uint8_t* bg, const uint8_t* bg8, uint
 #pragma unroll
         for (uint32_t qq = 0; qq < NQ; qq++) {
             if (qq < nq) {
-                const BFrag f0 = bq(X, L, qq, e), f1 = bq(X, L, qq, e + 4);
-                const BFrag g0 = bq(X, L, qq, e + 32), g1 = bq(X, L, qq, e + 36);
+                BFrag f0, f1, g0, g1;
+                bq2(X, L, qq, e, f0, f1);
+                bq2(X, L, qq, e + 32, g0, g1);
                 float cl[4] = {0.f, 0.f, 0.f, 0.f}, ch[4] = {0.f, 0.f, 0.f, 0.f};
                 mma16816(cl, w0 & 0x000F000Fu, v0 & 0x000F000Fu, w0s & 0x000F000Fu, v0s & 0x000F000Fu, f0.b0, f0.b1);
                 mma16816(cl, w1 & 0x000F000Fu, v1 & 0x000F000Fu, w1s & 0x000F000Fu, v1s & 0x000F000Fu, f1.b0, f1.b1);

@@ -244,6 +244,7 @@ struct BSeg {
     uint32_t type = 0, rows = 0;
     uint32_t rb0 = 0;              // first row block (filled by bgemm_plan)
     float* part = nullptr;         // [ksplit][B][rows] raw sums
+    uint32_t ub = 0, wrs = 0;      // bytes per K unit, shared-memory row stride (filled by bgemm_plan)
 };
 struct BGemmArgs {
     const uint16_t* xh = nullptr;
@@ -252,8 +253,10 @@ struct BGemmArgs {
     uint32_t B = 0, K = 0;
     uint32_t nseg = 0;
     BSeg seg[3];
-    // filled by bgemm_plan
-    uint32_t ue = 0, ub = 0, ups = 0, ksplit = 0, rblocks = 0, wrs = 0, xs = 0, bpad = 0;
+    // filled by bgemm_plan: unit elements, units per split, K split, row blocks,
+    // largest weight row stride, input row stride (halves), padded batch, byte
+    // offset of the low halves from the high halves in a buffer
+    uint32_t ue = 0, ups = 0, ksplit = 0, rblocks = 0, wrs = 0, xs = 0, bpad = 0, xlo = 0;
 };
 struct BFinishArgs {
     const float* part = nullptr;   // [ksplit][B][rows]

@@ -117,12 +117,19 @@ __global__ void __launch_bounds__(256) bstage_kernel(const BStageArgs a) {
         rs += __shfl_xor_sync(0xffffffffu, rs, 1);
         rs += __shfl_xor_sync(0xffffffffu, rs, 2);
         if (i < n4) {
+            // fragment order within the 4-group: elements 0, 2, 1, 3
+            __half h[4], l[4];
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-                const __half h = __float2half_rn(v[j]);
-                xh[4 * i + j] = h;
-                xl[4 * i + j] = __float2half_rn(v[j] - __half2float(h));
+                h[j] = __float2half_rn(v[j]);
+                l[j] = __float2half_rn(v[j] - __half2float(h[j]));
             }
+            const __half2 h0 = __halves2half2(h[0], h[2]), h1 = __halves2half2(h[1], h[3]);
+            const __half2 l0 = __halves2half2(l[0], l[2]), l1 = __halves2half2(l[1], l[3]);
+            reinterpret_cast<__half2*>(xh)[2 * i] = h0;
+            reinterpret_cast<__half2*>(xh)[2 * i + 1] = h1;
+            reinterpret_cast<__half2*>(xl)[2 * i] = l0;
+            reinterpret_cast<__half2*>(xl)[2 * i + 1] = l1;
             if ((i & 3u) == 0) sx[i >> 2] = rs;
         }
     }
@@ -138,21 +145,29 @@ struct BBuf {
     float* sx;
 };
 
-__device__ __forceinline__ BBuf bbuf(uint8_t* base, const BGemmArgs& a, uint32_t i) {
+__host__ __device__ __forceinline__ uint32_t bbuf_bytes(const BGemmArgs& a) {
     const uint32_t wbytes = kBRows * a.wrs;
     const uint32_t xbytes = a.bpad * a.xs * 2;
     const uint32_t sbytes = a.bpad * (a.ue / 16) * 4;
-    const uint32_t stride = (wbytes + 2 * xbytes + sbytes + 127) & ~127u;
-    uint8_t* p = base + i * stride;
-    return BBuf{p, reinterpret_cast<uint16_t*>(p + wbytes), reinterpret_cast<uint16_t*>(p + wbytes + xbytes),
-                reinterpret_cast<float*>(p + wbytes + 2 * xbytes)};
+    return (wbytes + a.xlo + ((xbytes + 15) & ~15u) + sbytes + 127) & ~127u;
+}
+
+// Buffer i: weight rows, then the high halves, the low halves a.xlo bytes
+// further (so hi and lo fall in different banks), then the 16-element sums.
+__device__ __forceinline__ BBuf bbuf(uint8_t* base, const BGemmArgs& a, uint32_t i) {
+    const uint32_t wbytes = kBRows * a.wrs;
+    const uint32_t xbytes = (a.bpad * a.xs * 2 + 15) & ~15u;
+    uint8_t* p = base + i * bbuf_bytes(a);
+    uint8_t* xh = p + wbytes;
+    return BBuf{p, reinterpret_cast<uint16_t*>(xh), reinterpret_cast<uint16_t*>(xh + a.xlo),
+                reinterpret_cast<float*>(xh + a.xlo + xbytes)};
 }
 
 // Issue the copies of K unit u into buffer `buf`.
 __device__ __forceinline__ void bstage_unit(const BGemmArgs& a, const BSeg& S, uint32_t row0, uint32_t u, const BBuf& buf) {
     const uint32_t tid = threadIdx.x;
     // weight rows: bytes [o, o + ub) of each row, from the 16-byte boundary below o
-    const uint32_t ub = a.ub;
+    const uint32_t ub = S.ub;
     const uint32_t pieces = (ub + 15) / 16 + 1;
     for (uint32_t i = tid; i < kBRows * pieces; i += kBThreads) {
         const uint32_t r = i / pieces, p = i - r * pieces;
@@ -160,7 +175,7 @@ __device__ __forceinline__ void bstage_unit(const BGemmArgs& a, const BSeg& S, u
         const uint64_t o = (uint64_t)(row0 + r) * S.row_bytes + (uint64_t)u * ub;
         const uint64_t a16 = o & ~uint64_t(15);
         if (a16 + 16 * p >= o + ub) continue;
-        cpa16(buf.w + r * a.wrs + 16 * p, S.w + a16 + 16 * p);
+        cpa16(buf.w + r * S.wrs + 16 * p, S.w + a16 + 16 * p);
     }
     // staged inputs of every sequence for elements [u * ue, (u + 1) * ue)
     const uint32_t xp = a.ue / 8;                          // 16-byte pieces per sequence
@@ -196,10 +211,10 @@ __device__ __forceinline__ void bcompute_unit(const BGemmArgs& a, const BSeg& S,
     X.xs = a.xs;
     X.sxs = a.ue / 16;
     const uint32_t nq = (a.B + 3) / 4;
-    const uint64_t ob = (uint64_t)u * a.ub;
+    const uint64_t ob = (uint64_t)u * S.ub;
     const uint32_t rg = rt + L.g, rg8 = rt + L.g + 8;
-    const uint8_t* bg = buf.w + (16 * warp + L.g) * a.wrs + (uint32_t)(((uint64_t)rg * S.row_bytes + ob) & 15u);
-    const uint8_t* bg8 = buf.w + (16 * warp + L.g + 8) * a.wrs + (uint32_t)(((uint64_t)rg8 * S.row_bytes + ob) & 15u);
+    const uint8_t* bg = buf.w + (16 * warp + L.g) * S.wrs + (uint32_t)(((uint64_t)rg * S.row_bytes + ob) & 15u);
+    const uint8_t* bg8 = buf.w + (16 * warp + L.g + 8) * S.wrs + (uint32_t)(((uint64_t)rg8 * S.row_bytes + ob) & 15u);
     switch (S.type) {
     case T_Q4_K: bq4k<NQ>(bg, bg8, 0, nq, L, X, acc); break;
     case T_Q6_K: bq6k<NQ>(bg, bg8, 0, nq, L, X, acc); break;
@@ -216,7 +231,7 @@ __device__ __forceinline__ void bcompute_unit(const BGemmArgs& a, const BSeg& S,
 }
 
 template <uint32_t NQ>
-__global__ void __launch_bounds__(kBThreads) bgemm_kernel(const __grid_constant__ BGemmArgs a) {
+__global__ void __launch_bounds__(kBThreads, 1) bgemm_kernel(const __grid_constant__ BGemmArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint32_t s = 0;
 #pragma unroll
@@ -322,12 +337,7 @@ static uint32_t unit_bytes(uint32_t type, uint32_t ue) {
     }
 }
 
-size_t bgemm_smem(const BGemmArgs& a) {
-    const size_t wbytes = (size_t)kBRows * a.wrs;
-    const size_t xbytes = (size_t)a.bpad * a.xs * 2;
-    const size_t sbytes = (size_t)a.bpad * (a.ue / 16) * 4;
-    return 2 * ((wbytes + 2 * xbytes + sbytes + 127) & ~size_t(127));
-}
+size_t bgemm_smem(const BGemmArgs& a) { return 2 * (size_t)bbuf_bytes(a); }
 
 constexpr size_t kBSmemMax = 226 * 1024;
 
@@ -348,7 +358,7 @@ bool bgemm_plan(BGemmArgs& a, uint32_t target_ctas) {
     bool kquant = false;
     for (uint32_t i = 0; i < a.nseg; i++) {
         BSeg& S = a.seg[i];
-        if (!bgemm_type(S.type) || S.type != a.seg[0].type) return false;
+        if (!bgemm_type(S.type)) return false;
         if (reinterpret_cast<uintptr_t>(S.w) % 16 != 0) return false;
         if (S.type == T_F16 && a.K % 4 != 0) return false;
         kquant = kquant || S.type == T_Q4_K || S.type == T_Q6_K;
@@ -360,11 +370,22 @@ bool bgemm_plan(BGemmArgs& a, uint32_t target_ctas) {
     for (uint32_t ue = units_max; ue >= 32; ue /= 8) {     // 256, then 32 for block formats
         if (kquant && ue != 256) return false;
         a.ue = ue;
-        a.ub = unit_bytes(a.seg[0].type, a.ue);
-        uint32_t wrs = (a.ub + 15 + 16 + 15) & ~15u;       // slack: alignment delta + word reads
-        if ((wrs / 16) % 2 == 0) wrs += 16;               // odd number of 16-byte units: rows spread over banks
-        a.wrs = wrs;
-        a.xs = a.ue + 8;
+        a.wrs = 0;
+        for (uint32_t i = 0; i < a.nseg; i++) {
+            BSeg& S = a.seg[i];
+            S.ub = unit_bytes(S.type, ue);
+            uint32_t wrs = (S.ub + 15 + 16 + 15) & ~15u;   // slack: alignment delta + word reads
+            if ((wrs / 16) % 2 == 0) wrs += 16;           // odd number of 16-byte units: rows spread over banks
+            S.wrs = wrs;
+            a.wrs = a.wrs > wrs ? a.wrs : wrs;
+        }
+        // input rows: a stride of 64 (mod 128) bytes between sequences, and the
+        // low halves 64 (Q4_K: one 16-byte load per lane) or 32 (8-byte loads)
+        // bytes (mod 128) after the high halves, so a warp's fragment loads
+        // fall in distinct banks
+        a.xs = a.ue % 64 == 0 ? a.ue + 32 : a.ue + 64;
+        const uint32_t xbytes = (a.bpad * a.xs * 2 + 15) & ~15u;
+        a.xlo = ((xbytes + 127) & ~127u) + (a.seg[0].type == T_Q4_K ? 64u : 32u);
         if (bgemm_smem(a) <= kBSmemMax) break;
         if (ue == 32) return false;
     }

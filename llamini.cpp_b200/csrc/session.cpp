@@ -827,7 +827,7 @@ struct llamini_batch {
     u32 max_batch = 0, max_seq = 0, B = 0;
     u32 n_split = 1, kv_f16 = 0, kmax = 0;
     float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *ffn_h = nullptr, *logits = nullptr;
-    float *sx = nullptr, *part = nullptr, *part2 = nullptr, *apart = nullptr;
+    float *sx = nullptr, *part = nullptr, *part2 = nullptr, *part3 = nullptr, *apart = nullptr;
     uint16_t *xh = nullptr, *xl = nullptr;
     u32 *counters = nullptr, *tokens = nullptr, *n_prompt = nullptr;
     unsigned long long* keys = nullptr;
@@ -849,23 +849,32 @@ size_t batch_cache_bytes_per_seq(const llamini_batch* b) {
     return (size_t)b->w->n_kv * b->max_seq * b->w->hd * (b->kv_f16 ? 2 : 4);
 }
 
-// GEMM plan of one matrix for the current batch (false: format not supported)
-bool batch_gemm(const llamini_batch* b, const DevMat& m, u32 K, float* part, BGemmArgs* out) {
+// GEMM plan of up to three matrices that share an input (false: a format is
+// not supported); segment i writes its raw sums to parts[i].
+bool batch_gemm(const llamini_batch* b, const DevMat* const* m, float* const* parts, u32 n, u32 K, BGemmArgs* out) {
     BGemmArgs g;
     g.xh = b->xh;
     g.xl = b->xl;
     g.sx = b->sx;
     g.B = b->B;
     g.K = K;
-    g.nseg = 1;
-    g.seg[0].w = m.ptr;
-    g.seg[0].row_bytes = m.row_bytes;
-    g.seg[0].type = m.type;
-    g.seg[0].rows = m.rows;
-    g.seg[0].part = part;
-    if (m.cols != K || !bgemm_plan(g, 2u * (u32)sm_count())) return false;
+    g.nseg = n;
+    for (u32 i = 0; i < n; i++) {
+        if (m[i]->cols != K) return false;
+        g.seg[i].w = m[i]->ptr;
+        g.seg[i].row_bytes = m[i]->row_bytes;
+        g.seg[i].type = m[i]->type;
+        g.seg[i].rows = m[i]->rows;
+        g.seg[i].part = parts[i];
+    }
+    if (!bgemm_plan(g, 2u * (u32)sm_count())) return false;
     *out = g;
     return true;
+}
+bool batch_gemm(const llamini_batch* b, const DevMat& m, u32 K, float* part, BGemmArgs* out) {
+    const DevMat* mm[1] = {&m};
+    float* pp[1] = {part};
+    return batch_gemm(b, mm, pp, 1, K, out);
 }
 
 bool batch_stage(llamini_batch* b, const float* x, u32 K, u32 norm, const float* w, const float* bias, cudaStream_t st) {
@@ -883,6 +892,23 @@ bool batch_stage(llamini_batch* b, const float* x, u32 K, u32 norm, const float*
     a.sx = b->sx;
     a.oscale = b->sx + (size_t)b->max_batch * (b->kmax / 16);
     return launch_bstage(a, st);
+}
+
+bool batch_finish(llamini_batch* b, const BGemmArgs& g, u32 seg, const float* part2_src, uint32_t epi,
+                  const float* bias, float* out, u32 ldo, unsigned long long* keys, cudaStream_t st) {
+    BFinishArgs f;
+    f.part = g.seg[seg].part;
+    f.part2 = part2_src;
+    f.ksplit = g.ksplit;
+    f.B = b->B;
+    f.rows = g.seg[seg].rows;
+    f.oscale = b->sx + (size_t)b->max_batch * (b->kmax / 16);
+    f.bias = bias;
+    f.epi = epi;
+    f.out = out;
+    f.ldo = ldo;
+    f.keys = keys;
+    return launch_bfinish(f, st);
 }
 
 bool batch_linear(llamini_batch* b, const DevMat& m, u32 K, float* part, const float* part2_src, uint32_t epi,
@@ -929,9 +955,18 @@ bool batch_enqueue_step(llamini_batch* b, cudaStream_t st) {
         if (gpt2) {
             if (!batch_linear(b, W.q, s->dim, b->part, nullptr, EPI_STORE, W.bq, b->qkv, qkvd, nullptr, st)) return false;
         } else {
-            if (!batch_linear(b, W.q, s->dim, b->part, nullptr, EPI_STORE, W.bq, b->qkv, qkvd, nullptr, st) ||
-                !batch_linear(b, W.k, s->dim, b->part, nullptr, EPI_STORE, W.bk, b->qkv + s->qd, qkvd, nullptr, st) ||
-                !batch_linear(b, W.v, s->dim, b->part, nullptr, EPI_STORE, W.bv, b->qkv + s->qd + s->kvd, qkvd, nullptr, st))
+            // q, k and v share their input: one launch, three partial buffers
+            const DevMat* mm[3] = {&W.q, &W.k, &W.v};
+            float* pp[3] = {b->part, b->part2, b->part3};
+            BGemmArgs g;
+            if (!batch_gemm(b, mm, pp, 3, s->dim, &g)) {
+                set_error("batched decode: q/k/v formats have no batched kernel");
+                return false;
+            }
+            if (!launch_bgemm(g, st) ||
+                !batch_finish(b, g, 0, nullptr, EPI_STORE, W.bq, b->qkv, qkvd, nullptr, st) ||
+                !batch_finish(b, g, 1, nullptr, EPI_STORE, W.bk, b->qkv + s->qd, qkvd, nullptr, st) ||
+                !batch_finish(b, g, 2, nullptr, EPI_STORE, W.bv, b->qkv + s->qd + s->kvd, qkvd, nullptr, st))
                 return false;
         }
         AttnArgs at;
@@ -964,20 +999,17 @@ bool batch_enqueue_step(llamini_batch* b, cudaStream_t st) {
             if (!batch_linear(b, W.up, s->dim, b->part, nullptr, EPI_GELU, W.bup, b->ffn_h, s->ffn, nullptr, st))
                 return false;
         } else {
-            BGemmArgs gu;
-            if (!batch_gemm(b, W.up, s->dim, b->part2, &gu)) {
-                set_error("batched decode: matrix format %u has no batched kernel", W.up.type);
+            // gate and up in one launch; the finish combines act(gate) * up (model.c:14-25)
+            const DevMat* mm[2] = {&W.gate, &W.up};
+            float* pp[2] = {b->part, b->part2};
+            BGemmArgs g;
+            if (!batch_gemm(b, mm, pp, 2, s->dim, &g)) {
+                set_error("batched decode: gate/up formats have no batched kernel");
                 return false;
             }
-            if (!launch_bgemm(gu, st)) return false;
-            // the gate GEMM's finish combines both: act(gate) * up (model.c:14-25)
-            BGemmArgs gg;
-            if (!batch_gemm(b, W.gate, s->dim, b->part, &gg) || gg.ksplit != gu.ksplit) {
-                set_error("batched decode: gate/up plans differ");
-                return false;
-            }
-            if (!batch_linear(b, W.gate, s->dim, b->part, b->part2,
-                              s->act_gelu ? (u32)EPI_GLU_GELU : (u32)EPI_GLU_SILU, nullptr, b->ffn_h, s->ffn, nullptr, st))
+            if (!launch_bgemm(g, st) ||
+                !batch_finish(b, g, 0, b->part2, s->act_gelu ? (u32)EPI_GLU_GELU : (u32)EPI_GLU_SILU, nullptr,
+                              b->ffn_h, s->ffn, nullptr, st))
                 return false;
         }
         if (!batch_stage(b, b->ffn_h, s->ffn, NORM_NONE, nullptr, nullptr, st) ||
@@ -1040,21 +1072,34 @@ bool batch_alloc(llamini_batch* b) {
     // partial sums: the largest plan over the step's matrices at the full batch
     b->B = MB;
     size_t pmax = 0;
-    auto need = [&](const DevMat& m, u32 K) -> bool {
+    auto need = [&](const DevMat* const* mm, u32 n, u32 K) -> bool {
+        float* none[3] = {nullptr, nullptr, nullptr};
         BGemmArgs g;
-        if (!batch_gemm(b, m, K, nullptr, &g)) {
-            set_error("batched decode: matrix format %u (%u x %u) has no batched kernel", m.type, m.rows, m.cols);
+        if (!batch_gemm(b, mm, none, n, K, &g)) {
+            set_error("batched decode: matrix format %u (%u x %u) has no batched kernel", mm[0]->type, mm[0]->rows,
+                      mm[0]->cols);
             return false;
         }
-        const size_t n = (size_t)g.ksplit * MB * m.rows;
-        pmax = pmax > n ? pmax : n;
+        for (u32 i = 0; i < n; i++) {
+            const size_t m = (size_t)g.ksplit * MB * mm[i]->rows;
+            pmax = pmax > m ? pmax : m;
+        }
         return true;
     };
-    bool ok = need(s->head, s->dim);
+    auto need1 = [&](const DevMat& m, u32 K) -> bool {
+        const DevMat* mm[1] = {&m};
+        return need(mm, 1, K);
+    };
+    bool ok = need1(s->head, s->dim);
     for (u32 l = 0; ok && l < s->n_layers; l++) {
         const auto& W = s->layers[l];
-        ok = need(W.q, s->dim) && need(W.o, s->qd) && need(W.up, s->dim) && need(W.down, s->ffn) &&
-             (s->kind == 1 || (need(W.k, s->dim) && need(W.v, s->dim) && need(W.gate, s->dim)));
+        ok = need1(W.o, s->qd) && need1(W.down, s->ffn);
+        if (ok && s->kind == 1) ok = need1(W.q, s->dim) && need1(W.up, s->dim);
+        if (ok && s->kind == 0) {
+            const DevMat* qkv[3] = {&W.q, &W.k, &W.v};
+            const DevMat* gu[2] = {&W.gate, &W.up};
+            ok = need(qkv, 3, s->dim) && need(gu, 2, s->dim);
+        }
     }
     if (!ok) return false;
     b->part_floats = pmax;
@@ -1070,6 +1115,7 @@ bool batch_alloc(llamini_batch* b) {
     b->sx = (float*)own(s, ((size_t)MB * (b->kmax / 16) + MB) * 4);
     b->part = (float*)own(s, pmax * 4);
     b->part2 = (float*)own(s, pmax * 4);
+    b->part3 = (float*)own(s, pmax * 4);
     b->apart = (float*)own(s, (size_t)MB * s->n_heads * b->n_split * (s->hd + 4) * 4);
     b->counters = (u32*)own(s, (size_t)MB * s->n_heads * 4);
     b->tokens = (u32*)own(s, (size_t)MB * (b->max_seq + 1) * 4);
@@ -1079,7 +1125,7 @@ bool batch_alloc(llamini_batch* b) {
     b->vc = own(s, cache);
     b->st = (StepState*)own(s, sizeof(StepState));
     if (!b->hidden || !b->qkv || !b->attn || !b->ffn_h || !b->logits || !b->xh || !b->xl || !b->sx || !b->part ||
-        !b->part2 || !b->apart || !b->counters || !b->tokens || !b->n_prompt || !b->keys || !b->kc || !b->vc || !b->st)
+        !b->part2 || !b->part3 || !b->apart || !b->counters || !b->tokens || !b->n_prompt || !b->keys || !b->kc || !b->vc || !b->st)
         return false;
     return LM_CUDA(cudaMemset(b->counters, 0, (size_t)MB * s->n_heads * 4)) &&
            LM_CUDA(cudaMemset(b->keys, 0, (size_t)MB * 8)) && LM_CUDA(cudaMemset(b->st, 0, sizeof(StepState))) &&
