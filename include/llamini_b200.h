@@ -171,6 +171,17 @@ u32 llamini_batch_pos(llamini_batch* b);
 u64 llamini_batch_weight_bytes(llamini_batch* b);
 void llamini_batch_free(llamini_batch* b);
 
+/* Which GEMM a batch runs its matrices on: 1 = the tcgen05 tensor-core GEMM
+ * (weights dequantised once per step into fp16 hi + lo, f32 accumulation in
+ * tensor memory), 0 = the mma.sync GEMM; -1 = NULL. */
+int llamini_batch_gemm_kind(llamini_batch* b);
+
+/* GEMM for batched products (batches and the batch columns of llamini_gemv_*)
+ * created or called from now on: 1 = tcgen05 (the default), 0 = mma.sync,
+ * -1 = the default again (LLAMINI_BATCH_GEMM=mma in the environment selects
+ * mma.sync). Shapes the tcgen05 GEMM does not take use mma.sync either way. */
+int llamini_set_batch_gemm(int kind);
+
 /* Per-layer residual stream of the most recent step: n_layers x dim floats,
  * captured when `enable` was set before the step ran. For parity tests. */
 int llamini_session_trace(llamini_session* s, int enable);

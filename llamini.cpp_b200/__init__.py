@@ -160,6 +160,8 @@ SIGNATURES = {
     "llamini_batch_logits": (C.c_int, [P, u32, P]),
     "llamini_batch_pos": (u32, [P]),
     "llamini_batch_weight_bytes": (u64, [P]),
+    "llamini_batch_gemm_kind": (C.c_int, [P]),
+    "llamini_set_batch_gemm": (C.c_int, [C.c_int]),
     "llamini_batch_free": (None, [P]),
     "llamini_session_kernel": (C.c_int, [P]),
     "llamini_session_weight_bytes": (u64, [P]),

@@ -237,6 +237,9 @@ struct BStageArgs {
     uint16_t* xl = nullptr;        // low part
     float* sx = nullptr;           // [B][K/16] 16-element sums * 2^(E_b - 24)
     float* oscale = nullptr;       // [B] 2^(24 - E_b)
+    // nonzero: xh/xl in the tensor-core GEMM's layout [K/8][np/8][8][8] for
+    // np (the batch padded to 16) columns, and no 16-element sums
+    uint32_t np = 0;
 };
 struct BSeg {
     const uint8_t* w = nullptr;
@@ -293,6 +296,35 @@ bool bgemm_type(uint32_t type);
 bool bgemm_plan(BGemmArgs& a, uint32_t target_ctas);
 bool launch_bgemm(const BGemmArgs& a, cudaStream_t st);
 bool launch_bstage(const BStageArgs& a, cudaStream_t st);
+
+// Tensor-core (tcgen05) dequant GEMM for a batch of vectors (k_tgemm.cu):
+// same partial sums as bgemm_kernel, inputs staged with BStageArgs::np.
+struct TSeg {
+    const uint8_t* w = nullptr;
+    uint64_t row_bytes = 0;
+    uint32_t type = 0, rows = 0;
+    float* part = nullptr;         // [ksplit][B][rows] raw sums
+    // filled by tgemm_plan: first row block, elements per raw unit, bytes of
+    // one row's raw unit, raw-buffer row stride
+    uint32_t rb0 = 0, ru = 0, ub = 0, rrs = 0;
+};
+struct TGemmArgs {
+    const uint16_t* xh = nullptr;  // staged inputs, [K/8][NP/8][8][8] halves
+    const uint16_t* xl = nullptr;
+    uint32_t B = 0, K = 0;
+    uint32_t nseg = 0;
+    TSeg seg[3];
+    uint32_t* err = nullptr;       // error bits (wait ran out, weight beyond fp16), or null
+    // filled by tgemm_plan: padded batch, K split unit, units per CTA, K split,
+    // row blocks, raw buffer bytes, A/x stages, tensor-memory columns
+    uint32_t NP = 0, ue = 0, ups = 0, ksplit = 0, rblocks = 0, raw_bytes = 0, stages = 0, tcols = 0;
+};
+bool tgemm_init();
+bool batch_tc();   // tcgen05 GEMM for batched products (default) or mma.sync
+extern int g_batch_gemm;   // llamini_set_batch_gemm: -1 default, 0 mma.sync, 1 tcgen05
+bool tgemm_type(uint32_t type);
+bool tgemm_plan(TGemmArgs& a, uint32_t sms);
+bool launch_tgemm(const TGemmArgs& a, cudaStream_t st);
 bool launch_bfinish(const BFinishArgs& a, cudaStream_t st);
 
 // Host-pointer op kernels (model.h per-op exports), device buffers in/out.

@@ -116,7 +116,22 @@ __global__ void __launch_bounds__(256) bstage_kernel(const BStageArgs a) {
         float rs = ((v[0] + v[1]) + (v[2] + v[3])) * 5.9604644775390625e-08f;   // units of 2^(E-24)
         rs += __shfl_xor_sync(0xffffffffu, rs, 1);
         rs += __shfl_xor_sync(0xffffffffu, rs, 2);
-        if (i < n4) {
+        if (i < n4 && a.np) {
+            // tensor-core layout: element (b, k) at half (k/8) * 8np + 8b + k%8
+            __half h[4], l[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                h[j] = __float2half_rn(v[j]);
+                l[j] = __float2half_rn(v[j] - __half2float(h[j]));
+            }
+            const uint64_t o = (uint64_t)(i >> 1) * 8u * a.np + 8u * b + 4u * (i & 1u);
+            __half* gh = reinterpret_cast<__half*>(a.xh) + o;
+            __half* gl = reinterpret_cast<__half*>(a.xl) + o;
+            reinterpret_cast<__half2*>(gh)[0] = __halves2half2(h[0], h[1]);
+            reinterpret_cast<__half2*>(gh)[1] = __halves2half2(h[2], h[3]);
+            reinterpret_cast<__half2*>(gl)[0] = __halves2half2(l[0], l[1]);
+            reinterpret_cast<__half2*>(gl)[1] = __halves2half2(l[2], l[3]);
+        } else if (i < n4) {
             // fragment order within the 4-group: elements 0, 2, 1, 3
             __half h[4], l[4];
 #pragma unroll

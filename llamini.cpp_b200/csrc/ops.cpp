@@ -29,7 +29,7 @@ struct Scratch {
         return p;
     }
 };
-Scratch g_s[10];
+Scratch g_s[11];
 
 bool h2d(void* d, const void* h, size_t n) {
     return n == 0 || LM_CUDA(cudaMemcpyAsync(d, h, n, cudaMemcpyHostToDevice, lm::stream()));
@@ -43,9 +43,65 @@ float* fbuf(int slot, size_t n) { return (float*)g_s[slot].get(n * sizeof(float)
 // y[b] = W x[b] for b < batch through the batched dequant-GEMM (per-sequence
 // staging, split-K partials, finish); scratch in slots 6..9. *handled is false
 // when the format or shape has no batched path (the caller loops columns).
+// The tcgen05 GEMM (k_tgemm.cu): staging in its layout, the GEMM, the same
+// finish; its error word (slot 10) is read back after the call.
+bool gemv_batch_tc(uint32_t type, const uint8_t* w, uint32_t rows, uint32_t cols, const float* x, uint32_t batch,
+                   float* y, bool* handled) {
+    lm::TGemmArgs g;
+    g.B = batch;
+    g.K = cols;
+    g.nseg = 1;
+    g.seg[0].w = w;
+    g.seg[0].row_bytes = lm::type_bytes(type, cols);
+    g.seg[0].type = type;
+    g.seg[0].rows = rows;
+    if (g.seg[0].row_bytes == 0 || !lm::tgemm_plan(g, (uint32_t)lm::sm_count())) return true;
+    *handled = true;
+    uint16_t* xh = (uint16_t*)g_s[6].get((size_t)g.NP * cols * 2);
+    uint16_t* xl = (uint16_t*)g_s[7].get((size_t)g.NP * cols * 2);
+    float* osc = fbuf(8, batch);
+    float* part = fbuf(9, (size_t)g.ksplit * batch * rows);
+    uint32_t* err = (uint32_t*)g_s[10].get(4);
+    if (!xh || !xl || !osc || !part || !err) return false;
+    if (!LM_CUDA(cudaMemsetAsync(err, 0, 4, lm::stream()))) return false;
+    lm::BStageArgs st;
+    st.x = x;
+    st.ldx = cols;
+    st.K = cols;
+    st.B = batch;
+    st.xh = xh;
+    st.xl = xl;
+    st.oscale = osc;
+    st.np = g.NP;
+    g.xh = xh;
+    g.xl = xl;
+    g.err = err;
+    g.seg[0].part = part;
+    lm::BFinishArgs f;
+    f.part = part;
+    f.ksplit = g.ksplit;
+    f.B = batch;
+    f.rows = rows;
+    f.oscale = osc;
+    f.epi = lm::EPI_STORE;
+    f.out = y;
+    f.ldo = rows;
+    if (!lm::launch_bstage(st, lm::stream()) || !lm::launch_tgemm(g, lm::stream()) ||
+        !lm::launch_bfinish(f, lm::stream()))
+        return false;
+    uint32_t e = 0;
+    if (!d2h(&e, err, 4)) return false;
+    if (e) {
+        lm::set_error("tensor-core GEMM: %s", (e & 1u) ? "a pipeline wait ran out" : "a weight outside the fp16 range");
+        return false;
+    }
+    return true;
+}
+
 bool gemv_batch(uint32_t type, const uint8_t* w, uint32_t rows, uint32_t cols, const float* x, uint32_t batch,
                 float* y, bool* handled) {
     *handled = false;
+    if (lm::batch_tc()) return gemv_batch_tc(type, w, rows, cols, x, batch, y, handled);
     lm::BGemmArgs g;
     g.B = batch;
     g.K = cols;

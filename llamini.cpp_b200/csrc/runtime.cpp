@@ -74,6 +74,15 @@ cudaStream_t stream() { return g_stream; }
 
 // Programmatic dependent launch between the step's kernels; LLAMINI_PDL=0
 // turns it off (every launch then waits for its predecessor to finish).
+// Batched products run on the tcgen05 GEMM (k_tgemm.cu) unless
+// LLAMINI_BATCH_GEMM=mma selects the mma.sync kernel (k_bgemm.cu).
+int g_batch_gemm = -1;
+
+bool batch_tc() {
+    static const bool on = [] { const char* e = getenv("LLAMINI_BATCH_GEMM"); return !(e && strcmp(e, "mma") == 0); }();
+    return g_batch_gemm >= 0 ? g_batch_gemm == 1 : on;
+}
+
 bool pdl_enabled() {
     static const bool on = [] { const char* e = getenv("LLAMINI_PDL"); return !(e && e[0] == '0'); }();
     return on;

@@ -830,6 +830,8 @@ struct llamini_batch {
     float *sx = nullptr, *part = nullptr, *part2 = nullptr, *part3 = nullptr, *apart = nullptr;
     uint16_t *xh = nullptr, *xl = nullptr;
     u32 *counters = nullptr, *tokens = nullptr, *n_prompt = nullptr;
+    u32* err = nullptr;               // tensor-core GEMM error bits
+    bool tc = false;                  // matrices on the tcgen05 GEMM (else mma.sync)
     unsigned long long* keys = nullptr;
     void *kc = nullptr, *vc = nullptr;
     lm::StepState* st = nullptr;
@@ -849,29 +851,64 @@ size_t batch_cache_bytes_per_seq(const llamini_batch* b) {
     return (size_t)b->w->n_kv * b->max_seq * b->w->hd * (b->kv_f16 ? 2 : 4);
 }
 
-// GEMM plan of up to three matrices that share an input (false: a format is
-// not supported); segment i writes its raw sums to parts[i].
-bool batch_gemm(const llamini_batch* b, const DevMat* const* m, float* const* parts, u32 n, u32 K, BGemmArgs* out) {
-    BGemmArgs g;
-    g.xh = b->xh;
-    g.xl = b->xl;
-    g.sx = b->sx;
-    g.B = b->B;
-    g.K = K;
-    g.nseg = n;
-    for (u32 i = 0; i < n; i++) {
+// GEMM plan of up to three matrices that share an input, on the tcgen05 GEMM
+// (k_tgemm.cu) or the mma.sync one (k_bgemm.cu); both write raw sums
+// part[ksplit][B][rows] that bfinish_kernel completes.
+struct BPlan {
+    bool tc = false;
+    BGemmArgs m;
+    TGemmArgs t;
+    u32 ksplit() const { return tc ? t.ksplit : m.ksplit; }
+    float* part(u32 i) const { return tc ? t.seg[i].part : m.seg[i].part; }
+    u32 rows(u32 i) const { return tc ? t.seg[i].rows : m.seg[i].rows; }
+};
+
+bool launch_plan(const BPlan& p, cudaStream_t st) { return p.tc ? launch_tgemm(p.t, st) : launch_bgemm(p.m, st); }
+
+// False when a format or shape has no batched kernel; segment i writes its
+// raw sums to parts[i].
+bool batch_gemm(const llamini_batch* b, const DevMat* const* m, float* const* parts, u32 n, u32 K, BPlan* out) {
+    BPlan p;
+    p.tc = b->tc;
+    for (u32 i = 0; i < n; i++)
         if (m[i]->cols != K) return false;
-        g.seg[i].w = m[i]->ptr;
-        g.seg[i].row_bytes = m[i]->row_bytes;
-        g.seg[i].type = m[i]->type;
-        g.seg[i].rows = m[i]->rows;
-        g.seg[i].part = parts[i];
+    if (p.tc) {
+        TGemmArgs& g = p.t;
+        g.xh = b->xh;
+        g.xl = b->xl;
+        g.B = b->B;
+        g.K = K;
+        g.nseg = n;
+        g.err = b->err;
+        for (u32 i = 0; i < n; i++) {
+            g.seg[i].w = m[i]->ptr;
+            g.seg[i].row_bytes = m[i]->row_bytes;
+            g.seg[i].type = m[i]->type;
+            g.seg[i].rows = m[i]->rows;
+            g.seg[i].part = parts[i];
+        }
+        if (!tgemm_plan(g, (u32)sm_count())) return false;
+    } else {
+        BGemmArgs& g = p.m;
+        g.xh = b->xh;
+        g.xl = b->xl;
+        g.sx = b->sx;
+        g.B = b->B;
+        g.K = K;
+        g.nseg = n;
+        for (u32 i = 0; i < n; i++) {
+            g.seg[i].w = m[i]->ptr;
+            g.seg[i].row_bytes = m[i]->row_bytes;
+            g.seg[i].type = m[i]->type;
+            g.seg[i].rows = m[i]->rows;
+            g.seg[i].part = parts[i];
+        }
+        if (!bgemm_plan(g, 2u * (u32)sm_count())) return false;
     }
-    if (!bgemm_plan(g, 2u * (u32)sm_count())) return false;
-    *out = g;
+    *out = p;
     return true;
 }
-bool batch_gemm(const llamini_batch* b, const DevMat& m, u32 K, float* part, BGemmArgs* out) {
+bool batch_gemm(const llamini_batch* b, const DevMat& m, u32 K, float* part, BPlan* out) {
     const DevMat* mm[1] = {&m};
     float* pp[1] = {part};
     return batch_gemm(b, mm, pp, 1, K, out);
@@ -891,17 +928,18 @@ bool batch_stage(llamini_batch* b, const float* x, u32 K, u32 norm, const float*
     a.xl = b->xl;
     a.sx = b->sx;
     a.oscale = b->sx + (size_t)b->max_batch * (b->kmax / 16);
+    a.np = b->tc ? (b->B + 15) & ~15u : 0u;
     return launch_bstage(a, st);
 }
 
-bool batch_finish(llamini_batch* b, const BGemmArgs& g, u32 seg, const float* part2_src, uint32_t epi,
+bool batch_finish(llamini_batch* b, const BPlan& g, u32 seg, const float* part2_src, uint32_t epi,
                   const float* bias, float* out, u32 ldo, unsigned long long* keys, cudaStream_t st) {
     BFinishArgs f;
-    f.part = g.seg[seg].part;
+    f.part = g.part(seg);
     f.part2 = part2_src;
-    f.ksplit = g.ksplit;
+    f.ksplit = g.ksplit();
     f.B = b->B;
-    f.rows = g.seg[seg].rows;
+    f.rows = g.rows(seg);
     f.oscale = b->sx + (size_t)b->max_batch * (b->kmax / 16);
     f.bias = bias;
     f.epi = epi;
@@ -913,16 +951,16 @@ bool batch_finish(llamini_batch* b, const BGemmArgs& g, u32 seg, const float* pa
 
 bool batch_linear(llamini_batch* b, const DevMat& m, u32 K, float* part, const float* part2_src, uint32_t epi,
                   const float* bias, float* out, u32 ldo, unsigned long long* keys, cudaStream_t st) {
-    BGemmArgs g;
+    BPlan g;
     if (!batch_gemm(b, m, K, part, &g)) {
         set_error("batched decode: matrix format %u (%u x %u) has no batched kernel", m.type, m.rows, m.cols);
         return false;
     }
-    if (!launch_bgemm(g, st)) return false;
+    if (!launch_plan(g, st)) return false;
     BFinishArgs f;
     f.part = part;
     f.part2 = part2_src;
-    f.ksplit = g.ksplit;
+    f.ksplit = g.ksplit();
     f.B = b->B;
     f.rows = m.rows;
     f.oscale = b->sx + (size_t)b->max_batch * (b->kmax / 16);
@@ -958,12 +996,12 @@ bool batch_enqueue_step(llamini_batch* b, cudaStream_t st) {
             // q, k and v share their input: one launch, three partial buffers
             const DevMat* mm[3] = {&W.q, &W.k, &W.v};
             float* pp[3] = {b->part, b->part2, b->part3};
-            BGemmArgs g;
+            BPlan g;
             if (!batch_gemm(b, mm, pp, 3, s->dim, &g)) {
                 set_error("batched decode: q/k/v formats have no batched kernel");
                 return false;
             }
-            if (!launch_bgemm(g, st) ||
+            if (!launch_plan(g, st) ||
                 !batch_finish(b, g, 0, nullptr, EPI_STORE, W.bq, b->qkv, qkvd, nullptr, st) ||
                 !batch_finish(b, g, 1, nullptr, EPI_STORE, W.bk, b->qkv + s->qd, qkvd, nullptr, st) ||
                 !batch_finish(b, g, 2, nullptr, EPI_STORE, W.bv, b->qkv + s->qd + s->kvd, qkvd, nullptr, st))
@@ -1002,12 +1040,12 @@ bool batch_enqueue_step(llamini_batch* b, cudaStream_t st) {
             // gate and up in one launch; the finish combines act(gate) * up (model.c:14-25)
             const DevMat* mm[2] = {&W.gate, &W.up};
             float* pp[2] = {b->part, b->part2};
-            BGemmArgs g;
+            BPlan g;
             if (!batch_gemm(b, mm, pp, 2, s->dim, &g)) {
                 set_error("batched decode: gate/up formats have no batched kernel");
                 return false;
             }
-            if (!launch_bgemm(g, st) ||
+            if (!launch_plan(g, st) ||
                 !batch_finish(b, g, 0, b->part2, s->act_gelu ? (u32)EPI_GLU_GELU : (u32)EPI_GLU_SILU, nullptr,
                               b->ffn_h, s->ffn, nullptr, st))
                 return false;
@@ -1062,6 +1100,9 @@ bool batch_alloc(llamini_batch* b) {
     if (s->ffn > b->kmax) b->kmax = s->ffn;
     b->kmax = (b->kmax + 255) & ~255u;
     b->kv_f16 = g_kv_f16 ? 1u : 0u;
+    b->tc = batch_tc();
+    b->err = (u32*)own(s, 4);
+    if (!b->err || !LM_CUDA(cudaMemset(b->err, 0, 4))) return false;
     const u32 hb = s->n_heads * MB;
     u32 ns = (u32)(2 * sm_count()) / (hb ? hb : 1);
     if (ns < 1) ns = 1;
@@ -1074,14 +1115,14 @@ bool batch_alloc(llamini_batch* b) {
     size_t pmax = 0;
     auto need = [&](const DevMat* const* mm, u32 n, u32 K) -> bool {
         float* none[3] = {nullptr, nullptr, nullptr};
-        BGemmArgs g;
+        BPlan g;
         if (!batch_gemm(b, mm, none, n, K, &g)) {
             set_error("batched decode: matrix format %u (%u x %u) has no batched kernel", mm[0]->type, mm[0]->rows,
                       mm[0]->cols);
             return false;
         }
         for (u32 i = 0; i < n; i++) {
-            const size_t m = (size_t)g.ksplit * MB * mm[i]->rows;
+            const size_t m = (size_t)g.ksplit() * MB * mm[i]->rows;
             pmax = pmax > m ? pmax : m;
         }
         return true;
@@ -1090,18 +1131,27 @@ bool batch_alloc(llamini_batch* b) {
         const DevMat* mm[1] = {&m};
         return need(mm, 1, K);
     };
-    bool ok = need1(s->head, s->dim);
-    for (u32 l = 0; ok && l < s->n_layers; l++) {
-        const auto& W = s->layers[l];
-        ok = need1(W.o, s->qd) && need1(W.down, s->ffn);
-        if (ok && s->kind == 1) ok = need1(W.q, s->dim) && need1(W.up, s->dim);
-        if (ok && s->kind == 0) {
-            const DevMat* qkv[3] = {&W.q, &W.k, &W.v};
-            const DevMat* gu[2] = {&W.gate, &W.up};
-            ok = need(qkv, 3, s->dim) && need(gu, 2, s->dim);
+    auto plan_all = [&]() -> bool {
+        bool ok = need1(s->head, s->dim);
+        for (u32 l = 0; ok && l < s->n_layers; l++) {
+            const auto& W = s->layers[l];
+            ok = need1(W.o, s->qd) && need1(W.down, s->ffn);
+            if (ok && s->kind == 1) ok = need1(W.q, s->dim) && need1(W.up, s->dim);
+            if (ok && s->kind == 0) {
+                const DevMat* qkv[3] = {&W.q, &W.k, &W.v};
+                const DevMat* gu[2] = {&W.gate, &W.up};
+                ok = need(qkv, 3, s->dim) && need(gu, 2, s->dim);
+            }
         }
+        return ok;
+    };
+    if (!plan_all()) {
+        // a shape the tensor-core GEMM does not take: the whole batch on mma.sync
+        if (!b->tc) return false;
+        b->tc = false;
+        pmax = 0;
+        if (!plan_all()) return false;
     }
-    if (!ok) return false;
     b->part_floats = pmax;
     const size_t per_seq = batch_cache_bytes_per_seq(b);
     const size_t cache = (size_t)s->n_layers * MB * per_seq;
@@ -1110,8 +1160,9 @@ bool batch_alloc(llamini_batch* b) {
     b->attn = (float*)own(s, (size_t)MB * s->qd * 4);
     b->ffn_h = (float*)own(s, (size_t)MB * s->ffn * 4);
     b->logits = (float*)own(s, (size_t)MB * s->vocab * 4);
-    b->xh = (uint16_t*)own(s, (size_t)MB * b->kmax * 2);
-    b->xl = (uint16_t*)own(s, (size_t)MB * b->kmax * 2);
+    const size_t xcols = ((size_t)MB + 15) & ~size_t(15);         // the tensor-core layout pads the batch to 16
+    b->xh = (uint16_t*)own(s, xcols * b->kmax * 2);
+    b->xl = (uint16_t*)own(s, xcols * b->kmax * 2);
     b->sx = (float*)own(s, ((size_t)MB * (b->kmax / 16) + MB) * 4);
     b->part = (float*)own(s, pmax * 4);
     b->part2 = (float*)own(s, pmax * 4);
@@ -1145,6 +1196,17 @@ llamini_batch* batch_create(M* model, u32 max_batch, u32 max_seq, Bind bind) {
     if (!bind(b->w, model, max_seq) || !batch_alloc(b)) { batch_destroy(b); return nullptr; }
     b->B = 0;
     return b;
+}
+
+// After a synchronize: false (error set) when a tensor-core GEMM of the steps
+// run so far reported a failure.
+bool batch_ok(llamini_batch* b) {
+    if (!b->tc) return true;
+    u32 e = 0;
+    if (!LM_CUDA(cudaMemcpy(&e, b->err, 4, cudaMemcpyDeviceToHost))) return false;
+    if (e == 0) return true;
+    set_error("batched decode: tensor-core GEMM: %s", (e & 1u) ? "a pipeline wait ran out" : "a weight outside the fp16 range");
+    return false;
 }
 
 bool batch_run(llamini_batch* b, u32 n) {
@@ -1312,7 +1374,7 @@ int llamini_batch_step(llamini_batch* b, u32 n_steps) {
 
 int llamini_batch_tokens(llamini_batch* b, u32 seq, u32* out, u32 n) {
     if (!b || !out || seq >= b->B) { lm::set_error("batched decode: bad sequence index"); return -1; }
-    if (!LM_CUDA(cudaStreamSynchronize(lm::stream()))) return -1;
+    if (!LM_CUDA(cudaStreamSynchronize(lm::stream())) || !lm::batch_ok(b)) return -1;
     const u32 have = b->pos + 1 > b->lens[seq] ? b->pos + 1 : b->lens[seq];
     const u32 k = n < have ? n : have;
     if (!LM_CUDA(cudaMemcpy(out, b->tokens + (size_t)seq * (b->max_seq + 1), (size_t)k * 4, cudaMemcpyDeviceToHost)))
@@ -1322,7 +1384,7 @@ int llamini_batch_tokens(llamini_batch* b, u32 seq, u32* out, u32 n) {
 
 int llamini_batch_logits(llamini_batch* b, u32 seq, f32* out) {
     if (!b || !out || seq >= b->B) { lm::set_error("batched decode: bad sequence index"); return -1; }
-    if (!LM_CUDA(cudaStreamSynchronize(lm::stream()))) return -1;
+    if (!LM_CUDA(cudaStreamSynchronize(lm::stream())) || !lm::batch_ok(b)) return -1;
     return LM_CUDA(cudaMemcpy(out, b->logits + (size_t)seq * b->w->vocab, (size_t)b->w->vocab * 4,
                               cudaMemcpyDeviceToHost)) ? 0 : -1;
 }
@@ -1332,5 +1394,13 @@ u32 llamini_batch_pos(llamini_batch* b) { return b ? b->pos : 0; }
 u64 llamini_batch_weight_bytes(llamini_batch* b) { return b ? b->w->weight_bytes : 0; }
 
 void llamini_batch_free(llamini_batch* b) { lm::batch_destroy(b); }
+
+int llamini_batch_gemm_kind(llamini_batch* b) { return b ? (b->tc ? 1 : 0) : -1; }
+
+int llamini_set_batch_gemm(int kind) {
+    if (kind < -1 || kind > 1) { lm::set_error("batched GEMM kind %d outside -1..1", kind); return -1; }
+    lm::g_batch_gemm = kind;
+    return 0;
+}
 
 }  // extern "C"
