@@ -7,6 +7,8 @@
 #include <cstddef>
 
 #include "common.h"
+
+#include <cuda.h>
 #include "gguf.h"
 #include "tensor.h"
 #include "kv_cache.h"
@@ -305,10 +307,13 @@ struct TSeg {
     uint32_t type = 0, rows = 0;
     float* part = nullptr;         // [ksplit][B][rows] raw sums
     // filled by tgemm_plan: first row block, elements per raw unit, bytes of
-    // one row's raw unit, raw-buffer row stride
+    // one row's raw unit, raw-buffer row stride (= the TMA box width)
     uint32_t rb0 = 0, ru = 0, ub = 0, rrs = 0;
 };
-struct TGemmArgs {
+struct alignas(64) TGemmArgs {
+    // filled by tgemm_plan: per segment a 2-D TMA map of the rows as uint16
+    // (used when `tma`; otherwise 16-byte cp.async copies)
+    CUtensorMap tmap[3];
     const uint16_t* xh = nullptr;  // staged inputs, [K/8][NP/8][8][8] halves
     const uint16_t* xl = nullptr;
     uint32_t B = 0, K = 0;
@@ -316,8 +321,9 @@ struct TGemmArgs {
     TSeg seg[3];
     uint32_t* err = nullptr;       // error bits (wait ran out, weight beyond fp16), or null
     // filled by tgemm_plan: padded batch, K split unit, units per CTA, K split,
-    // row blocks, raw buffer bytes, A/x stages, tensor-memory columns
-    uint32_t NP = 0, ue = 0, ups = 0, ksplit = 0, rblocks = 0, raw_bytes = 0, stages = 0, tcols = 0;
+    // row blocks, raw buffer bytes, A/x stages, tensor-memory columns, CTAs
+    uint32_t NP = 0, ue = 0, ups = 0, ksplit = 0, rblocks = 0, raw_bytes = 0, stages = 0, tcols = 0, grid = 0;
+    uint32_t tma = 0;
 };
 bool tgemm_init();
 bool batch_tc();   // tcgen05 GEMM for batched products (default) or mma.sync

@@ -3,8 +3,8 @@
 // y[b][r] = sum_k W[r][k] x[b][k] for up to 64 vectors at once: the matrix
 // products of batched decode (model.c:66-176 and gpt2.c's forward, once per
 // sequence) and of the batch columns of the GEMV entry points. The weights stay
-// in their GGUF block layout in HBM. A CTA owns 128 rows of one matrix and a K
-// range, and runs five roles:
+// in their GGUF block layout in HBM. A tile is 128 rows of one matrix x one K
+// range; one persistent CTA per SM walks its tiles with five roles:
 //
 //   raw warp       bulk copies (cp.async.bulk, the TMA engine) of each row's
 //                  bytes of the current unit -- one 256-element super-block for
@@ -18,10 +18,11 @@
 //                  kind::f16 (M = 128, N = batch padded to 16, K = 16, f32
 //                  accumulators in tensor memory): w_hi x_hi + w_hi x_lo +
 //                  w_lo x_hi per 16-element step; tcgen05.commit frees each
-//                  stage and finally hands the accumulators to the epilogue
-//   epilogue       the dequant warps read the accumulators (tcgen05.ld) and
-//                  store raw sums to part[ksplit][B][rows] in the units that
-//                  bfinish_kernel (k_bgemm.cu) scales and finishes
+//                  stage and hands each finished tile's accumulator (two, used
+//                  alternately) to the epilogue
+//   4 epilogue     read the accumulators (tcgen05.ld) and store raw sums to
+//   warps          part[ksplit][B][rows] in the units that bfinish_kernel
+//                  (k_bgemm.cu) scales and finishes
 //
 // Inputs are staged by bstage_kernel as x * 2^E (per sequence) split into fp16
 // hi + lo, laid out [K/8][NP/8][8 sequences][8 elements], the same UMMA layout,
@@ -43,17 +44,34 @@
 #include "quant.cuh"
 
 #include <cuda_fp16.h>
+#include <cudaTypedefs.h>
 
 namespace lm {
 
 constexpr uint32_t kTRows = 128;                 // MMA M: matrix rows per CTA
 constexpr uint32_t kTSlab = 64;                  // K elements per stage
-constexpr uint32_t kTATile = kTRows * kTSlab * 2;   // bytes of one fp16 A tile (hi or lo)
-constexpr uint32_t kTDeqWarps = 8;
-constexpr uint32_t kTWarpMma = 8, kTWarpRaw = 9, kTWarpX = 10;
-constexpr uint32_t kTThreads = 11 * 32;
-constexpr uint32_t kTRaw = 2;                    // raw buffers
-constexpr uint32_t kTMaxStages = 4;
+// Tensor memory (512 columns): two accumulator sets (used by alternate tiles)
+// of three independent f32 accumulators -- w_hi x_hi, w_hi x_lo, w_lo x_hi --
+// 64 columns each, so the MMAs of a K step do not wait on one another; then
+// kTNA stages of the A slab, 32 columns hi and 32 lo (fp16 pairs: column c
+// holds K elements 2c and 2c + 1).
+constexpr uint32_t kTAccW = 64;                  // columns per accumulator (NP <= 64)
+constexpr uint32_t kTSetCols = 3 * kTAccW;
+constexpr uint32_t kTACol0 = 2 * kTSetCols;      // first A-stage column
+constexpr uint32_t kTACols = 64;
+constexpr uint32_t kTNA = 2;                     // A stages in tensor memory
+constexpr uint32_t kTCols = 512;
+constexpr uint32_t kTGroupWarps = 8;            // one dequant group: a slab's 128 rows x 2 runs
+constexpr uint32_t kTDeqWarps = 16;             // warps 0-15: two groups decode alternate slabs
+constexpr uint32_t kTEpiWarps = 4;              // warps 16-19 (tensor-memory lanes 0-127)
+constexpr uint32_t kTIssuers = 3;               // warps 20-22: one issuing thread per accumulator chain
+constexpr uint32_t kTWarpEpi = 16, kTWarpMma = 20, kTWarpRaw = 23, kTWarpX = 24;
+constexpr uint32_t kTThreads = 25 * 32;
+constexpr uint32_t kTAlign = 1024;              // dynamic shared memory aligned up to this
+constexpr uint32_t kTSlack = 64;                // after the raw buffers: the decoders' word reads
+                                                // may run up to 8 bytes past a row's last byte
+constexpr uint32_t kTRaw = 4;                    // raw buffers
+constexpr uint32_t kTMaxStages = 4;              // x stages in shared memory
 constexpr uint64_t kTWaitNs = 2000000000ull;     // 2 s
 constexpr size_t kTSmemMax = 226 * 1024;
 
@@ -62,8 +80,10 @@ constexpr uint32_t kTErrRange = 2u;              // a weight outside the fp16 ra
 
 struct TShared {
     uint64_t raw_full[kTRaw], raw_empty[kTRaw];
-    uint64_t xfull[kTMaxStages], afull[kTMaxStages], sempty[kTMaxStages];
-    uint64_t accf;
+    uint64_t xfull[kTMaxStages], xempty[kTMaxStages];   // x slab landed / read by its MMAs
+    uint64_t afull[kTNA], aempty[kTNA];                  // A slab in tensor memory / read by its MMAs
+    uint64_t accf[2], acce[2];          // accumulator full (MMA -> epilogue) / empty
+    uint64_t mdone;                     // every MMA of the CTA finished
     uint32_t tmem;
     uint32_t abort;
 };
@@ -117,6 +137,22 @@ __device__ __forceinline__ void tg_arrive(uint64_t* bar) {
 }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 
+// TMA tiled load of a 2-D box (x in elements of the map, y in rows) into
+// shared memory, completing on `bar`. No multicast.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n"
+                 ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
+}
+// 16-byte asynchronous copy (both addresses 16-byte aligned); the executing
+// thread's copies are tracked by tg_cpa_arrive.
+__device__ __forceinline__ void tg_cpa16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// One arrival on `bar` once every cp.async this thread issued has landed.
+__device__ __forceinline__ void tg_cpa_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // UMMA shared-memory descriptor, K-major without swizzle: start address,
 // leading byte offset (K direction) and stride byte offset (M/N direction),
 // all in 16-byte units; version 1 at bits 46-47; layout type 0 (no swizzle).
@@ -152,6 +188,20 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
                  : "r"(taddr) : "memory");
 }
 
+// This warp's 32 tensor-memory lanes, 16 consecutive columns, from registers.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};\n"
+                 ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+                   "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]) : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+// D (+)= A B with A (128 x 16 fp16) in tensor memory and B in shared memory.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                 " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
+                 ::"r"(d), "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate) : "memory");
+}
+
 // NW little-endian words from a 2-byte aligned shared-memory address (the
 // aligned words around it, funnel-shifted; reads one word past the range).
 template <int NW>
@@ -169,36 +219,74 @@ __device__ __forceinline__ void sm_words(const uint8_t* p, uint32_t* w) {
 }
 
 // ---------------------------------------------------------------- decoders
-// Each yields the 32 weights of run j of a unit in natural K order, bit-exact
-// with gguf.c. p is the row's first byte of the unit in shared memory.
+// Each yields the 32 weights of run j of a unit -- 32 consecutive K elements,
+// bit-exact with gguf.c -- as fp16 hi and lo pairs: h[i] and l[i] hold
+// elements 2i (low half) and 2i + 1 (high half), the order of a row's A
+// operand in tensor memory. p is the row's first byte of the unit in shared
+// memory. Returns false when a weight of the run may leave the fp16 range
+// (checked once per run from its scales).
+
+// 2^23 + b for a byte b < 256 as f32 bits: the byte placed into the mantissa.
+__device__ __forceinline__ float magic_byte(uint32_t word, uint32_t sel) {
+    return __uint_as_float(__byte_perm(word, 0x4B000000u, sel));
+}
+
+// Eight weights to four hi pairs and four lo pairs.
+__device__ __forceinline__ void st8(uint32_t* h, uint32_t* l, const float* w) {
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const __half2 hh = __floats2half2_rn(w[2 * q], w[2 * q + 1]);
+        const float2 hf = __half22float2(hh);
+        const __half2 ll = __floats2half2_rn(__fsub_rn(w[2 * q], hf.x), __fsub_rn(w[2 * q + 1], hf.y));
+        h[q] = *reinterpret_cast<const uint32_t*>(&hh);
+        l[q] = *reinterpret_cast<const uint32_t*>(&ll);
+    }
+}
 
 // Q4_K (gguf.c:504-529): run j = sub-block j; its quants are the low (j even)
 // or high (j odd) nibbles of qs[32 (j/2) + l], weight d*sc_j*q - dmin*m_j.
 // d*sc_j*q is exact in f32 (at most 21 significant bits), so one fused
 // multiply-add rounds exactly as the reference's multiply-then-subtract.
-__device__ __forceinline__ void dq_q4k(const uint8_t* p, uint32_t j, float* w) {
-    const uint4 h = *reinterpret_cast<const uint4*>(p);
-    const uint4 q0 = *reinterpret_cast<const uint4*>(p + 16 + 32 * (j >> 1));
-    const uint4 q1 = *reinterpret_cast<const uint4*>(p + 32 + 32 * (j >> 1));
-    const uint32_t hs[3] = {h.y, h.z, h.w};
+__device__ __forceinline__ bool dq_q4k(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
+    const uint4 hd = *reinterpret_cast<const uint4*>(p);
+    // 6-bit scale and min of sub-block j (gguf.c:391-399) from scale bytes 0-11
+    const uint32_t jj = j & 3u, sh8 = 8u * jj;
     uint32_t sc, mn;
-    k4_scale_min(hs, j, &sc, &mn);
-    const float d1 = __fmul_rn(f16_bits(h.x & 0xFFFFu), u2f(sc));
-    const float m1 = __fmul_rn(f16_bits(h.x >> 16), u2f(mn));
-    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    if (j < 4) {
+        sc = (hd.y >> sh8) & 63u;
+        mn = (hd.z >> sh8) & 63u;
+    } else {
+        sc = ((hd.w >> sh8) & 15u) | (((hd.y >> (sh8 + 6)) & 3u) << 4);
+        mn = ((hd.w >> (sh8 + 4)) & 15u) | (((hd.z >> (sh8 + 6)) & 3u) << 4);
+    }
+    const float d1 = __fmul_rn(f16_bits(hd.x & 0xFFFFu), u2f(sc));
+    const float m1 = __fmul_rn(f16_bits(hd.x >> 16), u2f(mn));
+    const uint8_t* qp = p + 16 + 32 * (j >> 1);
     const uint32_t sh = (j & 1u) * 4u;
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
+    for (int half = 0; half < 2; half++) {
+        const uint4 q = *reinterpret_cast<const uint4*>(qp + 16 * half);
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-        for (int b = 0; b < 4; b++) w[4 * i + b] = __fmaf_rn(d1, u2f((qw[i] >> (8 * b + sh)) & 15u), -m1);
+        for (int sl = 0; sl < 2; sl++) {
+            float w[8];
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const uint32_t n = (qw[2 * sl + e] >> sh) & 0x0F0F0F0Fu;
+#pragma unroll
+                for (int b = 0; b < 4; b++) w[4 * e + b] = __fmaf_rn(d1, magic_byte(n, 0x7440u | (uint32_t)b) - 8388608.0f, -m1);
+            }
+            st8(h + 4 * (2 * half + sl), l + 4 * (2 * half + sl), w);
+        }
     }
+    return fabsf(d1) * 15.0f + fabsf(m1) <= 65504.0f;
 }
 
 // Q6_K (gguf.c:561-590): run j covers elements 128H + 32c + l (H = j/4,
 // c = j%4, l < 32): low 4 bits from nibble c/2 of ql[64H + 32(c%2) + l], high
 // 2 bits from bits 2c of qh[32H + l], scale sc[8H + 2c + l/16]; weight
 // (d*sc)*(q - 32), exact in f32.
-__device__ __forceinline__ void dq_q6k(const uint8_t* p, uint32_t j, float* w) {
+__device__ __forceinline__ bool dq_q6k(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
     const uint32_t H = j >> 2, c = j & 3u;
     uint32_t ql[8], qh[8];
     sm_words<8>(p + 64 * H + 32 * (c & 1u), ql);
@@ -209,93 +297,129 @@ __device__ __forceinline__ void dq_q6k(const uint8_t* p, uint32_t j, float* w) {
     const float ds1 = __fmul_rn(d, (float)(int)(int8_t)(uint8_t)((sw >> 8) & 0xFFu));
     const uint32_t ns = (c >> 1) * 4u, hs = 2u * c;
 #pragma unroll
-    for (int l = 0; l < 32; l++) {
-        const uint32_t nib = (ql[l >> 2] >> (8 * (l & 3) + ns)) & 15u;
-        const uint32_t hb = (qh[l >> 2] >> (8 * (l & 3) + hs)) & 3u;
-        const float q = __uint_as_float(0x4B000000u | (nib | (hb << 4))) - 8388640.0f;   // (q6 - 32), exact
-        w[l] = __fmul_rn(l < 16 ? ds0 : ds1, q);
+    for (int sl = 0; sl < 4; sl++) {
+        float w[8];
+        const float ds = sl < 2 ? ds0 : ds1;
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const uint32_t i = 2 * sl + e;
+            const uint32_t q6 = ((ql[i] >> ns) & 0x0F0F0F0Fu) | (((qh[i] >> hs) & 0x03030303u) << 4);
+#pragma unroll
+            for (int b = 0; b < 4; b++) w[4 * e + b] = __fmul_rn(ds, magic_byte(q6, 0x7440u | (uint32_t)b) - 8388640.0f);
+        }
+        st8(h + 4 * sl, l + 4 * sl, w);
     }
+    return fmaxf(fabsf(ds0), fabsf(ds1)) * 32.0f <= 65504.0f;
 }
 
-// Q8_0 (gguf.c:489-503): run j = block j of the unit, weight q * d.
-__device__ __forceinline__ void dq_q80(const uint8_t* p, uint32_t j, float* w) {
+// Q8_0 (gguf.c:489-503): run j = block j of the unit, weight q * d (the int8
+// made unsigned by flipping its sign bit, then offset back).
+__device__ __forceinline__ bool dq_q80(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
     const uint8_t* b = p + 34 * j;
     const float d = f16_bits(lds_u16(b));
     uint32_t q[8];
     sm_words<8>(b + 2, q);
 #pragma unroll
-    for (int i = 0; i < 32; i++) w[i] = __fmul_rn((float)(int)(int8_t)(uint8_t)((q[i >> 2] >> (8 * (i & 3))) & 0xFFu), d);
+    for (int sl = 0; sl < 4; sl++) {
+        float w[8];
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const uint32_t u = q[2 * sl + e] ^ 0x80808080u;
+#pragma unroll
+            for (int k = 0; k < 4; k++) w[4 * e + k] = __fmul_rn(magic_byte(u, 0x7440u | (uint32_t)k) - 8388736.0f, d);
+        }
+        st8(h + 4 * sl, l + 4 * sl, w);
+    }
+    return fabsf(d) * 128.0f <= 65504.0f;
 }
 
 // Q4_0 (gguf.c:427-444): run j = block j; element l < 16 is the low nibble of
 // qs[l], element l + 16 its high nibble; weight (q - 8) * d.
-__device__ __forceinline__ void dq_q40(const uint8_t* p, uint32_t j, float* w) {
+__device__ __forceinline__ bool dq_q40(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
     const uint8_t* b = p + 18 * j;
     const float d = f16_bits(lds_u16(b));
     uint32_t q[4];
     sm_words<4>(b + 2, q);
 #pragma unroll
-    for (int i = 0; i < 16; i++) {
-        const uint32_t v = (q[i >> 2] >> (8 * (i & 3))) & 0xFFu;
-        w[i] = __fmul_rn(u2f(v & 15u) - 8.0f, d);
-        w[i + 16] = __fmul_rn(u2f(v >> 4) - 8.0f, d);
+    for (int sl = 0; sl < 4; sl++) {
+        float w[8];
+        const uint32_t sh = sl < 2 ? 0u : 4u;                // elements 16.. are the high nibbles
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const uint32_t n = (q[(2 * sl + e) & 3] >> sh) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int k = 0; k < 4; k++) w[4 * e + k] = __fmul_rn(magic_byte(n, 0x7440u | (uint32_t)k) - 8388616.0f, d);
+        }
+        st8(h + 4 * sl, l + 4 * sl, w);
     }
+    return fabsf(d) * 8.0f <= 65504.0f;
 }
 
-// Split 32 weights into fp16 hi and lo and store them as four 8-element
-// K slices (16 bytes each, 16R bytes apart) of the A tiles.
-__device__ __forceinline__ void tstore(uint8_t* ahi, uint8_t* alo, const float* w) {
+// F16 rows: the weights are their own hi halves; lo is zero.
+__device__ __forceinline__ bool dq_f16(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
+    const uint8_t* b = p + 64 * j;
 #pragma unroll
     for (int sl = 0; sl < 4; sl++) {
-        uint32_t h[4], l[4];
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const float a = w[8 * sl + 2 * q], b = w[8 * sl + 2 * q + 1];
-            const __half2 hh = __floats2half2_rn(a, b);
-            const float2 hf = __half22float2(hh);
-            const __half2 ll = __floats2half2_rn(__fsub_rn(a, hf.x), __fsub_rn(b, hf.y));
-            h[q] = *reinterpret_cast<const uint32_t*>(&hh);
-            l[q] = *reinterpret_cast<const uint32_t*>(&ll);
-        }
-        *reinterpret_cast<uint4*>(ahi + sl * (16 * kTRows)) = make_uint4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<uint4*>(alo + sl * (16 * kTRows)) = make_uint4(l[0], l[1], l[2], l[3]);
+        const uint4 v = *reinterpret_cast<const uint4*>(b + 16 * sl);
+        h[4 * sl] = v.x;
+        h[4 * sl + 1] = v.y;
+        h[4 * sl + 2] = v.z;
+        h[4 * sl + 3] = v.w;
     }
+#pragma unroll
+    for (int i = 0; i < 16; i++) l[i] = 0;
+    return true;
 }
 
 // ---------------------------------------------------------------- kernel
+//
+// Persistent: one CTA per SM walks the tiles (128 rows of one segment x one K
+// range) t = blockIdx.x, + gridDim.x, ...; every role walks the same tile and
+// slab sequence, so the shared-memory rings (raw units, A/x stages) and the
+// two tensor-memory accumulators run across tile boundaries without a pause.
 
-__host__ __device__ __forceinline__ uint32_t tg_stage_bytes(uint32_t np) { return 2 * kTATile + 2 * (128 * np); }
+__host__ __device__ __forceinline__ uint32_t tg_stage_bytes(uint32_t np) { return 2 * (128 * np); }   // x hi + lo
+
+struct TTile {
+    uint32_t seg, row0, ks, sl0, sl1;   // segment, first row, K split, slabs [sl0, sl1)
+};
+__device__ __forceinline__ TTile tg_tile(const TGemmArgs& a, uint32_t t) {
+    const uint32_t rb = t / a.ksplit, ks = t - rb * a.ksplit;
+    uint32_t s = 0;
+#pragma unroll
+    for (uint32_t i = 1; i < 3; i++)
+        if (i < a.nseg && rb >= a.seg[i].rb0) s = i;
+    const uint32_t units = a.K / a.ue, spu = a.ue / kTSlab;
+    const uint32_t u0 = ks * a.ups, u1 = min(units, u0 + a.ups);
+    return TTile{s, (rb - a.seg[s].rb0) * kTRows, ks, u0 * spu, u1 * spu};
+}
 
 __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_constant__ TGemmArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ TShared S;
-    uint32_t sgi = 0;
-#pragma unroll
-    for (uint32_t i = 1; i < 3; i++)
-        if (i < a.nseg && blockIdx.x >= a.seg[i].rb0) sgi = i;
-    const TSeg& G = a.seg[sgi];
-    const uint32_t row0 = (blockIdx.x - G.rb0) * kTRows;
-    const uint32_t ks = blockIdx.y;
-    const uint32_t units = a.K / a.ue;
-    const uint32_t u0 = ks * a.ups, u1 = min(units, u0 + a.ups);
-    const uint32_t sl0 = u0 * (a.ue / kTSlab), sl1 = u1 * (a.ue / kTSlab);   // slabs [sl0, sl1)
-    const uint32_t ru = G.ru, spr = ru / kTSlab;                             // slabs per raw unit
-    const uint32_t ur0 = sl0 / spr;
     const uint32_t NS = a.stages, NP = a.NP;
+    const uint32_t ntiles = a.rblocks * a.ksplit;
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
 
-    uint8_t* const abase = smem;                                      // NS x (A hi, A lo)
-    uint8_t* const xbase = smem + NS * 2 * kTATile;                   // NS x (x hi, x lo)
+    uint8_t* const sbase = smem + ((kTAlign - (smem_u32(smem) & (kTAlign - 1))) & (kTAlign - 1));
+    uint8_t* const xbase = sbase;                                     // NS x (x hi, x lo)
     uint8_t* const rbase = xbase + NS * 2 * (128 * NP);               // kTRaw raw buffers
 
     if (tid == 0) {
-        for (uint32_t i = 0; i < kTRaw; i++) { mbar_init(&S.raw_full[i], 1); mbar_init(&S.raw_empty[i], kTDeqWarps); }
+        for (uint32_t i = 0; i < kTRaw; i++) {
+            mbar_init(&S.raw_full[i], a.tma ? 1u : 32u);              // TMA: one expect-tx; cp.async: every raw lane
+            mbar_init(&S.raw_empty[i], kTDeqWarps);
+        }
         for (uint32_t i = 0; i < NS; i++) {
             mbar_init(&S.xfull[i], 1);
-            mbar_init(&S.afull[i], kTDeqWarps);
-            mbar_init(&S.sempty[i], 1);
+            mbar_init(&S.xempty[i], kTIssuers);                    // one commit per issuing thread
         }
-        mbar_init(&S.accf, 1);
+        for (uint32_t i = 0; i < kTNA; i++) {
+            mbar_init(&S.afull[i], kTGroupWarps);
+            mbar_init(&S.aempty[i], kTIssuers);
+        }
+        for (uint32_t i = 0; i < 2; i++) { mbar_init(&S.accf[i], kTIssuers); mbar_init(&S.acce[i], kTEpiWarps); }
+        mbar_init(&S.mdone, kTIssuers);
         S.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         fence_async_smem();
@@ -312,159 +436,201 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
 
     if (warp == kTWarpRaw) {
         // ------------------------------------------------ raw weight bytes
-        const uint32_t nru = (sl1 - sl0) / spr;
-        uint32_t armed = 0;                                            // raw units issued
-        for (uint32_t lr = 0; lr < nru; lr++) {
-            const uint32_t buf = lr % kTRaw, t = lr / kTRaw;
-            if (t > 0 && !tg_wait_warp(S, &S.raw_empty[buf], (t - 1) & 1u, a.err)) break;
-            const uint64_t ur = ur0 + lr;
-            uint8_t* dst = rbase + buf * a.raw_bytes;
-            uint32_t len[4], tot = 0;
-            uint64_t src[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const uint32_t r = lane + 32u * i;
-                len[i] = 0;
-                src[i] = 0;
-                if (row0 + r < G.rows) {
-                    const uint64_t o = (uint64_t)(row0 + r) * G.row_bytes + ur * G.ub;
-                    src[i] = o & ~uint64_t(15);
-                    len[i] = (uint32_t)(((o + G.ub + 15) & ~uint64_t(15)) - src[i]);
-                    tot += len[i];
+        uint32_t lr = 0;                                               // raw units issued
+        bool ok = true;
+        for (uint32_t t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
+            const TTile T = tg_tile(a, t);
+            const TSeg& G = a.seg[T.seg];
+            const uint32_t spr = G.ru / kTSlab;
+            for (uint32_t ur = T.sl0 / spr; ur < T.sl1 / spr; ur++) {
+                const uint32_t buf = lr % kTRaw, ph = lr / kTRaw;
+                if (ph > 0 && !tg_wait_warp(S, &S.raw_empty[buf], (ph - 1) & 1u, a.err)) { ok = false; break; }
+                uint8_t* dst = rbase + buf * a.raw_bytes;
+                if (a.tma) {
+                    // one box: 128 rows x rrs bytes from the 16-byte boundary at or below the unit
+                    if (lane == 0) {
+                        mbar_expect_tx(&S.raw_full[buf], kTRows * G.rrs);
+                        const uint64_t o = (uint64_t)ur * G.ub;
+                        tma_load_2d(dst, &a.tmap[T.seg], (int32_t)((o & ~uint64_t(15)) >> 1), (int32_t)T.row0, &S.raw_full[buf]);
+                    }
+                    __syncwarp();
+                } else {
+                    // row strides that are not a multiple of 16 bytes: the 16-byte chunks
+                    // covering each row's unit, lanes 0-15 on even rows, 16-31 on odd rows
+                    const uint32_t ch = lane & 15u;
+                    for (uint32_t r = lane >> 4; r < kTRows && T.row0 + r < G.rows; r += 2) {
+                        const uint64_t o = (uint64_t)(T.row0 + r) * G.row_bytes + (uint64_t)ur * G.ub;
+                        const uint64_t a16 = o & ~uint64_t(15);
+                        const uint32_t nch = (uint32_t)((((o + G.ub + 15) & ~uint64_t(15)) - a16) >> 4);
+                        if (ch < nch) tg_cpa16(dst + r * G.rrs + 16 * ch, G.w + a16 + 16 * ch);
+                    }
+                    tg_cpa_arrive(&S.raw_full[buf]);
                 }
+                lr++;
             }
-            tot = __reduce_add_sync(0xffffffffu, tot);
-            if (lane == 0) mbar_expect_tx(&S.raw_full[buf], tot);
-            __syncwarp();
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-                if (len[i]) bulk_g2s(dst + (lane + 32u * i) * G.rrs, G.w + src[i], len[i], &S.raw_full[buf]);
-            armed = lr + 1;
         }
         // every issued copy has landed before the CTA can exit
         if (lane == 0)
-            for (uint32_t lr = (armed > kTRaw ? armed - kTRaw : 0); lr < armed; lr++)
-                tg_drain(&S.raw_full[lr % kTRaw], (lr / kTRaw) & 1u);
+            for (uint32_t u = (lr > kTRaw ? lr - kTRaw : 0); u < lr; u++) tg_drain(&S.raw_full[u % kTRaw], (u / kTRaw) & 1u);
         __syncwarp();
     } else if (warp == kTWarpX) {
         // ------------------------------------------------ staged inputs
         if (lane == 0) {
             const uint32_t xb = 128 * NP;                               // bytes of one half-slab
-            uint32_t armed = 0;
-            for (uint32_t i = 0; i < sl1 - sl0; i++) {
-                const uint32_t si = i % NS, t = i / NS;
-                if (t > 0 && !tg_wait(S, &S.sempty[si], (t - 1) & 1u, a.err)) break;
-                const uint64_t off = (uint64_t)(sl0 + i) * (kTSlab * NP);   // halves
-                uint8_t* dst = xbase + si * 2 * xb;
-                mbar_expect_tx(&S.xfull[si], 2 * xb);
-                bulk_g2s(dst, a.xh + off, xb, &S.xfull[si]);
-                bulk_g2s(dst + xb, a.xl + off, xb, &S.xfull[si]);
-                armed = i + 1;
+            uint32_t i = 0;                                             // slabs issued
+            bool ok = true;
+            for (uint32_t t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
+                const TTile T = tg_tile(a, t);
+                for (uint32_t s = T.sl0; s < T.sl1; s++) {
+                    const uint32_t si = i % NS, ph = i / NS;
+                    if (ph > 0 && !tg_wait(S, &S.xempty[si], (ph - 1) & 1u, a.err)) { ok = false; break; }
+                    const uint64_t off = (uint64_t)s * (kTSlab * NP);   // halves
+                    uint8_t* dst = xbase + si * 2 * xb;
+                    mbar_expect_tx(&S.xfull[si], 2 * xb);
+                    bulk_g2s(dst, a.xh + off, xb, &S.xfull[si]);
+                    bulk_g2s(dst + xb, a.xl + off, xb, &S.xfull[si]);
+                    i++;
+                }
             }
-            for (uint32_t i = (armed > NS ? armed - NS : 0); i < armed; i++) tg_drain(&S.xfull[i % NS], (i / NS) & 1u);
+            for (uint32_t u = (i > NS ? i - NS : 0); u < i; u++) tg_drain(&S.xfull[u % NS], (u / NS) & 1u);
         }
         __syncwarp();
-    } else if (warp == kTWarpMma) {
-        // ------------------------------------------------ tensor-core issue
+    } else if (warp >= kTWarpMma && warp < kTWarpMma + kTIssuers) {
+        // ------------------------------------------------ tensor-core issue: chain ch accumulates
+        // w_hi x_hi (0), w_hi x_lo (1) or w_lo x_hi (2); MMAs from several threads
+        // overlap in the tensor pipe where one thread's would wait on each other
+        const uint32_t ch = warp - kTWarpMma;
         if (lane == 0) {
             const uint32_t idesc = umma_idesc_f16(kTRows, NP);
-            const bool lo = G.type != T_F16;                            // F16 weights are exact in hi
-            uint32_t issued = 0;
-            for (uint32_t i = 0; i < sl1 - sl0; i++) {
-                const uint32_t si = i % NS, t = i / NS;
-                if (!tg_wait(S, &S.afull[si], t & 1u, a.err) || !tg_wait(S, &S.xfull[si], t & 1u, a.err)) break;
+            uint32_t i = 0, tl = 0;                                     // slabs, tiles consumed
+            bool ok = true;
+            for (uint32_t t = blockIdx.x; ok && t < ntiles; t += gridDim.x, tl++) {
+                const TTile T = tg_tile(a, t);
+                const bool work = ch != 2 || a.seg[T.seg].type != T_F16;   // F16 weights are exact in hi
+                const uint32_t ab = tl & 1u, aph = tl >> 1;
+                if (aph > 0 && !tg_wait(S, &S.acce[ab], (aph - 1) & 1u, a.err)) break;
                 tc_fence_after();
-                const uint32_t ah = smem_u32(abase + si * 2 * kTATile), al = ah + kTATile;
-                const uint32_t xh = smem_u32(xbase + si * 2 * (128 * NP)), xl = xh + 128 * NP;
+                const uint32_t d = tmem + ab * kTSetCols + ch * kTAccW;      // this chain's accumulator
+                for (uint32_t s = T.sl0; s < T.sl1; s++, i++) {
+                    const uint32_t si = i % NS, ai = i % kTNA;
+                    if (!tg_wait(S, &S.afull[ai], (i / kTNA) & 1u, a.err) || !tg_wait(S, &S.xfull[si], (i / NS) & 1u, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t at = tmem + kTACol0 + ai * kTACols + (ch == 2 ? kTACols / 2 : 0u);   // A hi or lo
+                    const uint32_t xt = smem_u32(xbase + si * 2 * (128 * NP)) + (ch == 1 ? 128 * NP : 0u);  // x hi or lo
+                    if (work) {
 #pragma unroll
-                for (uint32_t kk = 0; kk < kTSlab / 16; kk++) {
-                    const uint64_t dah = umma_desc(ah + kk * 32 * kTRows, 16 * kTRows, 128);
-                    const uint64_t dal = umma_desc(al + kk * 32 * kTRows, 16 * kTRows, 128);
-                    const uint64_t dxh = umma_desc(xh + kk * 32 * NP, 16 * NP, 128);
-                    const uint64_t dxl = umma_desc(xl + kk * 32 * NP, 16 * NP, 128);
-                    umma_f16(tmem, dah, dxh, idesc, (i | kk) != 0);
-                    umma_f16(tmem, dah, dxl, idesc, 1);
-                    if (lo) umma_f16(tmem, dal, dxh, idesc, 1);
+                        for (uint32_t kk = 0; kk < kTSlab / 16; kk++)
+                            umma_f16_ts(d, at + 8 * kk, umma_desc(xt + kk * 32 * NP, 16 * NP, 128), idesc,
+                                        (s != T.sl0 || kk != 0) ? 1u : 0u);
+                    }
+                    umma_commit(&S.aempty[ai]);
+                    umma_commit(&S.xempty[si]);
                 }
-                umma_commit(&S.sempty[si]);
-                issued = i + 1;
+                if (ok) umma_commit(&S.accf[ab]);
             }
-            umma_commit(&S.accf);
-            if (issued < sl1 - sl0) tg_drain(&S.accf, 0);               // aborted: let issued MMAs finish
+            // every issued MMA has finished before the tensor memory is freed
+            umma_commit(&S.mdone);
+            tg_drain(&S.mdone, 0);
         }
         __syncwarp();
-    } else {
-        // ------------------------------------------------ dequant, then epilogue
-        const uint32_t r = tid & (kTRows - 1), c = tid >> 7;           // row, 32-element run of the slab
-        const bool valid = row0 + r < G.rows;
-        uint32_t rng = 0;
-        for (uint32_t i = 0; i < sl1 - sl0; i++) {
-            const uint32_t s = sl0 + i, si = i % NS, t = i / NS;
-            const uint32_t lr = s / spr - ur0, buf = lr % kTRaw, first = s % spr == 0;
-            if (first && !tg_wait_warp(S, &S.raw_full[buf], (lr / kTRaw) & 1u, a.err)) break;
-            if (t > 0 && !tg_wait_warp(S, &S.sempty[si], (t - 1) & 1u, a.err)) break;
-            uint8_t* ahi = abase + si * 2 * kTATile + c * 4 * (16 * kTRows) + 16 * r;
-            uint8_t* alo = ahi + kTATile;
-            if (!valid) {
-#pragma unroll
-                for (int sl = 0; sl < 4; sl++) {
-                    *reinterpret_cast<uint4*>(ahi + sl * (16 * kTRows)) = make_uint4(0, 0, 0, 0);
-                    *reinterpret_cast<uint4*>(alo + sl * (16 * kTRows)) = make_uint4(0, 0, 0, 0);
-                }
-            } else {
-                const uint64_t o = (uint64_t)(row0 + r) * G.row_bytes + (uint64_t)(s / spr) * G.ub;
-                const uint8_t* p = rbase + buf * a.raw_bytes + r * G.rrs + (uint32_t)(o & 15u);
-                const uint32_t j = (s % spr) * 2 + c;                  // run within the raw unit
-                if (G.type == T_F16) {
-                    const uint8_t* b = p + 64 * j;
-#pragma unroll
-                    for (int sl = 0; sl < 4; sl++) {
-                        *reinterpret_cast<uint4*>(ahi + sl * (16 * kTRows)) = *reinterpret_cast<const uint4*>(b + 16 * sl);
-                        *reinterpret_cast<uint4*>(alo + sl * (16 * kTRows)) = make_uint4(0, 0, 0, 0);
-                    }
-                } else {
-                    float w[32];
-                    switch (G.type) {
-                    case T_Q4_K: dq_q4k(p, j, w); break;
-                    case T_Q6_K: dq_q6k(p, j, w); break;
-                    case T_Q8_0: dq_q80(p, j, w); break;
-                    default: dq_q40(p, j, w); break;
-                    }
-                    float m = 0.f;
-#pragma unroll
-                    for (int e = 0; e < 32; e++) m = fmaxf(m, fabsf(w[e]));
-                    if (!(m <= 65504.f)) rng = 1;                      // overflow (or NaN) in fp16
-                    tstore(ahi, alo, w);
-                }
-            }
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                tg_arrive(&S.afull[si]);
-                if ((s + 1) % spr == 0) tg_arrive(&S.raw_empty[buf]);
-            }
-        }
-        if (rng && a.err) atomicOr(a.err, kTErrRange);
-        // epilogue: warp w reads lanes 32 (w % 4) .. +31 (its rows), column
-        // chunks of 16 starting at chunk w / 4, step 2
-        const bool ok = tg_wait_warp(S, &S.accf, 0, a.err);
-        tc_fence_after();
-        if (ok) {
-            const uint32_t q = warp & 3u;
-            const uint32_t row = row0 + 32 * q + lane;
-            float* part = G.part + (uint64_t)ks * a.B * G.rows;
-            for (uint32_t cc = warp >> 2; 16 * cc < NP; cc += 2) {
-                uint32_t v[16];
-                tmem_ld16(tmem + ((32u * q) << 16) + 16 * cc, v);
+    } else if (warp >= kTWarpEpi) {
+        // ------------------------------------------------ epilogue
+        const uint32_t q = warp & 3u;                                   // tensor-memory lanes 32q..32q+31
+        uint32_t tl = 0;
+        for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x, tl++) {
+            const TTile T = tg_tile(a, t);
+            const TSeg& G = a.seg[T.seg];
+            const uint32_t ab = tl & 1u;
+            if (!tg_wait_warp(S, &S.accf[ab], (tl >> 1) & 1u, a.err)) break;
+            tc_fence_after();
+            const uint32_t row = T.row0 + 32 * q + lane;
+            const bool lo = G.type != T_F16;
+            float* part = G.part + (uint64_t)T.ks * a.B * G.rows;
+            const uint32_t tb = tmem + ((32u * q) << 16) + ab * kTSetCols;
+            for (uint32_t cc = 0; 16 * cc < NP; cc++) {
+                uint32_t vh[16], vx[16], vl[16];
+                tmem_ld16(tb + 16 * cc, vh);
+                tmem_ld16(tb + kTAccW + 16 * cc, vx);
+                if (lo) tmem_ld16(tb + 2 * kTAccW + 16 * cc, vl);
                 if (row < G.rows) {
 #pragma unroll
                     for (int e = 0; e < 16; e++) {
                         const uint32_t b = 16 * cc + e;
-                        if (b < a.B) part[(uint64_t)b * G.rows + row] = __uint_as_float(v[e]) * 5.9604644775390625e-08f;
+                        float v = __uint_as_float(vh[e]) + __uint_as_float(vx[e]);
+                        if (lo) v += __uint_as_float(vl[e]);
+                        if (b < a.B) part[(uint64_t)b * G.rows + row] = v * 5.9604644775390625e-08f;
                     }
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tg_arrive(&S.acce[ab]);
         }
+    } else {
+        // ------------------------------------------------ dequant
+        const uint32_t grp = warp / kTGroupWarps;                      // decodes the slabs i with i % 2 == grp
+        const uint32_t r = tid & (kTRows - 1), c = (tid >> 7) & 1u;    // row, 32-element run of the slab
+        uint32_t i = 0, lr = 0;                                         // slabs, raw units consumed
+        bool ok = true, inrange = true;
+        for (uint32_t t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
+            const TTile T = tg_tile(a, t);
+            const TSeg& G = a.seg[T.seg];
+            const uint32_t spr = G.ru / kTSlab;
+            const bool valid = T.row0 + r < G.rows;
+            uint32_t cur = 0;
+            for (uint32_t s = T.sl0; s < T.sl1; s++, i++) {
+                const uint32_t ai = i % kTNA, aph = i / kTNA;
+                if (s % spr == 0) {
+                    cur = lr++;
+                    if (!tg_wait_warp(S, &S.raw_full[cur % kTRaw], (cur / kTRaw) & 1u, a.err)) { ok = false; break; }
+                }
+                const bool mine = (i & 1u) == grp;
+                if (!mine) {
+                    if ((s + 1) % spr == 0) {
+                        __syncwarp();
+                        if (lane == 0) tg_arrive(&S.raw_empty[cur % kTRaw]);
+                    }
+                    continue;
+                }
+                uint32_t h[16], l[16];
+                if (!valid) {
+#pragma unroll
+                    for (int e = 0; e < 16; e++) h[e] = l[e] = 0;
+                } else {
+                    const uint64_t o = (uint64_t)(T.row0 + r) * G.row_bytes + (uint64_t)(s / spr) * G.ub;
+                    const uint8_t* p = rbase + (cur % kTRaw) * a.raw_bytes + r * G.rrs + (uint32_t)(o & 15u);
+                    const uint32_t j = (s % spr) * 2 + c;              // run within the raw unit
+                    bool fine;
+                    switch (G.type) {
+                    case T_Q4_K: fine = dq_q4k(p, j, h, l); break;
+                    case T_Q6_K: fine = dq_q6k(p, j, h, l); break;
+                    case T_Q8_0: fine = dq_q80(p, j, h, l); break;
+                    case T_Q4_0: fine = dq_q40(p, j, h, l); break;
+                    default: fine = dq_f16(p, j, h, l); break;
+                    }
+                    inrange = inrange && fine;
+                }
+                // the A stage is free once the MMAs of slab i - kTNA have read it
+                if (aph > 0 && !tg_wait_warp(S, &S.aempty[ai], (aph - 1) & 1u, a.err)) { ok = false; break; }
+                tc_fence_after();
+                // this warp's rows are tensor-memory lanes 32 (warp % 4) .. +31; run c
+                // is K columns 16c .. 16c + 15 of the stage's hi and lo halves
+                const uint32_t ta = tmem + ((32u * (warp & 3u)) << 16) + kTACol0 + ai * kTACols + 16 * c;
+                tmem_st16(ta, h);
+                tmem_st16(ta + kTACols / 2, l);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    tg_arrive(&S.afull[ai]);
+                    if ((s + 1) % spr == 0) tg_arrive(&S.raw_empty[cur % kTRaw]);
+                }
+            }
+        }
+        if (!inrange && a.err) atomicOr(a.err, kTErrRange);
     }
     tc_fence_before();
     __syncthreads();
@@ -478,18 +644,57 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
 
 bool tgemm_type(uint32_t t) { return t == T_Q4_K || t == T_Q6_K || t == T_Q8_0 || t == T_Q4_0 || t == T_F16; }
 
-static uint32_t tg_ru(uint32_t type) { return (type == T_Q4_K || type == T_Q6_K) ? 256u : 64u; }
-static uint32_t tg_ub(uint32_t type) {
+// Elements per raw unit: a K-quant super-block; eight 32-element blocks when K
+// allows (a 16-byte multiple of bytes: one TMA box per unit); F16 64 elements.
+static uint32_t tg_ru(uint32_t type, uint32_t K) {
+    if (type == T_Q4_K || type == T_Q6_K) return 256;
+    if (type == T_F16) return 64;
+    return K % 256 == 0 ? 256u : 64u;
+}
+static uint32_t tg_ub(uint32_t type, uint32_t ru) {
     switch (type) {
     case T_Q4_K: return 144;
     case T_Q6_K: return 210;
-    case T_Q8_0: return 68;     // two 32-element blocks
-    case T_Q4_0: return 36;
-    default: return 128;        // F16
+    case T_Q8_0: return ru / 32 * 34;
+    case T_Q4_0: return ru / 32 * 18;
+    default: return ru * 2;     // F16
     }
 }
 
-size_t tgemm_smem(const TGemmArgs& a) { return (size_t)a.stages * tg_stage_bytes(a.NP) + (size_t)kTRaw * a.raw_bytes; }
+// cuTensorMapEncodeTiled from the driver, looked up once.
+static PFN_cuTensorMapEncodeTiled_v12000 tg_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+// 2-D map of a segment's rows as uint16 elements: box = rrs bytes x 128 rows,
+// no swizzle; rows past the end read as zeros.
+static bool tg_encode(CUtensorMap* m, const TSeg& S) {
+    PFN_cuTensorMapEncodeTiled_v12000 fn = tg_encoder();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {S.row_bytes / 2, S.rows};
+    cuuint64_t strides[1] = {S.row_bytes};
+    cuuint32_t box[2] = {S.rrs / 2, kTRows};
+    cuuint32_t es[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint8_t*>(S.w), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// At least kTSmemMin: two CTAs never share an SM (each allocates 512
+// tensor-memory columns; a second one would wait for the first to finish).
+constexpr size_t kTSmemMin = 120 * 1024;
+size_t tgemm_smem(const TGemmArgs& a) {
+    const size_t n = kTAlign + (size_t)a.stages * tg_stage_bytes(a.NP) + (size_t)kTRaw * a.raw_bytes + kTSlack;
+    return n > kTSmemMin ? n : kTSmemMin;
+}
 
 bool tgemm_init() {
     return LM_CUDA(cudaFuncSetAttribute(tgemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTSmemMax));
@@ -502,30 +707,51 @@ bool tgemm_plan(TGemmArgs& a, uint32_t sms) {
     a.NP = (a.B + 15) & ~15u;
     bool kq = false;
     uint32_t rbs = 0, raw = 0;
+    a.tma = 1;
     for (uint32_t i = 0; i < a.nseg; i++) {
         TSeg& S = a.seg[i];
         if (!tgemm_type(S.type) || S.rows == 0) return false;
         if (reinterpret_cast<uintptr_t>(S.w) % 16 != 0) return false;
         if (S.row_bytes != type_bytes(S.type, a.K)) return false;
         kq = kq || S.type == T_Q4_K || S.type == T_Q6_K;
-        S.ru = tg_ru(S.type);
-        S.ub = tg_ub(S.type);
-        uint32_t rrs = (S.ub + 15 + 4 + 15) & ~15u;        // alignment delta + one word of over-read
-        if ((rrs / 16) % 2 == 0) rrs += 16;                // odd count of 16-byte units: rows over all banks
-        S.rrs = rrs;
-        raw = raw > kTRows * rrs ? raw : kTRows * rrs;
+        S.ru = tg_ru(S.type, a.K);
+        S.ub = tg_ub(S.type, S.ru);
+        if (S.row_bytes % 16 != 0) a.tma = 0;             // TMA needs 16-byte row strides
         S.rb0 = rbs;
         rbs += (S.rows + kTRows - 1) / kTRows;
     }
+    for (uint32_t i = 0; i < a.nseg; i++) {
+        TSeg& S = a.seg[i];
+        if (a.tma) {
+            // the box starts at the 16-byte boundary at or below each unit (the
+            // byte offset of a unit is even: at most 14 bytes of lead-in)
+            S.rrs = S.ub % 16 == 0 ? S.ub : (S.ub + 14 + 15) & ~15u;
+        } else {
+            uint32_t rrs = (S.ub + 15 + 4 + 15) & ~15u;    // alignment delta + one word of over-read
+            if ((rrs / 16) % 2 == 0) rrs += 16;            // odd count of 16-byte units: rows over all banks
+            S.rrs = rrs;
+        }
+        raw = raw > kTRows * S.rrs ? raw : kTRows * S.rrs;
+    }
+    if (a.tma)
+        for (uint32_t i = 0; i < a.nseg; i++)
+            if (!tg_encode(&a.tmap[i], a.seg[i])) a.tma = 0;
+    if (!a.tma)                                           // cp.async copies: the padded row stride
+        for (uint32_t i = 0; i < a.nseg; i++) {
+            TSeg& S = a.seg[i];
+            uint32_t rrs = (S.ub + 15 + 4 + 15) & ~15u;
+            if ((rrs / 16) % 2 == 0) rrs += 16;
+            S.rrs = rrs;
+            raw = raw > kTRows * rrs ? raw : kTRows * rrs;
+        }
     a.ue = a.K % 256 == 0 ? 256u : 64u;
     if (kq && a.ue != 256) return false;
     a.raw_bytes = raw;
     a.stages = 0;
     for (uint32_t ns = kTMaxStages; ns >= 2; ns--)
-        if ((size_t)ns * tg_stage_bytes(a.NP) + (size_t)kTRaw * raw <= kTSmemMax) { a.stages = ns; break; }
+        if (kTAlign + (size_t)ns * tg_stage_bytes(a.NP) + (size_t)kTRaw * raw + kTSlack <= kTSmemMax) { a.stages = ns; break; }
     if (a.stages == 0) return false;
-    a.tcols = 32;
-    while (a.tcols < a.NP) a.tcols *= 2;
+    a.tcols = kTCols;                                    // accumulators + A stages
     // K split: the fewest units per CTA among the splits whose waves x units
     // per CTA is smallest (one CTA per SM)
     const uint32_t units = a.K / a.ue;
@@ -540,11 +766,12 @@ bool tgemm_plan(TGemmArgs& a, uint32_t sms) {
     a.ups = best;
     a.ksplit = (units + best - 1) / best;
     a.rblocks = rbs;
+    a.grid = rbs * a.ksplit < sms ? rbs * a.ksplit : sms;
     return true;
 }
 
 bool launch_tgemm(const TGemmArgs& a, cudaStream_t st) {
-    tgemm_kernel<<<dim3(a.rblocks, a.ksplit), kTThreads, tgemm_smem(a), st>>>(a);
+    tgemm_kernel<<<a.grid, kTThreads, tgemm_smem(a), st>>>(a);
     return LM_CUDA(cudaGetLastError());
 }
 
