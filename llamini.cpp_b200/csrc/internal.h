@@ -273,7 +273,21 @@ struct BFinishArgs {
     float* out = nullptr;          // out[b * ldo + r]
     uint32_t ldo = 0;
     unsigned long long* keys = nullptr;   // [B] argmax keys (or null)
+    // up to two more segments whose rows follow in the output row (q, k and v
+    // of one launch; EPI_STORE only): their partial sums, rows and biases
+    const float* part_b = nullptr;
+    const float* part_c = nullptr;
+    const float* bias_b = nullptr;
+    const float* bias_c = nullptr;
+    uint32_t rows_b = 0, rows_c = 0;
 };
+// Finish of one matrix whose output a staging for the next matrix reads at
+// once: one CTA per sequence does both (k_bgemm.cu).
+struct BFinStageArgs {
+    BFinishArgs f;                 // single segment; f.out receives the finished rows
+    BStageArgs s;                  // s.x / s.ldx unused: the finished rows are staged (s.K == f.rows)
+};
+bool launch_bfinstage(const BFinStageArgs& a, cudaStream_t st);
 struct BEmbedArgs {
     const StepState* st;           // pos (shared by the batch)
     const uint32_t* tokens;        // [B][tok_stride]
@@ -304,6 +318,7 @@ bool launch_bstage(const BStageArgs& a, cudaStream_t st);
 struct TSeg {
     const uint8_t* w = nullptr;
     uint64_t row_bytes = 0;
+    uint64_t pitch = 0;            // bytes between rows (0: row_bytes)
     uint32_t type = 0, rows = 0;
     float* part = nullptr;         // [ksplit][B][rows] raw sums
     // filled by tgemm_plan: first row block, elements per raw unit, bytes of

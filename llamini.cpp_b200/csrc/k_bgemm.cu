@@ -61,37 +61,34 @@ __device__ float bblock_max(float v, float* red) {
     return t;
 }
 
-// One sequence per CTA (blockIdx.x), 256 threads.
-__global__ void __launch_bounds__(256) bstage_kernel(const BStageArgs a) {
-    extern __shared__ __align__(16) float xf[];          // K floats
-    __shared__ float red[32];
-    const uint32_t b = blockIdx.x, K = a.K, tid = threadIdx.x;
-    const float* x = a.x + (uint64_t)b * a.ldx;
+// Stage sequence b's K values, already in shared memory xf (complete on
+// entry): RMSNorm (model.c:4-10) or LayerNorm (gpt2.c:130-139) in place, then
+// x * 2^E_b split into fp16 hi/lo. Called by every thread of the CTA.
+__device__ void stage_core(const BStageArgs& a, float* xf, uint32_t b, float* red) {
+    const uint32_t K = a.K, tid = threadIdx.x;
     float f = 1.0f;
-    if (a.norm == NORM_RMS) {                            // model.c:4-10
+    if (a.norm == NORM_RMS) {
         float s = 0.f;
         for (uint32_t i = tid; i < K; i += blockDim.x) {
-            const float v = x[i];
+            const float v = xf[i];
             s = fmaf(v, v, s);
             xf[i] = v * a.norm_w[i];
         }
         s = bblock_sum(s, red);
         f = 1.0f / sqrtf(s / (float)K + a.eps);
-    } else if (a.norm == NORM_LAYER) {                   // gpt2.c:130-139, two passes
+    } else if (a.norm == NORM_LAYER) {                   // two passes: mean, then variance
         float s = 0.f;
-        for (uint32_t i = tid; i < K; i += blockDim.x) s += x[i];
+        for (uint32_t i = tid; i < K; i += blockDim.x) s += xf[i];
         s = bblock_sum(s, red);
         const float mean = s / (float)K;
         float vs = 0.f;
         for (uint32_t i = tid; i < K; i += blockDim.x) {
-            const float c = x[i] - mean;
+            const float c = xf[i] - mean;
             vs = fmaf(c, c, vs);
         }
         vs = bblock_sum(vs, red);
         const float inv = 1.0f / sqrtf(vs / (float)K + a.eps);
-        for (uint32_t i = tid; i < K; i += blockDim.x) xf[i] = (x[i] - mean) * inv * a.norm_w[i] + a.norm_b[i];
-    } else {
-        for (uint32_t i = tid; i < K; i += blockDim.x) xf[i] = x[i];
+        for (uint32_t i = tid; i < K; i += blockDim.x) xf[i] = (xf[i] - mean) * inv * a.norm_w[i] + a.norm_b[i];
     }
     float m = 0.f;
     for (uint32_t i = tid; i < K; i += blockDim.x) m = fmaxf(m, fabsf(xf[i]));
@@ -149,6 +146,17 @@ __global__ void __launch_bounds__(256) bstage_kernel(const BStageArgs a) {
         }
     }
     if (tid == 0) a.oscale[b] = __int_as_float((127 + 24 - E) << 23);   // 2^(24-E)
+}
+
+// One sequence per CTA (blockIdx.x).
+__global__ void __launch_bounds__(1024) bstage_kernel(const BStageArgs a) {
+    extern __shared__ __align__(16) float xf[];          // K floats
+    __shared__ float red[32];
+    const uint32_t b = blockIdx.x;
+    const float* x = a.x + (uint64_t)b * a.ldx;
+    for (uint32_t i = threadIdx.x; i < a.K; i += blockDim.x) xf[i] = x[i];
+    __syncthreads();
+    stage_core(a, xf, b, red);
 }
 
 // ---------------------------------------------------------------- GEMM
@@ -305,28 +313,47 @@ __device__ __forceinline__ unsigned long long bkey(float v, uint32_t idx) {
     return ((unsigned long long)o << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
 }
 
-// grid (ceil(rows / 256), B)
+// Row r of sequence b of a single-segment finish: the K-range partials summed
+// in order, scaled by sc, then the epilogue; stores and returns the value.
+__device__ __forceinline__ float bfin_row(const BFinishArgs& a, uint32_t b, uint32_t r, float sc) {
+    float v = 0.f, w = 0.f;
+    for (uint32_t k = 0; k < a.ksplit; k++) v += a.part[((uint64_t)k * a.B + b) * a.rows + r];
+    v *= sc;
+    if (a.part2) {
+        for (uint32_t k = 0; k < a.ksplit; k++) w += a.part2[((uint64_t)k * a.B + b) * a.rows + r];
+        w *= sc;
+    }
+    float* o = a.out + (uint64_t)b * a.ldo + r;
+    switch (a.epi) {
+    case EPI_STORE: if (a.bias) v += a.bias[r]; break;
+    case EPI_RESID: if (a.bias) v += a.bias[r]; v = *o + v; break;
+    case EPI_GLU_SILU: v = v / (1.0f + expf(-v)) * w; break;       // model.c:22
+    case EPI_GLU_GELU: v = bgelu(v) * w; break;
+    case EPI_GELU: if (a.bias) v += a.bias[r]; v = bgelu(v); break;
+    }
+    *o = v;
+    return v;
+}
+
+// grid (ceil((rows + rows_b + rows_c) / 256), B)
 __global__ void __launch_bounds__(256) bfinish_kernel(const BFinishArgs a) {
     const uint32_t b = blockIdx.y, r = blockIdx.x * blockDim.x + threadIdx.x;
     unsigned long long key = 0ull;
+    const float sc = a.oscale[b];
     if (r < a.rows) {
-        const float sc = a.oscale[b];
-        float v = 0.f, w = 0.f;
-        for (uint32_t k = 0; k < a.ksplit; k++) v += a.part[((uint64_t)k * a.B + b) * a.rows + r];
-        v *= sc;
-        if (a.part2) {
-            for (uint32_t k = 0; k < a.ksplit; k++) w += a.part2[((uint64_t)k * a.B + b) * a.rows + r];
-            w *= sc;
-        }
-        float* o = a.out + (uint64_t)b * a.ldo + r;
-        switch (a.epi) {
-        case EPI_STORE: if (a.bias) v += a.bias[r]; *o = v; break;
-        case EPI_RESID: if (a.bias) v += a.bias[r]; *o = *o + v; break;
-        case EPI_GLU_SILU: v = v / (1.0f + expf(-v)) * w; *o = v; break;       // model.c:22
-        case EPI_GLU_GELU: v = bgelu(v) * w; *o = v; break;
-        case EPI_GELU: if (a.bias) v += a.bias[r]; v = bgelu(v); *o = v; break;
-        }
+        const float v = bfin_row(a, b, r, sc);
         if (a.keys) key = bkey(v, r);
+    } else if (r < a.rows + a.rows_b + a.rows_c) {
+        // a further segment: its own partials, rows and bias; plain store
+        const bool sb = r < a.rows + a.rows_b;
+        const uint32_t rr = sb ? r - a.rows : r - a.rows - a.rows_b, n = sb ? a.rows_b : a.rows_c;
+        const float* part = sb ? a.part_b : a.part_c;
+        const float* bias = sb ? a.bias_b : a.bias_c;
+        float v = 0.f;
+        for (uint32_t k = 0; k < a.ksplit; k++) v += part[((uint64_t)k * a.B + b) * n + rr];
+        v *= sc;
+        if (bias) v += bias[rr];
+        a.out[(uint64_t)b * a.ldo + r] = v;
     }
     if (a.keys) {
 #pragma unroll
@@ -336,6 +363,18 @@ __global__ void __launch_bounds__(256) bfinish_kernel(const BFinishArgs a) {
         }
         if ((threadIdx.x & 31u) == 0 && key != 0ull) atomicMax(a.keys + b, key);
     }
+}
+
+// One CTA per sequence: finish every row of the matrix into f.out and shared
+// memory, then stage those rows for the next matrix.
+__global__ void __launch_bounds__(1024) bfinstage_kernel(const BFinStageArgs a) {
+    extern __shared__ __align__(16) float xf[];          // f.rows floats
+    __shared__ float red[32];
+    const uint32_t b = blockIdx.x;
+    const float sc = a.f.oscale[b];                      // read before the staging rewrites it
+    for (uint32_t r = threadIdx.x; r < a.f.rows; r += blockDim.x) xf[r] = bfin_row(a.f, b, r, sc);
+    __syncthreads();
+    stage_core(a.s, xf, b, red);
 }
 
 // ---------------------------------------------------------------- host side
@@ -361,7 +400,8 @@ bool bgemm_init() {
            LM_CUDA(cudaFuncSetAttribute(bgemm_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBSmemMax)) &&
            LM_CUDA(cudaFuncSetAttribute(bgemm_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBSmemMax)) &&
            LM_CUDA(cudaFuncSetAttribute(bgemm_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBSmemMax)) &&
-           LM_CUDA(cudaFuncSetAttribute(bstage_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
+           LM_CUDA(cudaFuncSetAttribute(bstage_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024)) &&
+           LM_CUDA(cudaFuncSetAttribute(bfinstage_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
 }
 
 // Fill the launch geometry of `a` (segments, B, K and partial buffers set by
@@ -426,12 +466,21 @@ bool launch_bgemm(const BGemmArgs& a, cudaStream_t st) {
 
 bool launch_bstage(const BStageArgs& a, cudaStream_t st) {
     if (a.K % 4 != 0 || a.K > 16384) { set_error("batch staging: K %u", a.K); return false; }
-    bstage_kernel<<<a.B, 256, (size_t)a.K * 4, st>>>(a);
+    bstage_kernel<<<a.B, 1024, (size_t)a.K * 4, st>>>(a);
+    return LM_CUDA(cudaGetLastError());
+}
+
+bool launch_bfinstage(const BFinStageArgs& a, cudaStream_t st) {
+    if (a.s.K != a.f.rows || a.s.K % 4 != 0 || a.s.K > 16384 || a.f.rows_b || a.f.rows_c || a.f.keys) {
+        set_error("batch finish+staging: rows %u, K %u", a.f.rows, a.s.K);
+        return false;
+    }
+    bfinstage_kernel<<<a.f.B, 1024, (size_t)a.s.K * 4, st>>>(a);
     return LM_CUDA(cudaGetLastError());
 }
 
 bool launch_bfinish(const BFinishArgs& a, cudaStream_t st) {
-    bfinish_kernel<<<dim3((a.rows + 255) / 256, a.B), 256, 0, st>>>(a);
+    bfinish_kernel<<<dim3((a.rows + a.rows_b + a.rows_c + 255) / 256, a.B), 256, 0, st>>>(a);
     return LM_CUDA(cudaGetLastError());
 }
 

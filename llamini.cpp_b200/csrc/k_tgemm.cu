@@ -459,7 +459,7 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
                     // covering each row's unit, lanes 0-15 on even rows, 16-31 on odd rows
                     const uint32_t ch = lane & 15u;
                     for (uint32_t r = lane >> 4; r < kTRows && T.row0 + r < G.rows; r += 2) {
-                        const uint64_t o = (uint64_t)(T.row0 + r) * G.row_bytes + (uint64_t)ur * G.ub;
+                        const uint64_t o = (uint64_t)(T.row0 + r) * G.pitch + (uint64_t)ur * G.ub;
                         const uint64_t a16 = o & ~uint64_t(15);
                         const uint32_t nch = (uint32_t)((((o + G.ub + 15) & ~uint64_t(15)) - a16) >> 4);
                         if (ch < nch) tg_cpa16(dst + r * G.rrs + 16 * ch, G.w + a16 + 16 * ch);
@@ -600,7 +600,7 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
 #pragma unroll
                     for (int e = 0; e < 16; e++) h[e] = l[e] = 0;
                 } else {
-                    const uint64_t o = (uint64_t)(T.row0 + r) * G.row_bytes + (uint64_t)(s / spr) * G.ub;
+                    const uint64_t o = (uint64_t)(T.row0 + r) * G.pitch + (uint64_t)(s / spr) * G.ub;
                     const uint8_t* p = rbase + (cur % kTRaw) * a.raw_bytes + r * G.rrs + (uint32_t)(o & 15u);
                     const uint32_t j = (s % spr) * 2 + c;              // run within the raw unit
                     bool fine;
@@ -679,8 +679,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 tg_encoder() {
 static bool tg_encode(CUtensorMap* m, const TSeg& S) {
     PFN_cuTensorMapEncodeTiled_v12000 fn = tg_encoder();
     if (!fn) return false;
-    cuuint64_t dims[2] = {S.row_bytes / 2, S.rows};
-    cuuint64_t strides[1] = {S.row_bytes};
+    cuuint64_t dims[2] = {S.pitch / 2, S.rows};
+    cuuint64_t strides[1] = {S.pitch};
     cuuint32_t box[2] = {S.rrs / 2, kTRows};
     cuuint32_t es[2] = {1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint8_t*>(S.w), dims, strides, box, es,
@@ -713,10 +713,12 @@ bool tgemm_plan(TGemmArgs& a, uint32_t sms) {
         if (!tgemm_type(S.type) || S.rows == 0) return false;
         if (reinterpret_cast<uintptr_t>(S.w) % 16 != 0) return false;
         if (S.row_bytes != type_bytes(S.type, a.K)) return false;
+        if (S.pitch == 0) S.pitch = S.row_bytes;
+        if (S.pitch < S.row_bytes) return false;
         kq = kq || S.type == T_Q4_K || S.type == T_Q6_K;
         S.ru = tg_ru(S.type, a.K);
         S.ub = tg_ub(S.type, S.ru);
-        if (S.row_bytes % 16 != 0) a.tma = 0;             // TMA needs 16-byte row strides
+        if (S.pitch % 16 != 0) a.tma = 0;                 // TMA needs 16-byte row strides
         S.rb0 = rbs;
         rbs += (S.rows + kTRows - 1) / kTRows;
     }

@@ -21,6 +21,7 @@
 #include <cstring>
 #include <cmath>
 #include <ctime>
+#include <unordered_map>
 #include <vector>
 
 struct llamini_session {
@@ -832,6 +833,9 @@ struct llamini_batch {
     u32 *counters = nullptr, *tokens = nullptr, *n_prompt = nullptr;
     u32* err = nullptr;               // tensor-core GEMM error bits
     bool tc = false;                  // matrices on the tcgen05 GEMM (else mma.sync)
+    // copies of matrices whose row size is not a multiple of 16 bytes, rows
+    // padded to one (the tensor-core GEMM loads rows by TMA): pointer, pitch
+    std::unordered_map<const uint8_t*, std::pair<const uint8_t*, uint64_t>> pitched;
     unsigned long long* keys = nullptr;
     void *kc = nullptr, *vc = nullptr;
     lm::StepState* st = nullptr;
@@ -886,6 +890,11 @@ bool batch_gemm(const llamini_batch* b, const DevMat* const* m, float* const* pa
             g.seg[i].type = m[i]->type;
             g.seg[i].rows = m[i]->rows;
             g.seg[i].part = parts[i];
+            const auto it = b->pitched.find(m[i]->ptr);
+            if (it != b->pitched.end()) {
+                g.seg[i].w = it->second.first;
+                g.seg[i].pitch = it->second.second;
+            }
         }
         if (!tgemm_plan(g, (u32)sm_count())) return false;
     } else {
@@ -1068,12 +1077,182 @@ bool batch_enqueue_step(llamini_batch* b, cudaStream_t st) {
     return launch_btoken(t, st);
 }
 
+// The step on the tensor-core GEMM: each finish whose output is the next
+// matrix's input also stages that input (one kernel per sequence), and q, k
+// and v finish in one launch.
+bool batch_enqueue_step_tc(llamini_batch* b, cudaStream_t st) {
+    llamini_session* s = b->w;
+    const bool gpt2 = s->kind == 1;
+    const u32 qkvd = s->qd + 2 * s->kvd;
+    const u32 L = s->n_layers;
+    float* osc = b->sx + (size_t)b->max_batch * (b->kmax / 16);
+    BEmbedArgs e;
+    e.st = b->st;
+    e.tokens = b->tokens;
+    e.tok_stride = b->max_seq + 1;
+    e.tok = s->tok;
+    e.pos = s->pos_tab;
+    e.scale = s->emb_scale;
+    e.hidden = b->hidden;
+    e.dim = s->dim;
+    if (!launch_bembed(e, b->B, st)) return false;
+    const u32 norm = gpt2 ? NORM_LAYER : NORM_RMS;
+    auto stage_args = [&](u32 K, u32 nm, const float* w, const float* bias) {
+        BStageArgs a;
+        a.K = K;
+        a.B = b->B;
+        a.norm = nm;
+        a.norm_w = w;
+        a.norm_b = bias;
+        a.eps = s->eps;
+        a.xh = b->xh;
+        a.xl = b->xl;
+        a.sx = b->sx;
+        a.oscale = osc;
+        a.np = (b->B + 15) & ~15u;
+        return a;
+    };
+    auto fin_args = [&](const BPlan& g, u32 seg, const float* part2, u32 epi, const float* bias, float* out, u32 ldo) {
+        BFinishArgs f;
+        f.part = g.part(seg);
+        f.part2 = part2;
+        f.ksplit = g.ksplit();
+        f.B = b->B;
+        f.rows = g.rows(seg);
+        f.oscale = osc;
+        f.bias = bias;
+        f.epi = epi;
+        f.out = out;
+        f.ldo = ldo;
+        return f;
+    };
+    auto gemm = [&](const DevMat* const* mm, float* const* pp, u32 n, u32 K, BPlan* g) -> bool {
+        if (!batch_gemm(b, mm, pp, n, K, g)) {
+            set_error("batched decode: matrix format %u (%u x %u) has no batched kernel", mm[0]->type, mm[0]->rows, mm[0]->cols);
+            return false;
+        }
+        return launch_plan(*g, st);
+    };
+    auto finstage = [&](const BFinishArgs& f, u32 nm, const float* w, const float* bias) {
+        BFinStageArgs a;
+        a.f = f;
+        a.s = stage_args(f.rows, nm, w, bias);
+        return launch_bfinstage(a, st);
+    };
+    {
+        BStageArgs a = stage_args(s->dim, norm, s->layers[0].n1w, s->layers[0].n1b);
+        a.x = b->hidden;
+        a.ldx = s->dim;
+        if (!launch_bstage(a, st)) return false;
+    }
+    const size_t per_seq = batch_cache_bytes_per_seq(b);
+    for (u32 l = 0; l < L; l++) {
+        const llamini_session::Layer& W = s->layers[l];
+        BPlan g;
+        if (gpt2) {
+            const DevMat* mm[1] = {&W.q};
+            float* pp[1] = {b->part};
+            if (!gemm(mm, pp, 1, s->dim, &g) || !launch_bfinish(fin_args(g, 0, nullptr, EPI_STORE, W.bq, b->qkv, qkvd), st))
+                return false;
+        } else {
+            const DevMat* mm[3] = {&W.q, &W.k, &W.v};
+            float* pp[3] = {b->part, b->part2, b->part3};
+            if (!gemm(mm, pp, 3, s->dim, &g)) return false;
+            BFinishArgs f = fin_args(g, 0, nullptr, EPI_STORE, W.bq, b->qkv, qkvd);
+            f.part_b = g.part(1);
+            f.part_c = g.part(2);
+            f.rows_b = g.rows(1);
+            f.rows_c = g.rows(2);
+            f.bias_b = W.bk;
+            f.bias_c = W.bv;
+            if (!launch_bfinish(f, st)) return false;
+        }
+        AttnArgs at;
+        at.st = b->st;
+        at.qkv = b->qkv;
+        at.kc = (uint8_t*)b->kc + (size_t)l * b->max_batch * per_seq;
+        at.vc = (uint8_t*)b->vc + (size_t)l * b->max_batch * per_seq;
+        at.kv_f16 = b->kv_f16;
+        at.out = b->attn;
+        at.part = b->apart;
+        at.counter = b->counters;
+        at.n_heads = s->n_heads;
+        at.n_kv = s->n_kv;
+        at.hd = s->hd;
+        at.max_seq = b->max_seq;
+        at.n_split = b->n_split;
+        at.rope = s->rope_mode;
+        at.theta = s->theta;
+        AttnBatch ab;
+        ab.qkv_stride = qkvd;
+        ab.cache_stride = per_seq;
+        ab.out_stride = s->qd;
+        ab.part_stride = (uint64_t)s->n_heads * b->n_split * (s->hd + 4);
+        if (!launch_attention_batch(at, ab, b->B, st)) return false;
+        {
+            BStageArgs a = stage_args(s->qd, NORM_NONE, nullptr, nullptr);
+            a.x = b->attn;
+            a.ldx = s->qd;
+            if (!launch_bstage(a, st)) return false;
+        }
+        {
+            const DevMat* mm[1] = {&W.o};
+            float* pp[1] = {b->part};
+            if (!gemm(mm, pp, 1, s->qd, &g) ||
+                !finstage(fin_args(g, 0, nullptr, EPI_RESID, W.bo, b->hidden, s->dim), norm, W.n2w, W.n2b))
+                return false;
+        }
+        if (gpt2) {
+            const DevMat* mm[1] = {&W.up};
+            float* pp[1] = {b->part};
+            if (!gemm(mm, pp, 1, s->dim, &g) ||
+                !finstage(fin_args(g, 0, nullptr, EPI_GELU, W.bup, b->ffn_h, s->ffn), NORM_NONE, nullptr, nullptr))
+                return false;
+        } else {
+            const DevMat* mm[2] = {&W.gate, &W.up};
+            float* pp[2] = {b->part, b->part2};
+            const u32 epi = s->act_gelu ? (u32)EPI_GLU_GELU : (u32)EPI_GLU_SILU;
+            if (!gemm(mm, pp, 2, s->dim, &g) ||
+                !finstage(fin_args(g, 0, g.part(1), epi, nullptr, b->ffn_h, s->ffn), NORM_NONE, nullptr, nullptr))
+                return false;
+        }
+        {
+            const DevMat* mm[1] = {&W.down};
+            float* pp[1] = {b->part};
+            const float* nw = l + 1 < L ? s->layers[l + 1].n1w : s->fnw;
+            const float* nb = l + 1 < L ? s->layers[l + 1].n1b : s->fnb;
+            if (!gemm(mm, pp, 1, s->ffn, &g) ||
+                !finstage(fin_args(g, 0, nullptr, EPI_RESID, W.bdown, b->hidden, s->dim), norm, nw, nb))
+                return false;
+        }
+    }
+    {
+        const DevMat* mm[1] = {&s->head};
+        float* pp[1] = {b->part};
+        BPlan g;
+        BFinishArgs f;
+        if (!gemm(mm, pp, 1, s->dim, &g)) return false;
+        f = fin_args(g, 0, nullptr, EPI_STORE, nullptr, b->logits, s->vocab);
+        f.keys = b->keys;
+        if (!launch_bfinish(f, st)) return false;
+    }
+    BTokenArgs t;
+    t.st = b->st;
+    t.tokens = b->tokens;
+    t.tok_stride = b->max_seq + 1;
+    t.n_prompt = b->n_prompt;
+    t.keys = b->keys;
+    t.B = b->B;
+    t.max_tokens = b->max_seq + 1;
+    return launch_btoken(t, st);
+}
+
 bool batch_capture(llamini_batch* b, u32 steps, cudaGraphExec_t* out) {
     cudaStream_t st = stream();
     cudaGraph_t g = nullptr;
     if (!LM_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal))) return false;
     bool ok = true;
-    for (u32 i = 0; i < steps && ok; i++) ok = batch_enqueue_step(b, st);
+    for (u32 i = 0; i < steps && ok; i++) ok = b->tc ? batch_enqueue_step_tc(b, st) : batch_enqueue_step(b, st);
     cudaError_t e = cudaStreamEndCapture(st, &g);
     if (!ok || !LM_CUDA(e)) { if (g) cudaGraphDestroy(g); return false; }
     ok = LM_CUDA(cudaGraphInstantiate(out, g, 0));
@@ -1145,6 +1324,25 @@ bool batch_alloc(llamini_batch* b) {
         }
         return ok;
     };
+    if (b->tc) {
+        // rows of a size that is not a multiple of 16 bytes (Q6_K at some widths):
+        // a copy with 16-byte row pitch, so the tensor-core GEMM can load by TMA
+        auto pitch = [&](const DevMat& m) -> bool {
+            if (!m.ptr || !tgemm_type(m.type) || m.row_bytes % 16 == 0 || b->pitched.count(m.ptr)) return true;
+            const uint64_t p = (m.row_bytes + 15) & ~uint64_t(15);
+            uint8_t* d = (uint8_t*)own(s, p * m.rows + 16);
+            if (!d || !LM_CUDA(cudaMemcpy2D(d, p, m.ptr, m.row_bytes, m.row_bytes, m.rows, cudaMemcpyDeviceToDevice)))
+                return false;
+            b->pitched[m.ptr] = {d, p};
+            return true;
+        };
+        bool ok = pitch(s->head);
+        for (u32 l = 0; ok && l < s->n_layers; l++) {
+            const auto& W = s->layers[l];
+            ok = pitch(W.q) && pitch(W.k) && pitch(W.v) && pitch(W.o) && pitch(W.gate) && pitch(W.up) && pitch(W.down);
+        }
+        if (!ok) return false;
+    }
     if (!plan_all()) {
         // a shape the tensor-core GEMM does not take: the whole batch on mma.sync
         if (!b->tc) return false;
