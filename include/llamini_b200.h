@@ -171,6 +171,26 @@ u32 llamini_batch_pos(llamini_batch* b);
 u64 llamini_batch_weight_bytes(llamini_batch* b);
 void llamini_batch_free(llamini_batch* b);
 
+/* ---- tensor parallelism (no counterpart in the reference): LLaMA models split
+ *      over the GPUs of one box, one process per GPU --------------------------- */
+
+/* This process's 64-byte device-memory handle (a cudaIpcMemHandle_t) for the
+ * allreduce buffer the other ranks read; pass every rank's to llamini_tp_join. */
+int llamini_tp_handle(void* out64);
+
+/* Join a group of `world` ranks as `rank`; handles = world handles of 64 bytes
+ * in rank order. LLaMA sessions created afterwards hold this rank's shard:
+ * heads [rank*H/world, (rank+1)*H/world) of q and o (o split by its columns),
+ * the matching kv heads, and FFN columns split on 256-column boundaries (gate/up
+ * rows, down columns); embeddings, norms and lm_head are whole, so every rank
+ * computes the same logits. After the o projection and after ffn_down the
+ * ranks' partial sums are added over NVLink (bounded waits; a rank that does not
+ * arrive within 2 s sets the session's error). world = 1 leaves the group setting
+ * at one rank. Batched sessions are refused in a group. */
+int llamini_tp_join(u32 rank, u32 world, const void* handles);
+int llamini_tp_rank(void);
+int llamini_tp_world(void);
+
 /* Which GEMM a batch runs its matrices on: 1 = the tcgen05 tensor-core GEMM
  * (weights dequantised once per step into fp16 hi + lo, f32 accumulation in
  * tensor memory), 0 = the mma.sync GEMM; -1 = NULL. */

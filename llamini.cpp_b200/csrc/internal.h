@@ -340,6 +340,24 @@ struct alignas(64) TGemmArgs {
     uint32_t NP = 0, ue = 0, ups = 0, ksplit = 0, rblocks = 0, raw_bytes = 0, stages = 0, tcols = 0, grid = 0;
     uint32_t tma = 0;
 };
+// ---------------------------------------------------------------- tensor parallelism
+// One process per GPU; LLaMA sessions hold this rank's shard of the heads and
+// FFN columns, and sum the o-projection and ffn_down outputs across ranks
+// with tp_allreduce_kernel (k_tp.cu) over peer memory.
+constexpr uint32_t kTpMaxRanks = 8;
+constexpr uint32_t kTpSlotFloats = 16384;
+struct TpState {
+    uint32_t rank = 0, world = 1;
+    float* local = nullptr;                  // this rank's exported buffer
+    float* peer[kTpMaxRanks] = {};           // every rank's buffer, mapped here (this rank's included)
+    uint32_t* gen = nullptr;                 // allreduces this rank has finished (device)
+};
+TpState& tp();
+size_t tp_buffer_bytes();
+bool tp_alloc_buffer();
+// out[i] += sum over ranks of part[i] (rank order), i < n; part is this rank's.
+bool launch_tp_allreduce(const float* part, float* out, uint32_t n, uint32_t* err, cudaStream_t st);
+
 bool tgemm_init();
 bool batch_tc();   // tcgen05 GEMM for batched products (default) or mma.sync
 extern int g_batch_gemm;   // llamini_set_batch_gemm: -1 default, 0 mma.sync, 1 tcgen05

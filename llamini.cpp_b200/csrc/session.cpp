@@ -55,6 +55,8 @@ struct llamini_session {
     std::vector<void*> owned;
     float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *ffn_h = nullptr, *logits = nullptr;
     float *part = nullptr, *trace = nullptr;
+    float* tp_part = nullptr;           // tensor parallel: this rank's o / down partial sums
+    u32 tp_world = 1;                   // ranks the weights are split over
     u32 *counters = nullptr, *tokens = nullptr;
     void *kc = nullptr, *vc = nullptr;
     lm::StepState* st = nullptr;
@@ -130,6 +132,31 @@ const float* vec(llamini_session* s, const Tensor* t, u32 n) {
     return upload_f32(s, t->data, n);
 }
 
+// Tensor parallelism: keep rows [r0, r0 + n) of m (a view, no copy).
+void shard_rows(llamini_session* s, DevMat* m, u32 r0, u32 n) {
+    s->weight_bytes -= m->row_bytes * (m->rows - n);
+    m->ptr += (uint64_t)r0 * m->row_bytes;
+    m->rows = n;
+}
+// Tensor parallelism: columns [c0, c1) of every row, copied into a matrix of
+// their own (c0, c1 on block boundaries of m's format).
+bool shard_cols(llamini_session* s, DevMat* m, u32 c0, u32 c1) {
+    const uint64_t b0 = type_bytes(m->type, c0), w = type_bytes(m->type, c1 - c0);
+    if ((c0 && b0 == 0) || w == 0) {
+        set_error("tensor parallel: columns %u..%u of a type-%u matrix are not on block boundaries", c0, c1, m->type);
+        return false;
+    }
+    uint8_t* d = (uint8_t*)own(s, w * m->rows + 16);
+    if (!d || !LM_CUDA(cudaMemcpy2D(d, w, m->ptr + b0, m->row_bytes, w, m->rows, cudaMemcpyDeviceToDevice)) ||
+        !LM_CUDA(cudaMemset(d + w * m->rows, 0, 16)))
+        return false;
+    s->weight_bytes -= (m->row_bytes - w) * m->rows;
+    m->ptr = d;
+    m->cols = c1 - c0;
+    m->row_bytes = w;
+    return true;
+}
+
 bool alloc_buffers(llamini_session* s) {
     const u32 L = s->n_layers;
     s->hidden = (float*)own(s, (size_t)s->dim * 4);
@@ -145,6 +172,7 @@ bool alloc_buffers(llamini_session* s) {
     s->kc = own(s, kv_bytes);
     s->vc = own(s, kv_bytes);
     s->st = (StepState*)own(s, sizeof(StepState));
+    if (s->tp_world > 1 && !(s->tp_part = (float*)own(s, (size_t)s->dim * 4))) return false;
     if (!s->hidden || !s->qkv || !s->attn || !s->ffn_h || !s->logits || !s->part || !s->trace ||
         !s->counters || !s->tokens || !s->kc || !s->vc || !s->st)
         return false;
@@ -240,6 +268,10 @@ GemvArgs o_args(llamini_session* s, u32 l) {
     o.K = s->qd;
     o.nseg = 1;
     o.seg[0] = {W.o.ptr, nullptr, W.o.row_bytes, 0, W.o.type, 0, W.o.rows, EPI_RESID, s->hidden, W.bo, 0, 0};
+    if (s->tp_world > 1) {                            // partial sums; the allreduce adds them to hidden
+        o.seg[0].epi = EPI_STORE;
+        o.seg[0].out = s->tp_part;
+    }
     return o;
 }
 
@@ -273,6 +305,10 @@ GemvArgs down_args(llamini_session* s, u32 l) {
     d.K = s->ffn;
     d.nseg = 1;
     d.seg[0] = {W.down.ptr, nullptr, W.down.row_bytes, 0, W.down.type, 0, W.down.rows, EPI_RESID, s->hidden, W.bdown, 0, 0};
+    if (s->tp_world > 1) {
+        d.seg[0].epi = EPI_STORE;
+        d.seg[0].out = s->tp_part;
+    }
     return d;
 }
 
@@ -299,8 +335,10 @@ bool enqueue_step(llamini_session* s, cudaStream_t st, bool trace, bool nll) {
         if (!launch_gemv(qkv_args(s, l), st)) return false;
         if (!launch_attention(attn_args(s, l), st)) return false;
         if (!launch_gemv(o_args(s, l), st)) return false;
+        if (s->tp_world > 1 && !launch_tp_allreduce(s->tp_part, s->hidden, s->dim, &s->st->err, st)) return false;
         if (!launch_gemv(ffn_args(s, l), st)) return false;
         if (!launch_gemv(down_args(s, l), st)) return false;
+        if (s->tp_world > 1 && !launch_tp_allreduce(s->tp_part, s->hidden, s->dim, &s->st->err, st)) return false;
         if (trace && !launch_copy_f32(s->trace + (size_t)l * s->dim, s->hidden, s->dim, st)) return false;
     }
     if (!launch_gemv(head_args(s), st)) return false;
@@ -348,6 +386,7 @@ bool build_decode(llamini_session* s) {
     s->dec_on = false;
     const char* env = getenv("LLAMINI_DECODE_KERNEL");
     if (!env || env[0] != '1') return true;
+    if (s->tp_world > 1) return true;                 // the allreduces run as their own kernels
     if (s->hd > 256 || s->hd == 0 || s->hd % 4 != 0 || s->n_split > 32) return true;
     std::vector<DecOp> ops;
     u32 kmax = 0;
@@ -516,6 +555,27 @@ bool bind_llama(llamini_session* s, LLaMAModel* m, u32 max_seq) {
     s->act_gelu = c.ffn_act == ACT_GELU;
     bool ok = s->n_kv > 0 && s->n_heads % s->n_kv == 0 && s->hd > 0;
     if (!ok) set_error("llama session: inconsistent heads (heads %u kv %u hd %u)", s->n_heads, s->n_kv, s->hd);
+    // tensor parallelism: rank R of W keeps heads [R H/W, (R+1) H/W), the matching
+    // kv heads, and FFN columns [f0, f1) on 256-column boundaries (uneven when the
+    // super-blocks do not divide); embeddings, norms and lm_head stay whole
+    const u32 W = tp().world, R = tp().rank;
+    u32 f0 = 0, f1 = c.ffn_dim;
+    if (ok && W > 1) {
+        s->tp_world = W;
+        if (s->n_heads % W != 0 || s->n_kv % W != 0 || c.ffn_dim % 256 != 0 || c.ffn_dim / 256 < W) {
+            set_error("tensor parallel over %u ranks: heads %u, kv heads %u, ffn %u do not split", W, s->n_heads, s->n_kv,
+                      c.ffn_dim);
+            return false;
+        }
+        s->n_heads /= W;
+        s->n_kv /= W;
+        s->qd /= W;
+        s->kvd /= W;
+        const u32 nsb = c.ffn_dim / 256;
+        f0 = 256 * (u32)((uint64_t)nsb * R / W);
+        f1 = 256 * (u32)((uint64_t)nsb * (R + 1) / W);
+        s->ffn = f1 - f0;
+    }
     ok = ok && weight(s, m->embeddings, c.vocab_size, c.dim, &s->tok);
     ok = ok && weight(s, m->lm_head, c.vocab_size, c.dim, &s->head);
     s->fnw = ok ? vec(s, m->final_norm, c.dim) : nullptr;
@@ -524,14 +584,28 @@ bool bind_llama(llamini_session* s, LLaMAModel* m, u32 max_seq) {
     for (u32 l = 0; ok && l < c.n_layers; l++) {
         const DecoderLayer& L = m->layers[l];
         auto& W = s->layers[l];
-        ok = weight(s, L.q_proj, s->qd, c.dim, &W.q) && weight(s, L.k_proj, s->kvd, c.dim, &W.k) &&
-             weight(s, L.v_proj, s->kvd, c.dim, &W.v) && weight(s, L.o_proj, c.dim, s->qd, &W.o) &&
+        const u32 QD = c.n_heads * c.head_dim, KVD = c.n_heads_kv * c.head_dim;   // whole-model widths
+        ok = weight(s, L.q_proj, QD, c.dim, &W.q) && weight(s, L.k_proj, KVD, c.dim, &W.k) &&
+             weight(s, L.v_proj, KVD, c.dim, &W.v) && weight(s, L.o_proj, c.dim, QD, &W.o) &&
              weight(s, L.gate_proj, c.ffn_dim, c.dim, &W.gate) && weight(s, L.up_proj, c.ffn_dim, c.dim, &W.up) &&
              weight(s, L.down_proj, c.dim, c.ffn_dim, &W.down);
+        if (ok && s->tp_world > 1) {
+            shard_rows(s, &W.q, R * s->qd, s->qd);
+            shard_rows(s, &W.k, R * s->kvd, s->kvd);
+            shard_rows(s, &W.v, R * s->kvd, s->kvd);
+            shard_rows(s, &W.gate, f0, f1 - f0);
+            shard_rows(s, &W.up, f0, f1 - f0);
+            ok = shard_cols(s, &W.o, R * s->qd, (R + 1) * s->qd) && shard_cols(s, &W.down, f0, f1);
+        }
         if (ok) { W.n1w = vec(s, L.attn_norm, c.dim); W.n2w = vec(s, L.ffn_norm, c.dim); ok = W.n1w && W.n2w; }
         if (ok && c.qkv_bias) {
-            W.bq = vec(s, L.q_bias, s->qd); W.bk = vec(s, L.k_bias, s->kvd); W.bv = vec(s, L.v_bias, s->kvd);
+            W.bq = vec(s, L.q_bias, QD); W.bk = vec(s, L.k_bias, KVD); W.bv = vec(s, L.v_bias, KVD);
             ok = W.bq && W.bk && W.bv;
+            if (ok && s->tp_world > 1) {                  // this rank's slice of each bias
+                W.bq += R * s->qd;
+                W.bk += R * s->kvd;
+                W.bv += R * s->kvd;
+            }
         }
     }
     // the tok table is read one row per step, not whole
@@ -583,8 +657,8 @@ llamini_session* build_llama(LLaMAModel* m, KVCache* caches) {
     s->cache_max_seq = caches[0].max_seq;
     s->cache_dim = caches[0].dim;
     bool ok = bind_llama(s, m, caches[0].max_seq);
-    if (ok && caches[0].dim != s->kvd) {
-        set_error("llama session: cache dim %u != kv dim %u", caches[0].dim, s->kvd);
+    if (ok && caches[0].dim != s->kvd * s->tp_world) {    // the caller's cache is whole-model width
+        set_error("llama session: cache dim %u != kv dim %u", caches[0].dim, s->kvd * s->tp_world);
         ok = false;
     }
     ok = ok && finish_build(s);
@@ -1386,6 +1460,7 @@ template <class M, class Bind>
 llamini_batch* batch_create(M* model, u32 max_batch, u32 max_seq, Bind bind) {
     if (!ensure_device()) return nullptr;
     if (max_batch == 0 || max_batch > 64) { set_error("batched decode: batch %u outside 1..64", max_batch); return nullptr; }
+    if (tp().world > 1) { set_error("batched decode: not available in a tensor-parallel group"); return nullptr; }
     if (max_seq == 0) { set_error("batched decode: max_seq 0"); return nullptr; }
     auto* b = new llamini_batch();
     b->w = new llamini_session();
@@ -1594,6 +1669,54 @@ u64 llamini_batch_weight_bytes(llamini_batch* b) { return b ? b->w->weight_bytes
 void llamini_batch_free(llamini_batch* b) { lm::batch_destroy(b); }
 
 int llamini_batch_gemm_kind(llamini_batch* b) { return b ? (b->tc ? 1 : 0) : -1; }
+
+// ---------------------------------------------------------------- tensor parallelism
+
+int llamini_tp_handle(void* out) {
+    if (!out) { lm::set_error("tp handle: null output"); return -1; }
+    if (!lm::ensure_device() || !lm::tp_alloc_buffer()) return -1;
+    cudaIpcMemHandle_t h;
+    if (!LM_CUDA(cudaIpcGetMemHandle(&h, lm::tp().local))) return -1;
+    static_assert(sizeof(h) == 64, "IPC handles are 64 bytes");
+    memcpy(out, &h, sizeof(h));
+    return 0;
+}
+
+int llamini_tp_join(u32 rank, u32 world, const void* handles) {
+    lm::TpState& T = lm::tp();
+    if (world == 0 || world > lm::kTpMaxRanks || rank >= world) {
+        lm::set_error("tp join: rank %u of %u (at most %u ranks)", rank, world, lm::kTpMaxRanks);
+        return -1;
+    }
+    if (world == 1) {
+        T.rank = 0;
+        T.world = 1;
+        return 0;
+    }
+    if (!handles) { lm::set_error("tp join: null handles"); return -1; }
+    if (T.world > 1) { lm::set_error("tp join: this process is already in a group of %u", T.world); return -1; }
+    if (!lm::ensure_device() || !lm::tp_alloc_buffer()) return -1;
+    float* peer[lm::kTpMaxRanks] = {};
+    for (u32 j = 0; j < world; j++) {
+        if (j == rank) { peer[j] = T.local; continue; }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, (const uint8_t*)handles + 64 * j, sizeof(h));
+        void* p = nullptr;
+        if (!LM_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess))) {
+            for (u32 k = 0; k < j; k++)
+                if (k != rank && peer[k]) cudaIpcCloseMemHandle(peer[k]);
+            return -1;
+        }
+        peer[j] = (float*)p;
+    }
+    for (u32 j = 0; j < lm::kTpMaxRanks; j++) T.peer[j] = peer[j];
+    T.rank = rank;
+    T.world = world;
+    return 0;
+}
+
+int llamini_tp_rank(void) { return (int)lm::tp().rank; }
+int llamini_tp_world(void) { return (int)lm::tp().world; }
 
 int llamini_set_batch_gemm(int kind) {
     if (kind < -1 || kind > 1) { lm::set_error("batched GEMM kind %d outside -1..1", kind); return -1; }

@@ -50,6 +50,10 @@ def specs():
     tied = S.llama_spec(S.shape_llama_1b(dim=256, n_layers=2, n_heads=4, n_kv=1, ffn=512, vocab=600, ctx=64))
     tied.tensors = [t for t in tied.tensors if t.name != "output.weight"]
     out["tiny_tied"] = (tied, 14)
+    # Tensor-parallel shape: 8 heads of 64 and 4 kv heads, FFN of 6 super-blocks,
+    # so two ranks split o-proj and down on 256-column boundaries.
+    out["tiny_tp"] = (S.llama_spec(S.shape_llama_1b(
+        dim=512, n_layers=2, n_heads=8, n_kv=4, ffn=1536, vocab=1000, ctx=128)), 15)
     # GPT-2: Q8_0 matrices, F16 embeddings, LayerNorm + biases, GELU MLP.
     out["tiny_gpt2"] = (S.gpt2_spec(S.Gpt2Shape(dim=128, n_layers=2, n_heads=4, ffn=512, vocab=700, ctx=64)), 13)
     return out

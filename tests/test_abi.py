@@ -51,6 +51,19 @@ def test_no_device_fails_loudly(lm):
     assert np.all(out == 7.0)          # untouched: no CPU fallback computed anything
 
 
+def test_tp_join_argument_checks(lm):
+    """Group membership is validated on the host: bad ranks fail with a
+    message; a one-rank group needs no device."""
+    L = lm.lib()
+    assert L.llamini_tp_join(2, 2, None) == -1
+    assert "rank 2 of 2" in lm.last_error()
+    assert L.llamini_tp_join(0, 9, None) == -1
+    assert L.llamini_tp_join(0, 0, None) == -1
+    assert L.llamini_tp_join(0, 1, None) == 0
+    assert L.llamini_tp_world() == 1 and L.llamini_tp_rank() == 0
+    L.llamini_clear_error()
+
+
 def _write(tmp_path, name, data: bytes) -> str:
     p = str(tmp_path / name)
     with open(p, "wb") as f:

@@ -1,0 +1,98 @@
+"""Tensor parallelism (llamini_tp_*): a LLaMA model split over two GPUs, one
+process per GPU (heads and FFN columns sharded, embeddings / norms / lm_head
+whole, the o-projection and ffn_down sums added across ranks over NVLink).
+
+Both ranks must reproduce the oracle's greedy stream, and their logits must be
+bit-identical to each other (every rank adds the ranks' partial sums in rank
+order) and within the 1e-3 bar of the oracle's forward pass.
+"""
+from __future__ import annotations
+
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+
+from conftest import ROOT, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, path, prompt, n_gen, q):
+    import datetime
+    import importlib.util
+    import torch.distributed as dist
+    import torch
+    spec = importlib.util.spec_from_file_location("llamini_b200", os.path.join(ROOT, "llamini.cpp_b200", "__init__.py"))
+    lm = importlib.util.module_from_spec(spec)
+    sys.modules["llamini_b200"] = lm
+    spec.loader.exec_module(lm)
+    L = lm.lib()
+    try:
+        assert L.llamini_set_device(rank) == 0, lm.last_error()
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:%d" % port, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120))
+        h = np.zeros(64, np.uint8)
+        assert L.llamini_tp_handle(lm.ptr(h)) == 0, lm.last_error()
+        mine = torch.from_numpy(h)
+        hs = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(hs, mine)
+        allh = np.ascontiguousarray(np.concatenate([x.numpy() for x in hs]))
+        assert L.llamini_tp_join(rank, world, lm.ptr(allh)) == 0, lm.last_error()
+        assert L.llamini_tp_world() == world and L.llamini_tp_rank() == rank
+        m = lm.Model(path)
+        toks = m.generate(np.array(prompt, np.uint32), n_gen).tolist()
+        lgs = np.stack([m.forward(p, int(toks[p])) for p in range(6)])
+        err = lm.last_error()
+        m.close()
+        dist.barrier()
+        q.put((rank, toks, lgs, err))
+        dist.destroy_process_group()
+    except Exception as e:                            # report, then leave: the parent fails the test
+        q.put((rank, None, None, repr(e)))
+
+
+def test_tp_two_ranks_match_oracle(orc, tiny):
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("tensor parallelism needs two GPUs")
+    path = tiny.ensure("tiny_tp")
+    rng = np.random.default_rng(21)
+    prompt = rng.integers(3, 1000, 7).tolist()
+    n_gen = 24
+    # the oracle's greedy stream and logits (CPU)
+    o = orc.oracle_model(path)
+    toks = list(prompt)
+    want = []
+    for pos in range(len(prompt) + n_gen - 1):
+        lg = o.forward(pos, toks[pos])
+        if pos < 6:
+            want.append(lg)
+        if pos + 1 >= len(prompt):
+            toks.append(int(np.argmax(lg)))
+    ctx = mp.get_context("spawn")
+    qq = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_rank_main, args=(r, 2, port, path, prompt, n_gen, qq)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted((qq.get(timeout=600) for _ in ps), key=lambda r: r[0])
+    for p in ps:
+        p.join(timeout=120)
+    for rank, got, lgs, err in res:
+        assert got is not None, (rank, err)
+        assert got == toks, (rank, got, toks, err)
+        for pos in range(6):
+            assert rel_l2(lgs[pos], want[pos]) < TOL, (rank, pos, rel_l2(lgs[pos], want[pos]))
+    assert np.array_equal(res[0][2].view(np.uint32), res[1][2].view(np.uint32))
