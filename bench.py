@@ -249,11 +249,60 @@ def run_batch(args, lm, L, model, torch, stream, ws, rank, dist, hbm_peak):
         out = np.zeros(4, np.uint32)
         assert L.llamini_batch_tokens(b, 0, lm.ptr(out), 4) > 0
         weight_bytes = L.llamini_batch_weight_bytes(b)
+        tc = L.llamini_batch_gemm_kind(b) == 1
     finally:
         L.llamini_batch_free(b)
     kv_per_pos = L.llamini_session_kv_bytes_per_pos(model.session())
     ctx_mean = pos0 + (args.batch_steps - 1) / 2 + 1
-    return ms, weight_bytes + B * kv_per_pos * ctx_mean, B
+    return ms, weight_bytes + B * kv_per_pos * ctx_mean, B, tc
+
+
+TP_PROMPT = 1024
+
+
+def run_tp7b(args, lm, L, torch, ws, rank, dist, hbm_peak):
+    """LLaMA at 7B shape, batch 1, tensor parallel over every rank (unsharded at
+    one GPU): a 1024-token prompt, then timed decode steps. Returns this rank's
+    device time, weight bytes per step on this rank and the first timed position."""
+    S = synthetic()
+    directory = os.environ.get("LLAMINI_WORKDIR", "/tmp/llamini_b200")
+    if rank == 0:
+        S.ensure_workload("llama_7b", directory)
+    if dist:
+        dist.barrier()
+    path = S.ensure_workload("llama_7b", directory)
+    if ws > 1:
+        h = np.zeros(64, np.uint8)
+        assert L.llamini_tp_handle(lm.ptr(h)) == 0, lm.last_error()
+        mine = torch.from_numpy(h).cuda()
+        hs = [torch.zeros_like(mine) for _ in range(ws)]
+        dist.all_gather(hs, mine)
+        allh = np.ascontiguousarray(np.concatenate([x.cpu().numpy() for x in hs]))
+        assert L.llamini_tp_join(rank, ws, lm.ptr(allh)) == 0, lm.last_error()
+    m = lm.Model(path, max_seq=TP_PROMPT + args.warmup + args.tp_steps + 8)
+    try:
+        s = m.session()
+        stream = torch.cuda.ExternalStream(L.llamini_stream())
+        prompt = S.workload_prompt("llama_7b", TP_PROMPT)
+        assert L.llamini_session_begin(s, lm.ptr(prompt), TP_PROMPT) == 0, lm.last_error()
+        assert L.llamini_session_step(s, TP_PROMPT - 1 + args.warmup) == 0, lm.last_error()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        pos0 = L.llamini_session_pos(s)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        assert L.llamini_session_step(s, args.tp_steps) == 0, lm.last_error()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        tk = np.zeros(4, np.uint32)
+        assert L.llamini_session_tokens(s, lm.ptr(tk), 4) >= 0, lm.last_error()   # no step reported an error
+        wb = L.llamini_session_weight_bytes(s)
+        kvp = L.llamini_session_kv_bytes_per_pos(s)
+    finally:
+        m.close()
+    return ms, wb, kvp, pos0
 
 
 def run_ours(args, ws, rank, local):
@@ -305,8 +354,11 @@ def run_ours(args, ws, rank, local):
         if rank == 0 and not args.no_kernel_roofline:
             gemv_roof = kernel_roofline(lm, torch, stream, hbm_peak, peak_kind)
         bt = None if args.no_batch else run_batch(args, lm, L, model, torch, stream, ws, rank, dist, hbm_peak)
+    model.close()
+    tp7 = None if args.no_tp7b else run_tp7b(args, lm, L, torch, ws, rank, dist, hbm_peak)
     t_max, e2e_max = max_over_ranks(dist, [ms, e2e_s])
     b_max = max_over_ranks(dist, [bt[0]])[0] if bt else None
+    tp_max = max_over_ranks(dist, [tp7[0]])[0] if tp7 else None
     if rank == 0:
         steps = args.steps
         value = whole_job_rate(ws, steps, t_max)
@@ -350,13 +402,31 @@ def run_ours(args, ws, rank, local):
                             "timed decode steps after the prompt" % (b_per, args.prompt),
                 "weight_stream_gbs": round(b_bytes / b_step_s / 1e9, 1),
                 "frac_of_hbm": round(b_bytes / b_step_s / 1e9 / hbm_peak, 4),
-                # per step: embed; per layer 4 stagings, 4 GEMMs (qkv, o, gate+up, down),
-                # 6 finishes, attention; lm_head staging + GEMM + finish; token update
-                "gpu_launches": args.batch_steps * (1 + 22 * 15 + 3 + 1)}
+                "gemm": "tcgen05 (tensor memory)" if bt[3] else "mma.sync",
+                # per step, tensor-core GEMM: embed + staging; per layer the q/k/v GEMM and
+                # finish, attention, staging, then o, gate+up and down GEMMs each with a
+                # finish+staging; lm_head GEMM + finish; token update. mma.sync GEMM: embed;
+                # per layer 4 stagings, 4 GEMMs, 6 finishes, attention; lm_head staging + GEMM
+                # + finish; token update
+                "gpu_launches": args.batch_steps * ((2 + 22 * 10 + 3) if bt[3] else (1 + 22 * 15 + 3 + 1))}
+        if tp7:
+            t_step_s = tp_max / 1e3 / args.tp_steps
+            tp_bytes = tp7[1] + tp7[2] * (tp7[3] + (args.tp_steps - 1) / 2 + 1)
+            line["tp_7b"] = {
+                "value": round(args.tp_steps / (tp_max / 1e3), 2), "unit": "tok/s", "tp": ws, "batch": 1,
+                "steps": args.tp_steps, "ms_per_step": round(tp_max / args.tp_steps, 4), "scaling": "strong",
+                "workload": "llama_7b: LLaMA 7B shape (32 layers, dim 4096, 32/32 heads, ffn 11008, vocab 32000), "
+                            "Q4_K_M mix, seed 4; %d-token prompt, timed decode positions %d..%d; heads and FFN "
+                            "columns split over %d rank(s), o-proj and ffn_down sums added over NVLink" %
+                            (TP_PROMPT, tp7[3], tp7[3] + args.tp_steps - 1, ws),
+                "per_gpu_bytes_per_step": int(tp_bytes),
+                "per_gpu_stream_gbs": round(tp_bytes / t_step_s / 1e9, 1),
+                "frac_of_hbm": round(tp_bytes / t_step_s / 1e9 / hbm_peak, 4),
+                # embed, 5 per layer (+ 2 allreduces per layer when split), lm_head, finish
+                "gpu_launches": args.tp_steps * (1 + 32 * (5 + (2 if ws > 1 else 0)) + 2)}
         if ws == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(path)
         print(json.dumps(line), flush=True)
-    model.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -447,6 +517,8 @@ def main():
     ap.add_argument("--prompt", type=int, default=N_PROMPT, help="prompt length before the timed steps")
     ap.add_argument("--no-batch", action="store_true", help="skip the batch-64 decode timing")
     ap.add_argument("--batch-steps", type=int, default=32, help="timed steps of the batch-64 leg")
+    ap.add_argument("--no-tp7b", action="store_true", help="skip the 7B-shape tensor-parallel decode timing")
+    ap.add_argument("--tp-steps", type=int, default=64, help="timed decode steps of the 7B-shape leg")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
