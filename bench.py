@@ -404,11 +404,11 @@ def run_ours(args, ws, rank, local):
                 "frac_of_hbm": round(b_bytes / b_step_s / 1e9 / hbm_peak, 4),
                 "gemm": "tcgen05 (tensor memory)" if bt[3] else "mma.sync",
                 # per step, tensor-core GEMM: embed + staging; per layer the q/k/v GEMM and
-                # finish, attention, staging, then o, gate+up and down GEMMs each with a
-                # finish+staging; lm_head GEMM + finish; token update. mma.sync GEMM: embed;
-                # per layer 4 stagings, 4 GEMMs, 6 finishes, attention; lm_head staging + GEMM
-                # + finish; token update
-                "gpu_launches": args.batch_steps * ((2 + 22 * 10 + 3) if bt[3] else (1 + 22 * 15 + 3 + 1))}
+                # finish, attention, staging, then o, gate+up and down GEMMs each followed by
+                # a finish and a staging; lm_head GEMM + finish; token update. mma.sync GEMM:
+                # embed; per layer 4 stagings, 4 GEMMs, 6 finishes, attention; lm_head
+                # staging + GEMM + finish; token update
+                "gpu_launches": args.batch_steps * ((2 + 22 * 13 + 3) if bt[3] else (1 + 22 * 15 + 3 + 1))}
         if tp7:
             t_step_s = tp_max / 1e3 / args.tp_steps
             tp_bytes = tp7[1] + tp7[2] * (tp7[3] + (args.tp_steps - 1) / 2 + 1)

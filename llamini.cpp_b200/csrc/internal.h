@@ -281,13 +281,6 @@ struct BFinishArgs {
     const float* bias_c = nullptr;
     uint32_t rows_b = 0, rows_c = 0;
 };
-// Finish of one matrix whose output a staging for the next matrix reads at
-// once: one CTA per sequence does both (k_bgemm.cu).
-struct BFinStageArgs {
-    BFinishArgs f;                 // single segment; f.out receives the finished rows
-    BStageArgs s;                  // s.x / s.ldx unused: the finished rows are staged (s.K == f.rows)
-};
-bool launch_bfinstage(const BFinStageArgs& a, cudaStream_t st);
 struct BEmbedArgs {
     const StepState* st;           // pos (shared by the batch)
     const uint32_t* tokens;        // [B][tok_stride]

@@ -365,19 +365,9 @@ __global__ void __launch_bounds__(256) bfinish_kernel(const BFinishArgs a) {
     }
 }
 
-// One CTA per sequence: finish every row of the matrix into f.out and shared
-// memory, then stage those rows for the next matrix.
-__global__ void __launch_bounds__(1024) bfinstage_kernel(const BFinStageArgs a) {
-    extern __shared__ __align__(16) float xf[];          // f.rows floats
-    __shared__ float red[32];
-    const uint32_t b = blockIdx.x;
-    const float sc = a.f.oscale[b];                      // read before the staging rewrites it
-    for (uint32_t r = threadIdx.x; r < a.f.rows; r += blockDim.x) xf[r] = bfin_row(a.f, b, r, sc);
-    __syncthreads();
-    stage_core(a.s, xf, b, red);
-}
-
 // ---------------------------------------------------------------- host side
+
+
 
 bool bgemm_type(uint32_t t) { return t == T_Q4_K || t == T_Q6_K || t == T_Q8_0 || t == T_Q4_0 || t == T_F16; }
 
@@ -400,8 +390,7 @@ bool bgemm_init() {
            LM_CUDA(cudaFuncSetAttribute(bgemm_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBSmemMax)) &&
            LM_CUDA(cudaFuncSetAttribute(bgemm_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBSmemMax)) &&
            LM_CUDA(cudaFuncSetAttribute(bgemm_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBSmemMax)) &&
-           LM_CUDA(cudaFuncSetAttribute(bstage_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024)) &&
-           LM_CUDA(cudaFuncSetAttribute(bfinstage_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
+           LM_CUDA(cudaFuncSetAttribute(bstage_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
 }
 
 // Fill the launch geometry of `a` (segments, B, K and partial buffers set by
@@ -470,14 +459,6 @@ bool launch_bstage(const BStageArgs& a, cudaStream_t st) {
     return LM_CUDA(cudaGetLastError());
 }
 
-bool launch_bfinstage(const BFinStageArgs& a, cudaStream_t st) {
-    if (a.s.K != a.f.rows || a.s.K % 4 != 0 || a.s.K > 16384 || a.f.rows_b || a.f.rows_c || a.f.keys) {
-        set_error("batch finish+staging: rows %u, K %u", a.f.rows, a.s.K);
-        return false;
-    }
-    bfinstage_kernel<<<a.f.B, 1024, (size_t)a.s.K * 4, st>>>(a);
-    return LM_CUDA(cudaGetLastError());
-}
 
 bool launch_bfinish(const BFinishArgs& a, cudaStream_t st) {
     bfinish_kernel<<<dim3((a.rows + a.rows_b + a.rows_c + 255) / 256, a.B), 256, 0, st>>>(a);

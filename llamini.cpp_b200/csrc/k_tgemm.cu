@@ -95,10 +95,14 @@ __device__ __forceinline__ uint64_t tg_time() {
     asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
     return t;
 }
+// One test of the phase; a thread whose phase is not complete yet is suspended
+// in hardware (up to kTSuspendNs, resuming when the phase completes) instead of
+// spinning, so waiting roles leave the issue slots to the dequant warps.
+constexpr uint32_t kTSuspendNs = 1000000;
 __device__ __forceinline__ bool tg_try(uint32_t adr, uint32_t parity) {
     uint32_t done;
-    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-                 " selp.u32 %0, 1, 0, p;\n}\n" : "=r"(done) : "r"(adr), "r"(parity) : "memory");
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+                 " selp.u32 %0, 1, 0, p;\n}\n" : "=r"(done) : "r"(adr), "r"(parity), "n"(kTSuspendNs) : "memory");
     return done != 0;
 }
 __device__ __forceinline__ bool tg_aborted(TShared& S) { return *reinterpret_cast<volatile uint32_t*>(&S.abort) != 0; }

@@ -1151,9 +1151,8 @@ bool batch_enqueue_step(llamini_batch* b, cudaStream_t st) {
     return launch_btoken(t, st);
 }
 
-// The step on the tensor-core GEMM: each finish whose output is the next
-// matrix's input also stages that input (one kernel per sequence), and q, k
-// and v finish in one launch.
+// The step on the tensor-core GEMM: q, k and v finish in one launch, and the
+// inputs are staged in the tensor-core layout.
 bool batch_enqueue_step_tc(llamini_batch* b, cudaStream_t st) {
     llamini_session* s = b->w;
     const bool gpt2 = s->kind == 1;
@@ -1207,11 +1206,14 @@ bool batch_enqueue_step_tc(llamini_batch* b, cudaStream_t st) {
         }
         return launch_plan(*g, st);
     };
+    // finish (grid over rows x sequences), then stage the finished rows for the
+    // next matrix (one 1024-thread CTA per sequence)
     auto finstage = [&](const BFinishArgs& f, u32 nm, const float* w, const float* bias) {
-        BFinStageArgs a;
-        a.f = f;
-        a.s = stage_args(f.rows, nm, w, bias);
-        return launch_bfinstage(a, st);
+        if (!launch_bfinish(f, st)) return false;
+        BStageArgs a = stage_args(f.rows, nm, w, bias);
+        a.x = f.out;
+        a.ldx = f.ldo;
+        return launch_bstage(a, st);
     };
     {
         BStageArgs a = stage_args(s->dim, norm, s->layers[0].n1w, s->layers[0].n1b);
