@@ -54,6 +54,13 @@ def specs():
     # so two ranks split o-proj and down on 256-column boundaries.
     out["tiny_tp"] = (S.llama_spec(S.shape_llama_1b(
         dim=512, n_layers=2, n_heads=8, n_kv=4, ffn=1536, vocab=1000, ctx=128)), 15)
+    # Gemma: NEOX RoPE, GeGLU, embeddings scaled by sqrt(dim), lm_head tied to the
+    # embeddings (model.c:296-299, 319, 447-452).
+    g = S.shape_llama_1b(dim=256, n_layers=2, n_heads=4, n_kv=1, ffn=512, vocab=600, ctx=64)
+    g.arch = "gemma"
+    gemma = S.llama_spec(g)
+    gemma.tensors = [t for t in gemma.tensors if t.name != "output.weight"]
+    out["tiny_gemma"] = (gemma, 16)
     # GPT-2: Q8_0 matrices, F16 embeddings, LayerNorm + biases, GELU MLP.
     out["tiny_gpt2"] = (S.gpt2_spec(S.Gpt2Shape(dim=128, n_layers=2, n_heads=4, ffn=512, vocab=700, ctx=64)), 13)
     return out

@@ -66,7 +66,7 @@ def test_oracle_vs_reference_build(orc, tiny):
     if ref is None:
         pytest.skip("reference sources not compiled on this machine")
     rng = np.random.default_rng(5)
-    for name in ("tiny_llama", "tiny_qwen2", "tiny_gpt2"):
+    for name in ("tiny_llama", "tiny_qwen2", "tiny_gpt2", "tiny_gemma", "tiny_tp"):
         path = tiny.ensure(name)
         m = orc.oracle_model(path)
         assert ref.drv_open(path.encode(), 0) == 0
