@@ -171,6 +171,21 @@ u32 llamini_batch_pos(llamini_batch* b);
 u64 llamini_batch_weight_bytes(llamini_batch* b);
 void llamini_batch_free(llamini_batch* b);
 
+/* Prompt positions whose logits nobody reads (generate_autoregressive's
+ * prefill, llamini_session_step inside the prompt) run in chunks of 64
+ * positions through the tcgen05 GEMM, with causal attention over the cache, when
+ * every matrix takes the tensor-core path (one at a time otherwise): 1 = on (the
+ * default), 0 = one position at a time, -1 = the default again
+ * (LLAMINI_PREFILL=0 in the environment turns it off). The last prompt position
+ * always runs through the decode step, which produces the logits. */
+int llamini_set_prefill(int enable);
+
+/* Whether this session's prompts have run through chunked prefill: 1 = yes (its
+ * buffers are built), -1 = not available for this model (a format or shape the
+ * tensor-core GEMM does not take, or a tensor-parallel group), 0 = not tried
+ * yet; -2 = NULL. */
+int llamini_session_prefill(llamini_session* s);
+
 /* ---- tensor parallelism (no counterpart in the reference): LLaMA models split
  *      over the GPUs of one box, one process per GPU --------------------------- */
 

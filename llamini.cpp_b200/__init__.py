@@ -162,6 +162,8 @@ SIGNATURES = {
     "llamini_batch_weight_bytes": (u64, [P]),
     "llamini_batch_gemm_kind": (C.c_int, [P]),
     "llamini_set_batch_gemm": (C.c_int, [C.c_int]),
+    "llamini_set_prefill": (C.c_int, [C.c_int]),
+    "llamini_session_prefill": (C.c_int, [P]),
     "llamini_tp_handle": (C.c_int, [P]),
     "llamini_tp_join": (C.c_int, [C.c_uint32, C.c_uint32, P]),
     "llamini_tp_rank": (C.c_int, []),

@@ -351,6 +351,38 @@ bool tp_alloc_buffer();
 // out[i] += sum over ranks of part[i] (rank order), i < n; part is this rank's.
 bool launch_tp_allreduce(const float* part, float* out, uint32_t n, uint32_t* err, cudaStream_t st);
 
+// ---------------------------------------------------------------- prefill (k_prefill.cu)
+struct PEmbedArgs {
+    const uint32_t* tokens;        // token of position p at tokens[p]
+    uint32_t p0, C;
+    DevMat tok, pos;               // token table, learned positions (or ptr == nullptr)
+    float scale;
+    float* hidden;                 // [C][dim]
+    uint32_t dim;
+};
+struct PRopeArgs {
+    float* qkv;                    // [C][qkv_stride]: q | k | v of each position
+    uint32_t qkv_stride;
+    void* kc;                      // this layer's cache [n_kv][max_seq][hd]
+    void* vc;
+    uint32_t kv_f16, n_heads, n_kv, hd, max_seq, p0, rope;
+    const float* theta;
+};
+struct PAttnArgs {
+    const float* qkv;
+    uint32_t qkv_stride;
+    const void* kc;
+    const void* vc;
+    uint32_t kv_f16;
+    float* out;                    // [C][out_stride]
+    uint32_t out_stride;
+    uint32_t n_heads, n_kv, hd, max_seq, p0, C;
+};
+bool prefill_init();
+bool launch_pembed(const PEmbedArgs& a, cudaStream_t st);
+bool launch_prope(const PRopeArgs& a, uint32_t C, cudaStream_t st);
+bool launch_pattn(const PAttnArgs& a, cudaStream_t st);
+
 bool tgemm_init();
 bool batch_tc();   // tcgen05 GEMM for batched products (default) or mma.sync
 extern int g_batch_gemm;   // llamini_set_batch_gemm: -1 default, 0 mma.sync, 1 tcgen05

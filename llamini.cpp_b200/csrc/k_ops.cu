@@ -358,6 +358,7 @@ bool gemv_mma_init();
 bool attn_init();
 bool decode_init();
 bool bgemm_init();
+bool prefill_init();
 
 // Per-kernel attributes, set once when the device is selected (never during a
 // graph capture).
@@ -365,7 +366,7 @@ bool kernels_init() {
     // one shared-memory carveout for every kernel of the step, so consecutive
     // kernels never wait for an SM to reconfigure its L1 / shared split
     const int carve = cudaFuncAttributePreferredSharedMemoryCarveout;
-    return gemv_init() && gemv_mma_init() && attn_init() && decode_init() && bgemm_init() && tgemm_init() &&
+    return gemv_init() && gemv_mma_init() && attn_init() && decode_init() && bgemm_init() && tgemm_init() && prefill_init() &&
            LM_CUDA(cudaFuncSetAttribute(embed_kernel, (cudaFuncAttribute)carve, 100)) &&
            LM_CUDA(cudaFuncSetAttribute(finish_kernel, (cudaFuncAttribute)carve, 100)) &&
            LM_CUDA(cudaFuncSetAttribute(copy_kernel, (cudaFuncAttribute)carve, 100)) &&

@@ -24,6 +24,15 @@
 #include <unordered_map>
 #include <vector>
 
+// Buffers and weight copies of chunked prefill (session.cpp, prefill section).
+struct Prefill {
+    float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *ffn_h = nullptr, *osc = nullptr;
+    float *part = nullptr, *part2 = nullptr, *part3 = nullptr;
+    uint16_t *xh = nullptr, *xl = nullptr;
+    uint32_t* err = nullptr;
+    std::unordered_map<const uint8_t*, std::pair<const uint8_t*, uint64_t>> pitched;
+};
+
 struct llamini_session {
     int kind = 0;                         // 0 LLaMA family, 1 GPT-2
     const void* model = nullptr;
@@ -57,6 +66,8 @@ struct llamini_session {
     float *part = nullptr, *trace = nullptr;
     float* tp_part = nullptr;           // tensor parallel: this rank's o / down partial sums
     u32 tp_world = 1;                   // ranks the weights are split over
+    struct Prefill* pf = nullptr;       // prompt chunks on the tensor-core GEMM (built on first use)
+    int pf_state = 0;                   // 0 not tried, 1 built, -1 not available for this model
     u32 *counters = nullptr, *tokens = nullptr;
     void *kc = nullptr, *vc = nullptr;
     lm::StepState* st = nullptr;
@@ -372,6 +383,7 @@ void destroy(llamini_session* s) {
     for (auto g : gs) if (g) cudaGraphExecDestroy(g);
     for (void* p : s->owned) dev_free(p);
     if (s->st_host) cudaFreeHost(s->st_host);
+    delete s->pf;
     delete s;
 }
 
@@ -769,6 +781,12 @@ void drop_all_sessions() {
     g_sessions.clear();
 }
 
+namespace {
+// Prompt positions [pos, pos + n) without logits: chunked prefill when the
+// model allows it, else decode steps (defined with the batched code below).
+bool run_prompt(llamini_session* s, u32 n);
+}  // namespace
+
 // Shared by forward_step and gpt2_forward_step.
 static void forward_one(llamini_session* s, u32 pos, u32 token, f32* logits_out) {
     if (!s) { if (logits_out) memset(logits_out, 0, 4); return; }
@@ -819,7 +837,7 @@ static u32 generate(llamini_session* s, u32* input, u32 n_in, u32* out, u32 max_
         // prefill positions produce no tokens; run them in one go
         u32 pre = n_in > 1 ? n_in - 1 : 0;
         if (pre > want) pre = (u32)want;
-        if (pre && !run_steps(s, pre)) return total;
+        if (pre && !run_prompt(s, pre)) return total;
         done = pre;
         std::vector<u32> buf;
         u32 last = done;                                   // positions run, as the reference counts them
@@ -909,7 +927,7 @@ struct llamini_batch {
     bool tc = false;                  // matrices on the tcgen05 GEMM (else mma.sync)
     // copies of matrices whose row size is not a multiple of 16 bytes, rows
     // padded to one (the tensor-core GEMM loads rows by TMA): pointer, pitch
-    std::unordered_map<const uint8_t*, std::pair<const uint8_t*, uint64_t>> pitched;
+    std::unordered_map<const uint8_t*, std::pair<const uint8_t*, uint64_t>> pitched;   // PitchMap
     unsigned long long* keys = nullptr;
     void *kc = nullptr, *vc = nullptr;
     lm::StepState* st = nullptr;
@@ -943,6 +961,59 @@ struct BPlan {
 
 bool launch_plan(const BPlan& p, cudaStream_t st) { return p.tc ? launch_tgemm(p.t, st) : launch_bgemm(p.m, st); }
 
+using PitchMap = std::unordered_map<const uint8_t*, std::pair<const uint8_t*, uint64_t>>;
+
+// A copy of m with rows padded to a multiple of 16 bytes, when its rows are
+// not (the tensor-core GEMM loads rows by TMA); recorded in `map`.
+bool make_pitched(llamini_session* s, PitchMap& map, const DevMat& m) {
+    if (!m.ptr || !tgemm_type(m.type) || m.row_bytes % 16 == 0 || map.count(m.ptr)) return true;
+    const uint64_t p = (m.row_bytes + 15) & ~uint64_t(15);
+    uint8_t* d = (uint8_t*)own(s, p * m.rows + 16);
+    if (!d || !LM_CUDA(cudaMemcpy2D(d, p, m.ptr, m.row_bytes, m.row_bytes, m.rows, cudaMemcpyDeviceToDevice)))
+        return false;
+    map[m.ptr] = {d, p};
+    return true;
+}
+bool make_pitched_all(llamini_session* s, PitchMap& map) {
+    bool ok = make_pitched(s, map, s->head);
+    for (u32 l = 0; ok && l < s->n_layers; l++) {
+        const auto& W = s->layers[l];
+        ok = make_pitched(s, map, W.q) && make_pitched(s, map, W.k) && make_pitched(s, map, W.v) &&
+             make_pitched(s, map, W.o) && make_pitched(s, map, W.gate) && make_pitched(s, map, W.up) &&
+             make_pitched(s, map, W.down);
+    }
+    return ok;
+}
+
+// Tensor-core GEMM plan of up to three matrices sharing staged inputs xh/xl of
+// B columns (false: a format or shape the kernel does not take).
+bool plan_tc(const uint16_t* xh, const uint16_t* xl, u32 B, u32* err, const PitchMap& pitched,
+             const DevMat* const* m, float* const* parts, u32 n, u32 K, TGemmArgs* out) {
+    TGemmArgs g;
+    g.xh = xh;
+    g.xl = xl;
+    g.B = B;
+    g.K = K;
+    g.nseg = n;
+    g.err = err;
+    for (u32 i = 0; i < n; i++) {
+        if (m[i]->cols != K) return false;
+        g.seg[i].w = m[i]->ptr;
+        g.seg[i].row_bytes = m[i]->row_bytes;
+        g.seg[i].type = m[i]->type;
+        g.seg[i].rows = m[i]->rows;
+        g.seg[i].part = parts[i];
+        const auto it = pitched.find(m[i]->ptr);
+        if (it != pitched.end()) {
+            g.seg[i].w = it->second.first;
+            g.seg[i].pitch = it->second.second;
+        }
+    }
+    if (!tgemm_plan(g, (u32)sm_count())) return false;
+    *out = g;
+    return true;
+}
+
 // False when a format or shape has no batched kernel; segment i writes its
 // raw sums to parts[i].
 bool batch_gemm(const llamini_batch* b, const DevMat* const* m, float* const* parts, u32 n, u32 K, BPlan* out) {
@@ -951,26 +1022,7 @@ bool batch_gemm(const llamini_batch* b, const DevMat* const* m, float* const* pa
     for (u32 i = 0; i < n; i++)
         if (m[i]->cols != K) return false;
     if (p.tc) {
-        TGemmArgs& g = p.t;
-        g.xh = b->xh;
-        g.xl = b->xl;
-        g.B = b->B;
-        g.K = K;
-        g.nseg = n;
-        g.err = b->err;
-        for (u32 i = 0; i < n; i++) {
-            g.seg[i].w = m[i]->ptr;
-            g.seg[i].row_bytes = m[i]->row_bytes;
-            g.seg[i].type = m[i]->type;
-            g.seg[i].rows = m[i]->rows;
-            g.seg[i].part = parts[i];
-            const auto it = b->pitched.find(m[i]->ptr);
-            if (it != b->pitched.end()) {
-                g.seg[i].w = it->second.first;
-                g.seg[i].pitch = it->second.second;
-            }
-        }
-        if (!tgemm_plan(g, (u32)sm_count())) return false;
+        if (!plan_tc(b->xh, b->xl, b->B, b->err, b->pitched, m, parts, n, K, &p.t)) return false;
     } else {
         BGemmArgs& g = p.m;
         g.xh = b->xh;
@@ -1400,25 +1452,9 @@ bool batch_alloc(llamini_batch* b) {
         }
         return ok;
     };
-    if (b->tc) {
-        // rows of a size that is not a multiple of 16 bytes (Q6_K at some widths):
-        // a copy with 16-byte row pitch, so the tensor-core GEMM can load by TMA
-        auto pitch = [&](const DevMat& m) -> bool {
-            if (!m.ptr || !tgemm_type(m.type) || m.row_bytes % 16 == 0 || b->pitched.count(m.ptr)) return true;
-            const uint64_t p = (m.row_bytes + 15) & ~uint64_t(15);
-            uint8_t* d = (uint8_t*)own(s, p * m.rows + 16);
-            if (!d || !LM_CUDA(cudaMemcpy2D(d, p, m.ptr, m.row_bytes, m.row_bytes, m.rows, cudaMemcpyDeviceToDevice)))
-                return false;
-            b->pitched[m.ptr] = {d, p};
-            return true;
-        };
-        bool ok = pitch(s->head);
-        for (u32 l = 0; ok && l < s->n_layers; l++) {
-            const auto& W = s->layers[l];
-            ok = pitch(W.q) && pitch(W.k) && pitch(W.v) && pitch(W.o) && pitch(W.gate) && pitch(W.up) && pitch(W.down);
-        }
-        if (!ok) return false;
-    }
+    // rows of a size that is not a multiple of 16 bytes (Q6_K at some widths):
+    // copies with a 16-byte row pitch, so the tensor-core GEMM can load by TMA
+    if (b->tc && !make_pitched_all(s, b->pitched)) return false;
     if (!plan_all()) {
         // a shape the tensor-core GEMM does not take: the whole batch on mma.sync
         if (!b->tc) return false;
@@ -1482,6 +1518,246 @@ bool batch_ok(llamini_batch* b) {
     if (e == 0) return true;
     set_error("batched decode: tensor-core GEMM: %s", (e & 1u) ? "a pipeline wait ran out" : "a weight outside the fp16 range");
     return false;
+}
+
+// ---------------------------------------------------------------- prefill
+//
+// Prompt positions in chunks of kPfChunk: per layer the staging, tensor-core
+// GEMMs and finishes of batched decode with the chunk's positions as columns,
+// RoPE and cache writes for the chunk (prope), causal attention over the cache
+// (pattn). Used for the prompt positions whose logits the caller does not read
+// (generate_autoregressive's prefill, session steps inside the prompt).
+
+constexpr u32 kPfChunk = 64;
+int g_prefill = -1;                   // llamini_set_prefill: -1 default (on unless LLAMINI_PREFILL=0)
+
+bool prefill_enabled() {
+    static const bool env_on = [] { const char* e = getenv("LLAMINI_PREFILL"); return !(e && e[0] == '0'); }();
+    return g_prefill >= 0 ? g_prefill == 1 : env_on;
+}
+
+// Build the session's prefill buffers (false, no error: not available).
+bool prefill_build(llamini_session* s) {
+    if (s->pf_state) return s->pf_state > 0;
+    s->pf_state = -1;
+    if (s->tp_world > 1 || (s->kind != 0 && s->kind != 1)) return false;
+    Prefill* pf = new Prefill();
+    s->pf = pf;
+    if (!make_pitched_all(s, pf->pitched)) return false;
+    u32 kmax = s->dim;
+    if (s->qd > kmax) kmax = s->qd;
+    if (s->ffn > kmax) kmax = s->ffn;
+    // partial sums: the largest plan over the step's matrices with full chunks
+    size_t pmax = 0;
+    auto need = [&](const DevMat* const* mm, u32 n, u32 K) -> bool {
+        float* none[3] = {nullptr, nullptr, nullptr};
+        TGemmArgs g;
+        if (!plan_tc(nullptr, nullptr, kPfChunk, nullptr, pf->pitched, mm, none, n, K, &g)) return false;
+        for (u32 i = 0; i < n; i++) {
+            const size_t m = (size_t)g.ksplit * kPfChunk * mm[i]->rows;
+            pmax = pmax > m ? pmax : m;
+        }
+        return true;
+    };
+    bool ok = true;
+    for (u32 l = 0; ok && l < s->n_layers; l++) {
+        const auto& W = s->layers[l];
+        const DevMat* o1[1] = {&W.o};
+        const DevMat* d1[1] = {&W.down};
+        ok = need(o1, 1, s->qd) && need(d1, 1, s->ffn);
+        if (ok && s->kind == 1) {
+            const DevMat* q1[1] = {&W.q};
+            const DevMat* u1[1] = {&W.up};
+            ok = need(q1, 1, s->dim) && need(u1, 1, s->dim);
+        } else if (ok) {
+            const DevMat* qkv[3] = {&W.q, &W.k, &W.v};
+            const DevMat* gu[2] = {&W.gate, &W.up};
+            ok = need(qkv, 3, s->dim) && need(gu, 2, s->dim);
+        }
+    }
+    if (!ok) return false;                                  // a format or shape the GEMM does not take
+    const u32 qkvd = s->qd + 2 * s->kvd, C = kPfChunk;
+    pf->hidden = (float*)own(s, (size_t)C * s->dim * 4);
+    pf->qkv = (float*)own(s, (size_t)C * qkvd * 4);
+    pf->attn = (float*)own(s, (size_t)C * s->qd * 4);
+    pf->ffn_h = (float*)own(s, (size_t)C * s->ffn * 4);
+    pf->osc = (float*)own(s, (size_t)C * 4);
+    pf->xh = (uint16_t*)own(s, (size_t)C * kmax * 2);
+    pf->xl = (uint16_t*)own(s, (size_t)C * kmax * 2);
+    pf->part = (float*)own(s, pmax * 4);
+    pf->part2 = (float*)own(s, pmax * 4);
+    pf->part3 = (float*)own(s, pmax * 4);
+    pf->err = (uint32_t*)own(s, 4);
+    if (!pf->hidden || !pf->qkv || !pf->attn || !pf->ffn_h || !pf->osc || !pf->xh || !pf->xl || !pf->part ||
+        !pf->part2 || !pf->part3 || !pf->err || !LM_CUDA(cudaMemset(pf->err, 0, 4)))
+        return false;
+    s->pf_state = 1;
+    return true;
+}
+
+// Positions p0 .. p0 + C - 1 through every layer (their cache rows written).
+bool prefill_chunk(llamini_session* s, u32 p0, u32 C, cudaStream_t st) {
+    Prefill* pf = s->pf;
+    const bool gpt2 = s->kind == 1;
+    const u32 qkvd = s->qd + 2 * s->kvd, L = s->n_layers;
+    const u32 norm = gpt2 ? NORM_LAYER : NORM_RMS;
+    const u32 np = (C + 15) & ~15u;
+    PEmbedArgs e;
+    e.tokens = s->tokens;
+    e.p0 = p0;
+    e.C = C;
+    e.tok = s->tok;
+    e.pos = s->pos_tab;
+    e.scale = s->emb_scale;
+    e.hidden = pf->hidden;
+    e.dim = s->dim;
+    if (!launch_pembed(e, st)) return false;
+    auto stage = [&](const float* x, u32 K, u32 nm, const float* w, const float* bias) {
+        BStageArgs a;
+        a.x = x;
+        a.ldx = K;
+        a.K = K;
+        a.B = C;
+        a.norm = nm;
+        a.norm_w = w;
+        a.norm_b = bias;
+        a.eps = s->eps;
+        a.xh = pf->xh;
+        a.xl = pf->xl;
+        a.oscale = pf->osc;
+        a.np = np;
+        return launch_bstage(a, st);
+    };
+    auto gemm = [&](const DevMat* const* mm, float* const* pp, u32 n, u32 K, TGemmArgs* g) -> bool {
+        if (!plan_tc(pf->xh, pf->xl, C, pf->err, pf->pitched, mm, pp, n, K, g)) {
+            set_error("prefill: matrix format %u (%u x %u) has no tensor-core plan", mm[0]->type, mm[0]->rows, mm[0]->cols);
+            return false;
+        }
+        return launch_tgemm(*g, st);
+    };
+    auto fin = [&](const TGemmArgs& g, u32 seg, const float* part2, u32 epi, const float* bias, float* out, u32 ldo) {
+        BFinishArgs f;
+        f.part = g.seg[seg].part;
+        f.part2 = part2;
+        f.ksplit = g.ksplit;
+        f.B = C;
+        f.rows = g.seg[seg].rows;
+        f.oscale = pf->osc;
+        f.bias = bias;
+        f.epi = epi;
+        f.out = out;
+        f.ldo = ldo;
+        return f;
+    };
+    const size_t per_layer = (size_t)s->n_kv * s->max_seq * s->hd * (s->kv_f16 ? 2 : 4);
+    for (u32 l = 0; l < L; l++) {
+        const llamini_session::Layer& W = s->layers[l];
+        TGemmArgs g;
+        if (!stage(pf->hidden, s->dim, norm, W.n1w, W.n1b)) return false;
+        if (gpt2) {
+            const DevMat* mm[1] = {&W.q};
+            float* pp[1] = {pf->part};
+            if (!gemm(mm, pp, 1, s->dim, &g) || !launch_bfinish(fin(g, 0, nullptr, EPI_STORE, W.bq, pf->qkv, qkvd), st))
+                return false;
+        } else {
+            const DevMat* mm[3] = {&W.q, &W.k, &W.v};
+            float* pp[3] = {pf->part, pf->part2, pf->part3};
+            if (!gemm(mm, pp, 3, s->dim, &g)) return false;
+            BFinishArgs f = fin(g, 0, nullptr, EPI_STORE, W.bq, pf->qkv, qkvd);
+            f.part_b = g.seg[1].part;
+            f.part_c = g.seg[2].part;
+            f.rows_b = g.seg[1].rows;
+            f.rows_c = g.seg[2].rows;
+            f.bias_b = W.bk;
+            f.bias_c = W.bv;
+            if (!launch_bfinish(f, st)) return false;
+        }
+        void* kc = (uint8_t*)s->kc + l * per_layer;
+        void* vc = (uint8_t*)s->vc + l * per_layer;
+        PRopeArgs r;
+        r.qkv = pf->qkv;
+        r.qkv_stride = qkvd;
+        r.kc = kc;
+        r.vc = vc;
+        r.kv_f16 = s->kv_f16;
+        r.n_heads = s->n_heads;
+        r.n_kv = s->n_kv;
+        r.hd = s->hd;
+        r.max_seq = s->max_seq;
+        r.p0 = p0;
+        r.rope = s->rope_mode;
+        r.theta = s->theta;
+        if (!launch_prope(r, C, st)) return false;
+        PAttnArgs at;
+        at.qkv = pf->qkv;
+        at.qkv_stride = qkvd;
+        at.kc = kc;
+        at.vc = vc;
+        at.kv_f16 = s->kv_f16;
+        at.out = pf->attn;
+        at.out_stride = s->qd;
+        at.n_heads = s->n_heads;
+        at.n_kv = s->n_kv;
+        at.hd = s->hd;
+        at.max_seq = s->max_seq;
+        at.p0 = p0;
+        at.C = C;
+        if (!launch_pattn(at, st)) return false;
+        {
+            const DevMat* mm[1] = {&W.o};
+            float* pp[1] = {pf->part};
+            if (!stage(pf->attn, s->qd, NORM_NONE, nullptr, nullptr) || !gemm(mm, pp, 1, s->qd, &g) ||
+                !launch_bfinish(fin(g, 0, nullptr, EPI_RESID, W.bo, pf->hidden, s->dim), st))
+                return false;
+        }
+        if (!stage(pf->hidden, s->dim, norm, W.n2w, W.n2b)) return false;
+        if (gpt2) {
+            const DevMat* mm[1] = {&W.up};
+            float* pp[1] = {pf->part};
+            if (!gemm(mm, pp, 1, s->dim, &g) || !launch_bfinish(fin(g, 0, nullptr, EPI_GELU, W.bup, pf->ffn_h, s->ffn), st))
+                return false;
+        } else {
+            const DevMat* mm[2] = {&W.gate, &W.up};
+            float* pp[2] = {pf->part, pf->part2};
+            const u32 epi = s->act_gelu ? (u32)EPI_GLU_GELU : (u32)EPI_GLU_SILU;
+            if (!gemm(mm, pp, 2, s->dim, &g) || !launch_bfinish(fin(g, 0, g.seg[1].part, epi, nullptr, pf->ffn_h, s->ffn), st))
+                return false;
+        }
+        {
+            const DevMat* mm[1] = {&W.down};
+            float* pp[1] = {pf->part};
+            if (!stage(pf->ffn_h, s->ffn, NORM_NONE, nullptr, nullptr) || !gemm(mm, pp, 1, s->ffn, &g) ||
+                !launch_bfinish(fin(g, 0, nullptr, EPI_RESID, W.bdown, pf->hidden, s->dim), st))
+                return false;
+        }
+    }
+    return true;
+}
+
+bool run_prompt(llamini_session* s, u32 n) {
+    if (n < 2 || s->trace_on || !prefill_enabled() || !prefill_build(s)) return run_steps(s, n);
+    if ((u64)s->pos + n > s->max_pos) {
+        set_error("position %u + %u steps passes the cache capacity %u", s->pos, n, s->max_pos);
+        return false;
+    }
+    cudaStream_t st = stream();
+    for (u32 done = 0; done < n;) {
+        const u32 C = n - done < kPfChunk ? n - done : kPfChunk;
+        if (!prefill_chunk(s, s->pos + done, C, st)) return false;
+        done += C;
+    }
+    // the decode steps continue at the position after the prompt chunk
+    if (!LM_CUDA(cudaStreamSynchronize(st))) return false;
+    uint32_t e = 0;
+    if (!LM_CUDA(cudaMemcpy(&e, s->pf->err, 4, cudaMemcpyDeviceToHost))) return false;
+    if (e) {
+        set_error("prefill: tensor-core GEMM: %s", (e & 1u) ? "a pipeline wait ran out" : "a weight outside the fp16 range");
+        return false;
+    }
+    s->pos += n;
+    s->st_host->pos = s->pos;
+    return LM_CUDA(cudaMemcpyAsync(&s->st->pos, &s->st_host->pos, 4, cudaMemcpyHostToDevice, st)) &&
+           LM_CUDA(cudaStreamSynchronize(st));
 }
 
 bool batch_run(llamini_batch* b, u32 n) {
@@ -1552,7 +1828,19 @@ int llamini_session_begin(llamini_session* s, const u32* prompt, u32 n_prompt) {
 
 int llamini_session_step(llamini_session* s, u32 n_steps) {
     if (!s) return -1;
-    return lm::run_steps(s, n_steps) ? 0 : -1;
+    // positions whose next token is still the prompt's produce no token: prefill
+    u32 pre = s->pos + 1 < s->n_prompt ? s->n_prompt - 1 - s->pos : 0;
+    if (pre > n_steps) pre = n_steps;
+    if (pre && !lm::run_prompt(s, pre)) return -1;
+    return lm::run_steps(s, n_steps - pre) ? 0 : -1;
+}
+
+int llamini_session_prefill(llamini_session* s) { return s ? s->pf_state : -2; }
+
+int llamini_set_prefill(int enable) {
+    if (enable < -1 || enable > 1) { lm::set_error("prefill setting %d outside -1..1", enable); return -1; }
+    lm::g_prefill = enable;
+    return 0;
 }
 
 int llamini_session_tokens(llamini_session* s, u32* out, u32 n) {
