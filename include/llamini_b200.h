@@ -145,8 +145,9 @@ typedef struct llamini_batch llamini_batch;
 
 /* A batch of up to max_batch (<= 64) independent sequences of at most max_seq
  * positions over a loaded model. Every weight matrix is read once per step for
- * the whole batch; the device KV cache holds max_batch x max_seq positions. All
- * matrices must be Q4_K, Q6_K, Q8_0, Q4_0 or F16 (NULL and a message otherwise).
+ * the whole batch; the device KV cache holds max_batch x max_seq positions. The
+ * matrices may be any of gguf.c's block formats or F16 with rows of a multiple
+ * of 64 elements (256 for K-quants); NULL and a message otherwise.
  * Free it with llamini_batch_free before the model and its GGUF file. */
 llamini_batch* llamini_llama_batch(LLaMAModel* model, u32 max_batch, u32 max_seq);
 llamini_batch* llamini_gpt2_batch(GPT2Model* model, u32 max_batch, u32 max_seq);

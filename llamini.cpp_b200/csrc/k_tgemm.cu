@@ -359,6 +359,98 @@ __device__ __forceinline__ bool dq_q40(const uint8_t* p, uint32_t j, uint32_t* h
     return fabsf(d) * 8.0f <= 65504.0f;
 }
 
+// Q4_1 (gguf.c:445-462): run j = block j; element l < 16 is the low nibble of
+// qs[l], element l + 16 its high nibble; weight q * d + m (q * d is exact, so a
+// fused multiply-add rounds as the reference's multiply-then-add).
+__device__ __forceinline__ bool dq_q41(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
+    const uint8_t* b = p + 20 * j;
+    const uint32_t dm = lds_u32(b);
+    const float d = f16_bits(dm & 0xFFFFu), m = f16_bits(dm >> 16);
+    uint32_t q[4];
+    sm_words<4>(b + 4, q);
+#pragma unroll
+    for (int sl = 0; sl < 4; sl++) {
+        float w[8];
+        const uint32_t sh = sl < 2 ? 0u : 4u;
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const uint32_t n = (q[(2 * sl + e) & 3] >> sh) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int k = 0; k < 4; k++) w[4 * e + k] = __fmaf_rn(magic_byte(n, 0x7440u | (uint32_t)k) - 8388608.0f, d, m);
+        }
+        st8(h + 4 * sl, l + 4 * sl, w);
+    }
+    return fabsf(d) * 15.0f + fabsf(m) <= 65504.0f;
+}
+
+// Q5_0 (gguf.c:463-488): run j = block j; element l < 16 takes the low nibble
+// of qs[l] and bit l of qh, element l + 16 the high nibble and bit l + 16;
+// weight (q - 16) * d, exact.
+__device__ __forceinline__ bool dq_q50(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
+    const uint8_t* b = p + 22 * j;
+    const float d = f16_bits(lds_u16(b));
+    const uint32_t qh = lds_u32(b + 2);
+    uint32_t q[4];
+    sm_words<4>(b + 6, q);
+#pragma unroll
+    for (int sl = 0; sl < 4; sl++) {
+        float w[8];
+        const uint32_t sh = sl < 2 ? 0u : 4u;
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const uint32_t i0 = 4 * ((2 * sl + e) & 3);                  // first qs byte of these 4
+            const uint32_t n = (q[(2 * sl + e) & 3] >> sh) & 0x0F0F0F0Fu;
+            const uint32_t hb = qh >> (i0 + (sl < 2 ? 0u : 16u));       // bits of elements i0 .. i0+3
+            const uint32_t hi = ((hb & 1u) | ((hb & 2u) << 7) | ((hb & 4u) << 14) | ((hb & 8u) << 21)) << 4;
+            const uint32_t q5 = n | hi;
+#pragma unroll
+            for (int k = 0; k < 4; k++) w[4 * e + k] = __fmul_rn(magic_byte(q5, 0x7440u | (uint32_t)k) - 8388624.0f, d);
+        }
+        st8(h + 4 * sl, l + 4 * sl, w);
+    }
+    return fabsf(d) * 16.0f <= 65504.0f;
+}
+
+// Q5_K (gguf.c:530-560): Q4_K plus a high-bit plane: run j = sub-block j, the
+// quants are nibble j % 2 of qs[32 (j/2) + l] with bit j of qh[l] as bit 4;
+// weight d*sc_j*q - dmin*m_j (the product exact, one fused multiply-add).
+__device__ __forceinline__ bool dq_q5k(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
+    const uint4 hd = *reinterpret_cast<const uint4*>(p);
+    const uint32_t sh8 = 8u * (j & 3u);
+    uint32_t sc, mn;
+    if (j < 4) {
+        sc = (hd.y >> sh8) & 63u;
+        mn = (hd.z >> sh8) & 63u;
+    } else {
+        sc = ((hd.w >> sh8) & 15u) | (((hd.y >> (sh8 + 6)) & 3u) << 4);
+        mn = ((hd.w >> (sh8 + 4)) & 15u) | (((hd.z >> (sh8 + 6)) & 3u) << 4);
+    }
+    const float d1 = __fmul_rn(f16_bits(hd.x & 0xFFFFu), u2f(sc));
+    const float m1 = __fmul_rn(f16_bits(hd.x >> 16), u2f(mn));
+    const uint8_t* qp = p + 48 + 32 * (j >> 1);
+    const uint8_t* hp = p + 16;
+    const uint32_t sh = (j & 1u) * 4u;
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+        const uint4 q = *reinterpret_cast<const uint4*>(qp + 16 * half);
+        const uint4 hq = *reinterpret_cast<const uint4*>(hp + 16 * half);
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+        const uint32_t hw[4] = {hq.x, hq.y, hq.z, hq.w};
+#pragma unroll
+        for (int sl = 0; sl < 2; sl++) {
+            float w[8];
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const uint32_t n = ((qw[2 * sl + e] >> sh) & 0x0F0F0F0Fu) | (((hw[2 * sl + e] >> j) & 0x01010101u) << 4);
+#pragma unroll
+                for (int b = 0; b < 4; b++) w[4 * e + b] = __fmaf_rn(d1, magic_byte(n, 0x7440u | (uint32_t)b) - 8388608.0f, -m1);
+            }
+            st8(h + 4 * (2 * half + sl), l + 4 * (2 * half + sl), w);
+        }
+    }
+    return fabsf(d1) * 31.0f + fabsf(m1) <= 65504.0f;
+}
+
 // F16 rows: the weights are their own hi halves; lo is zero.
 __device__ __forceinline__ bool dq_f16(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
     const uint8_t* b = p + 64 * j;
@@ -613,6 +705,9 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
                     case T_Q6_K: fine = dq_q6k(p, j, h, l); break;
                     case T_Q8_0: fine = dq_q80(p, j, h, l); break;
                     case T_Q4_0: fine = dq_q40(p, j, h, l); break;
+                    case T_Q4_1: fine = dq_q41(p, j, h, l); break;
+                    case T_Q5_0: fine = dq_q50(p, j, h, l); break;
+                    case T_Q5_K: fine = dq_q5k(p, j, h, l); break;
                     default: fine = dq_f16(p, j, h, l); break;
                     }
                     inrange = inrange && fine;
@@ -646,21 +741,26 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
 
 // ---------------------------------------------------------------- host side
 
-bool tgemm_type(uint32_t t) { return t == T_Q4_K || t == T_Q6_K || t == T_Q8_0 || t == T_Q4_0 || t == T_F16; }
+bool tgemm_type(uint32_t t) {
+    return t == T_Q4_K || t == T_Q5_K || t == T_Q6_K || t == T_Q8_0 || t == T_Q4_0 || t == T_Q4_1 || t == T_Q5_0 || t == T_F16;
+}
 
 // Elements per raw unit: a K-quant super-block; eight 32-element blocks when K
 // allows (a 16-byte multiple of bytes: one TMA box per unit); F16 64 elements.
 static uint32_t tg_ru(uint32_t type, uint32_t K) {
-    if (type == T_Q4_K || type == T_Q6_K) return 256;
+    if (type == T_Q4_K || type == T_Q5_K || type == T_Q6_K) return 256;
     if (type == T_F16) return 64;
     return K % 256 == 0 ? 256u : 64u;
 }
 static uint32_t tg_ub(uint32_t type, uint32_t ru) {
     switch (type) {
     case T_Q4_K: return 144;
+    case T_Q5_K: return 176;
     case T_Q6_K: return 210;
     case T_Q8_0: return ru / 32 * 34;
     case T_Q4_0: return ru / 32 * 18;
+    case T_Q4_1: return ru / 32 * 20;
+    case T_Q5_0: return ru / 32 * 22;
     default: return ru * 2;     // F16
     }
 }
@@ -719,7 +819,7 @@ bool tgemm_plan(TGemmArgs& a, uint32_t sms) {
         if (S.row_bytes != type_bytes(S.type, a.K)) return false;
         if (S.pitch == 0) S.pitch = S.row_bytes;
         if (S.pitch < S.row_bytes) return false;
-        kq = kq || S.type == T_Q4_K || S.type == T_Q6_K;
+        kq = kq || S.type == T_Q4_K || S.type == T_Q5_K || S.type == T_Q6_K;
         S.ru = tg_ru(S.type, a.K);
         S.ub = tg_ub(S.type, S.ru);
         if (S.pitch % 16 != 0) a.tma = 0;                 // TMA needs 16-byte row strides

@@ -41,7 +41,7 @@ def _tokens(gpu, b, seq, n):
     return out[:min(k, n)].tolist()
 
 
-@pytest.mark.parametrize("name", ["tiny_llama", "tiny_tied", "tiny_gpt2"])
+@pytest.mark.parametrize("name", ["tiny_llama", "tiny_tied", "tiny_gpt2", "tiny_mixed", "tiny_qwen2"])
 def test_batch_streams_equal_single_sequence(gpu, orc, tiny, golden, name):
     path = tiny.ensure(name)
     m = gpu.Model(path)
@@ -80,13 +80,48 @@ def test_batch_streams_equal_single_sequence(gpu, orc, tiny, golden, name):
         m.close()
 
 
-def test_batch_rejects_unsupported_formats(gpu, tiny):
-    m = gpu.Model(tiny.ensure("tiny_mixed"))       # Q4_1, Q5_0, Q5_K matrices
+def test_batch_gemm_kinds(gpu, tiny):
+    """Every block format takes the tensor-core GEMM; the mma.sync GEMM (kept
+    behind llamini_set_batch_gemm(0)) refuses Q4_1, Q5_0 and Q5_K with a message."""
+    L = gpu.lib()
+    m = gpu.Model(tiny.ensure("tiny_mixed"))       # Q4_0 Q4_1 Q5_0 Q8_0 Q5_K Q4_K Q6_K matrices
     try:
-        assert not gpu.lib().llamini_llama_batch(C.byref(m.model), 4, 32)
-        assert "batched" in gpu.last_error()
-        gpu.lib().llamini_clear_error()
+        b = L.llamini_llama_batch(C.byref(m.model), 4, 32)
+        assert b, gpu.last_error()
+        assert L.llamini_batch_gemm_kind(b) == 1
+        L.llamini_batch_free(b)
+        assert L.llamini_set_batch_gemm(0) == 0
+        try:
+            assert not L.llamini_llama_batch(C.byref(m.model), 4, 32)
+            assert "batched" in gpu.last_error()
+            L.llamini_clear_error()
+        finally:
+            L.llamini_set_batch_gemm(-1)
     finally:
+        m.close()
+
+
+@pytest.mark.parametrize("name", ["tiny_llama", "tiny_gpt2"])
+def test_batch_mma_gemm_streams(gpu, tiny, golden, name):
+    """The mma.sync GEMM (llamini_set_batch_gemm(0)) still decodes the golden
+    prompt's stream."""
+    L = gpu.lib()
+    g = golden["tokens"][name]
+    m = gpu.Model(tiny.ensure(name))
+    assert L.llamini_set_batch_gemm(0) == 0
+    try:
+        b = _batch(gpu, m, 2, m.max_seq)
+    finally:
+        L.llamini_set_batch_gemm(-1)
+    try:
+        assert L.llamini_batch_gemm_kind(b) == 0
+        _begin(gpu, b, [g["prompt"], g["prompt"][:3]])
+        steps = min(m.max_seq, 40) - 1
+        assert L.llamini_batch_step(b, steps) == 0, gpu.last_error()
+        n = min(len(g["tokens"]), steps + 1)
+        assert _tokens(gpu, b, 0, n) == g["tokens"][:n]
+    finally:
+        L.llamini_batch_free(b)
         m.close()
 
 

@@ -40,10 +40,7 @@ def test_prefill_golden_streams(gpu, tiny, golden, name):
         on = _gen(gpu, m, prompt, 20, 1)
         off = _gen(gpu, m, prompt, 20, 0)
         assert on == off, (on, off)
-        # every matrix of these models takes the tensor-core path except tiny_qwen2's
-        # Q5_0 ones, which keep the one-position-at-a-time path
-        want_state = -1 if name == "tiny_qwen2" else 1
-        assert gpu.lib().llamini_session_prefill(m.session()) == want_state
+        assert gpu.lib().llamini_session_prefill(m.session()) == 1      # every format takes the GEMM
     finally:
         m.close()
 
