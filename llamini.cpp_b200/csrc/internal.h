@@ -240,7 +240,8 @@ struct BStageArgs {
     float* sx = nullptr;           // [B][K/16] 16-element sums * 2^(E_b - 24)
     float* oscale = nullptr;       // [B] 2^(24 - E_b)
     // nonzero: xh/xl in the tensor-core GEMM's layout [K/8][np/8][8][8] for
-    // np (the batch padded to 16) columns, and no 16-element sums
+    // np (the batch padded to 16) columns, no 16-element sums; when K % 256
+    // == 0 also the 32-element sums after the inputs in xh (tg_xh_halves)
     uint32_t np = 0;
 };
 struct BSeg {
@@ -308,6 +309,10 @@ bool launch_bstage(const BStageArgs& a, cudaStream_t st);
 
 // Tensor-core (tcgen05) dequant GEMM for a batch of vectors (k_tgemm.cu):
 // same partial sums as bgemm_kernel, inputs staged with BStageArgs::np.
+// A operand kinds of a segment: TG_PLAIN the weights as fp16 hi + lo;
+// TG_KMIN (Q4_K, Q5_K) d*sc*q as fp16 hi + lo, with the -dmin*m terms added by
+// extra MMAs against the staged 32-element sums of the inputs.
+constexpr uint32_t TG_PLAIN = 0, TG_KMIN = 1;
 struct TSeg {
     const uint8_t* w = nullptr;
     uint64_t row_bytes = 0;
@@ -315,14 +320,18 @@ struct TSeg {
     uint32_t type = 0, rows = 0;
     float* part = nullptr;         // [ksplit][B][rows] raw sums
     // filled by tgemm_plan: first row block, elements per raw unit, bytes of
-    // one row's raw unit, raw-buffer row stride (= the TMA box width)
-    uint32_t rb0 = 0, ru = 0, ub = 0, rrs = 0;
+    // one row's raw unit, raw-buffer row stride (= the TMA box width), and the
+    // A operand kind (TG_PLAIN, TG_KMIN)
+    uint32_t rb0 = 0, ru = 0, ub = 0, rrs = 0, mode = 0;
 };
+// Halves of an xh buffer staged for the tensor-core GEMM: the inputs, then
+// (K % 256 == 0) per super-block 16 x np halves of 32-element sums.
+inline size_t tg_xh_halves(size_t K, size_t np) { return np * (K + K / 16); }
 struct alignas(64) TGemmArgs {
     // filled by tgemm_plan: per segment a 2-D TMA map of the rows as uint16
     // (used when `tma`; otherwise 16-byte cp.async copies)
     CUtensorMap tmap[3];
-    const uint16_t* xh = nullptr;  // staged inputs, [K/8][NP/8][8][8] halves
+    const uint16_t* xh = nullptr;  // staged inputs, [K/8][NP/8][8][8] halves (then the sums)
     const uint16_t* xl = nullptr;
     uint32_t B = 0, K = 0;
     uint32_t nseg = 0;
@@ -332,6 +341,7 @@ struct alignas(64) TGemmArgs {
     // row blocks, raw buffer bytes, A/x stages, tensor-memory columns, CTAs
     uint32_t NP = 0, ue = 0, ups = 0, ksplit = 0, rblocks = 0, raw_bytes = 0, stages = 0, tcols = 0, grid = 0;
     uint32_t tma = 0;
+    uint32_t kmin = 0;             // some segment is TG_KMIN
 };
 // ---------------------------------------------------------------- tensor parallelism
 // One process per GPU; LLaMA sessions hold this rank's shard of the heads and

@@ -110,9 +110,28 @@ __device__ void stage_core(const BStageArgs& a, float* xf, uint32_t b, float* re
 #pragma unroll
             for (int j = 0; j < 4; j++) v[j] = xf[4 * i + j] * F;
         }
-        float rs = ((v[0] + v[1]) + (v[2] + v[3])) * 5.9604644775390625e-08f;   // units of 2^(E-24)
+        const float s4 = (v[0] + v[1]) + (v[2] + v[3]);
+        float rs = s4 * 5.9604644775390625e-08f;        // units of 2^(E-24)
         rs += __shfl_xor_sync(0xffffffffu, rs, 1);
         rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+        if (a.np && K % 256 == 0) {
+            // 32-element sums (lanes 8t .. 8t + 7) for the tensor-core GEMM's
+            // K-quant min terms: x * 2^(E-5) split into fp16 hi + lo, after the
+            // staged inputs at xh + K np, per super-block u the K-major chunk
+            // [2][np/8][8][8]: element (b, k) at half 16np u + 8np (k/8) + 8b + k%8
+            // with k = j (hi) or 8 + j (lo) for sub-block j
+            float s32 = s4 + __shfl_xor_sync(0xffffffffu, s4, 1);
+            s32 += __shfl_xor_sync(0xffffffffu, s32, 2);
+            s32 += __shfl_xor_sync(0xffffffffu, s32, 4);
+            if (i < n4 && (i & 7u) == 0) {
+                const float sv = s32 * 0.03125f;
+                const __half sh = __float2half_rn(sv), sl = __float2half_rn(sv - __half2float(sh));
+                __half* gs = reinterpret_cast<__half*>(a.xh) + (uint64_t)K * a.np + (uint64_t)(i >> 6) * 16u * a.np +
+                             8u * b + ((i >> 3) & 7u);
+                gs[0] = sh;
+                gs[8u * a.np] = sl;
+            }
+        }
         if (i < n4 && a.np) {
             // tensor-core layout: element (b, k) at half (k/8) * 8np + 8b + k%8
             __half h[4], l[4];

@@ -6,23 +6,39 @@
 // in their GGUF block layout in HBM. A tile is 128 rows of one matrix x one K
 // range; one persistent CTA per SM walks its tiles with five roles:
 //
-//   raw warp       bulk copies (cp.async.bulk, the TMA engine) of each row's
+//   raw warp       bulk copies (TMA, cp.async.bulk.tensor) of each row's
 //                  bytes of the current unit -- one 256-element super-block for
-//                  Q4_K/Q6_K, 64 elements otherwise -- into a ring of raw buffers
+//                  K-quants, eight 32-element blocks or 64 elements otherwise --
+//                  into a ring of raw buffers
 //   x warp         bulk copies of the staged inputs of each 64-element slab
-//   8 dequant      decode a slab (128 rows x 64 elements) to f32 exactly as
-//   warps          gguf.c:409-594 does, split each weight into fp16 hi + lo
-//                  (22 significant bits) and store both in the UMMA K-major,
-//                  no-swizzle layout
-//   MMA warp       allocates tensor memory; one thread issues tcgen05.mma
-//                  kind::f16 (M = 128, N = batch padded to 16, K = 16, f32
-//                  accumulators in tensor memory): w_hi x_hi + w_hi x_lo +
-//                  w_lo x_hi per 16-element step; tcgen05.commit frees each
-//                  stage and hands each finished tile's accumulator (two, used
-//                  alternately) to the epilogue
-//   4 epilogue     read the accumulators (tcgen05.ld) and store raw sums to
-//   warps          part[ksplit][B][rows] in the units that bfinish_kernel
-//                  (k_bgemm.cu) scales and finishes
+//                  (and of the super-block's sums for TG_KMIN tiles)
+//   16 dequant     two groups of 8 decode alternate slabs (128 rows x 64
+//   warps          elements) from the raw units into the A operand in tensor
+//                  memory (below)
+//   3 MMA warps    one allocates tensor memory; one thread per warp issues
+//                  tcgen05.mma kind::f16 (M = 128, N = batch padded to 16,
+//                  K = 16, f32 accumulators in tensor memory) of one chain --
+//                  A_hi x_hi, A_hi x_lo, A_lo x_hi -- each into its own
+//                  accumulator so their MMAs overlap in the tensor pipe;
+//                  tcgen05.commit frees each stage and hands each finished tile
+//                  (two accumulator sets, used by alternate tiles) to the epilogue
+//   4 epilogue     read the accumulators (tcgen05.ld), add the chains and
+//   warps          store raw sums to part[ksplit][B][rows] in the units that
+//                  bfinish_kernel (k_bgemm.cu) scales and finishes
+//
+// The A operand (fp16 hi + lo, 22 significant bits), per format:
+//   TG_PLAIN  each weight as gguf.c:409-503 and 561-590 decode it: Q8_0, Q4_0,
+//             Q5_0 (q - z) * d and Q6_K (d sc)(q - 32) from exact fp16 pair
+//             arithmetic (hi the rounded product, lo the remainder); Q4_1 and
+//             F16 from the f32 weight
+//   TG_KMIN   (Q4_K, Q5_K, gguf.c:504-560: w = d sc_j q - dmin m_j) A = d (sc_j q),
+//             the integer sc_j q from one exact fp16 fused multiply-add; the
+//             -dmin m_j terms enter through two more K = 16 MMAs per
+//             super-block (chain 2): A = -32 dmin m_j (hi, lo) from shared
+//             memory against the staged 32-element sums of x * 2^-5 (hi, lo)
+// The products are exact and accumulate in f32, so the sums differ from the
+// reference's f32 dot products only by rounding order (and, for K-quants, by
+// the reference's rounding of each weight to f32).
 //
 // Inputs are staged by bstage_kernel as x * 2^E (per sequence) split into fp16
 // hi + lo, laid out [K/8][NP/8][8 sequences][8 elements], the same UMMA layout,
@@ -51,26 +67,43 @@ namespace lm {
 constexpr uint32_t kTRows = 128;                 // MMA M: matrix rows per CTA
 constexpr uint32_t kTSlab = 64;                  // K elements per stage
 // Tensor memory (512 columns): two accumulator sets (used by alternate tiles)
-// of three independent f32 accumulators -- w_hi x_hi, w_hi x_lo, w_lo x_hi --
-// 64 columns each, so the MMAs of a K step do not wait on one another; then
-// kTNA stages of the A slab, 32 columns hi and 32 lo (fp16 pairs: column c
-// holds K elements 2c and 2c + 1).
+// of three independent f32 accumulators (one per MMA chain), 64 columns each,
+// so the MMAs of a K step do not wait on one another; then kTNA stages of the
+// A slab, 32 columns hi and 32 lo (fp16 pairs: column c holds K elements 2c
+// and 2c + 1).
 constexpr uint32_t kTAccW = 64;                  // columns per accumulator (NP <= 64)
+// Build-time pipeline shape (-D overrides): accumulator sets, A stages and
+// dequant groups. The defaults measured fastest on llama_1b batch 64; one set
+// with four A stages, or one dequant group, were within a few percent.
+#ifndef LM_TG_SETS
+#define LM_TG_SETS 2
+#endif
+#ifndef LM_TG_NA
+#define LM_TG_NA 2
+#endif
 constexpr uint32_t kTSetCols = 3 * kTAccW;
-constexpr uint32_t kTACol0 = 2 * kTSetCols;      // first A-stage column
+constexpr uint32_t kTSets = LM_TG_SETS;          // accumulator sets (alternate tiles)
+constexpr uint32_t kTACol0 = kTSets * kTSetCols; // first A-stage column
 constexpr uint32_t kTACols = 64;
-constexpr uint32_t kTNA = 2;                     // A stages in tensor memory
+constexpr uint32_t kTNA = LM_TG_NA;              // A stages in tensor memory
 constexpr uint32_t kTCols = 512;
+static_assert(kTACol0 + kTNA * kTACols <= kTCols, "tensor memory: accumulators and A stages exceed 512 columns");
+#ifndef LM_TG_GROUPS
+#define LM_TG_GROUPS 2
+#endif
 constexpr uint32_t kTGroupWarps = 8;            // one dequant group: a slab's 128 rows x 2 runs
-constexpr uint32_t kTDeqWarps = 16;             // warps 0-15: two groups decode alternate slabs
-constexpr uint32_t kTEpiWarps = 4;              // warps 16-19 (tensor-memory lanes 0-127)
-constexpr uint32_t kTIssuers = 3;               // warps 20-22: one issuing thread per accumulator chain
-constexpr uint32_t kTWarpEpi = 16, kTWarpMma = 20, kTWarpRaw = 23, kTWarpX = 24;
-constexpr uint32_t kTThreads = 25 * 32;
+constexpr uint32_t kTGroups = LM_TG_GROUPS;     // groups decode slabs i with i % kTGroups == group
+constexpr uint32_t kTDeqWarps = kTGroups * kTGroupWarps;
+constexpr uint32_t kTEpiWarps = 4;              // tensor-memory lanes 0-127
+constexpr uint32_t kTIssuers = 3;               // one issuing thread per accumulator chain
+constexpr uint32_t kTWarpEpi = kTDeqWarps, kTWarpMma = kTWarpEpi + kTEpiWarps, kTWarpRaw = kTWarpMma + kTIssuers,
+                   kTWarpX = kTWarpRaw + 1;
+constexpr uint32_t kTThreads = (kTWarpX + 1) * 32;
 constexpr uint32_t kTAlign = 1024;              // dynamic shared memory aligned up to this
 constexpr uint32_t kTSlack = 64;                // after the raw buffers: the decoders' word reads
                                                 // may run up to 8 bytes past a row's last byte
 constexpr uint32_t kTRaw = 4;                    // raw buffers
+constexpr uint32_t kTMinBytes = 2 * 2 * 16 * 128;    // two K = 16 A tiles of 128 rows (fp16)
 constexpr uint32_t kTMaxStages = 4;              // x stages in shared memory
 constexpr uint64_t kTWaitNs = 2000000000ull;     // 2 s
 constexpr size_t kTSmemMax = 226 * 1024;
@@ -82,7 +115,7 @@ struct TShared {
     uint64_t raw_full[kTRaw], raw_empty[kTRaw];
     uint64_t xfull[kTMaxStages], xempty[kTMaxStages];   // x slab landed / read by its MMAs
     uint64_t afull[kTNA], aempty[kTNA];                  // A slab in tensor memory / read by its MMAs
-    uint64_t accf[2], acce[2];          // accumulator full (MMA -> epilogue) / empty
+    uint64_t accf[kTSets], acce[kTSets];   // accumulator full (MMA -> epilogue) / empty
     uint64_t mdone;                     // every MMA of the CTA finished
     uint32_t tmem;
     uint32_t abort;
@@ -139,6 +172,8 @@ __device__ __forceinline__ bool tg_wait_warp(TShared& S, uint64_t* bar, uint32_t
 __device__ __forceinline__ void tg_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
 }
+// A 16-bit field of the weights in global memory (2-byte aligned).
+__device__ __forceinline__ uint32_t ldg_u16(const uint8_t* p) { return __ldg(reinterpret_cast<const unsigned short*>(p)); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 
 // TMA tiled load of a 2-D box (x in elements of the map, y in rows) into
@@ -183,13 +218,21 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
 
-// 16 consecutive f32 columns of this warp's 32 tensor-memory lanes, waited for.
+// 16 consecutive f32 columns of this warp's 32 tensor-memory lanes, not yet
+// waited for: the registers are valid after tmem_wait_ld.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n"
-                 "tcgen05.wait::ld.sync.aligned;\n"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
                    "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
                  : "r"(taddr) : "memory");
+}
+// Every tcgen05.ld of this thread has completed; `r` (the registers they
+// wrote) is tied in so no use is scheduled above the wait.
+__device__ __forceinline__ void tmem_wait_ld(uint32_t* r) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :: "memory");
 }
 
 // This warp's 32 tensor-memory lanes, 16 consecutive columns, from registers.
@@ -222,6 +265,46 @@ __device__ __forceinline__ void sm_words(const uint8_t* p, uint32_t* w) {
     }
 }
 
+// fp16 pair arithmetic on raw bits, round to nearest, subnormals kept.
+__device__ __forceinline__ uint32_t hfma2u(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t hadd2u(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("add.rn.f16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+// Two bytes of `word` (PRMT selector sel: 0x4140 bytes 0 and 1, 0x4342 bytes 2
+// and 3) as the fp16 pair 1024 + byte: 0x64 above a byte is 2^10 with the byte
+// as the low mantissa bits.
+__device__ __forceinline__ uint32_t h1024(uint32_t word, uint32_t sel) { return __byte_perm(word, 0x64u, sel); }
+__device__ __forceinline__ uint32_t h2pair(float v) {
+    const __half h = __float2half_rn(v);
+    const uint32_t b = __half_as_ushort(h);
+    return b | (b << 16);
+}
+constexpr uint32_t kHNeg = 0x80008000u;          // sign bits of an fp16 pair
+// Exact fp16 hi + lo of integers t*s (t, s fp16 pairs whose exact products have
+// at most 22 significant bits): hi the rounded product, lo the remainder.
+__device__ __forceinline__ void hilo(uint32_t t, uint32_t s, uint32_t& hi, uint32_t& lo) {
+    hi = hmul2u(t, s);
+    lo = hfma2u(t, s, hi ^ kHNeg);
+}
+
+// This warp's 32 tensor-memory lanes, 8 consecutive columns, from registers.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n"
+                 ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+
 // ---------------------------------------------------------------- decoders
 // Each yields the 32 weights of run j of a unit -- 32 consecutive K elements,
 // bit-exact with gguf.c -- as fp16 hi and lo pairs: h[i] and l[i] hold
@@ -247,50 +330,92 @@ __device__ __forceinline__ void st8(uint32_t* h, uint32_t* l, const float* w) {
     }
 }
 
-// Q4_K (gguf.c:504-529): run j = sub-block j; its quants are the low (j even)
-// or high (j odd) nibbles of qs[32 (j/2) + l], weight d*sc_j*q - dmin*m_j.
-// d*sc_j*q is exact in f32 (at most 21 significant bits), so one fused
-// multiply-add rounds exactly as the reference's multiply-then-subtract.
-__device__ __forceinline__ bool dq_q4k(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
+// 6-bit scale of sub-block j of a K-quant super-block (gguf.c:391-399) from
+// its first 16 bytes (d, dmin, scale bytes 0-11).
+__device__ __forceinline__ uint32_t k4_scale(const uint4& hd, uint32_t j) {
+    const uint32_t sh8 = 8u * (j & 3u);
+    return j < 4 ? (hd.y >> sh8) & 63u : ((hd.w >> sh8) & 15u) | (((hd.y >> (sh8 + 6)) & 3u) << 4);
+}
+// The min terms of a K-quant super-block (gguf.c:391-399, the eight 6-bit
+// mins m0..m7): -32 dmin m_j as exact fp16 hi + lo pairs (m0, m1) .. (m6, m7),
+// the A rows of the two min MMAs (the staged sums are x * 2^-5 per 32 elements).
+__device__ __forceinline__ bool k4_mins(const uint8_t* p, uint32_t* mh, uint32_t* ml) {
     const uint4 hd = *reinterpret_cast<const uint4*>(p);
-    // 6-bit scale and min of sub-block j (gguf.c:391-399) from scale bytes 0-11
-    const uint32_t jj = j & 3u, sh8 = 8u * jj;
-    uint32_t sc, mn;
-    if (j < 4) {
-        sc = (hd.y >> sh8) & 63u;
-        mn = (hd.z >> sh8) & 63u;
-    } else {
-        sc = ((hd.w >> sh8) & 15u) | (((hd.y >> (sh8 + 6)) & 3u) << 4);
-        mn = ((hd.w >> (sh8 + 4)) & 15u) | (((hd.z >> (sh8 + 6)) & 3u) << 4);
-    }
-    const float d1 = __fmul_rn(f16_bits(hd.x & 0xFFFFu), u2f(sc));
-    const float m1 = __fmul_rn(f16_bits(hd.x >> 16), u2f(mn));
+    const uint32_t lo = hd.z & 0x3F3F3F3Fu;                                        // m0 .. m3
+    const uint32_t hi = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);  // m4 .. m7
+    const uint32_t n1024 = 0xE400E400u;                                            // -1024, -1024
+    const float dmin = f16_bits(hd.x >> 16);
+    const uint32_t dm2 = h2pair(-32.0f * dmin);
+    hilo(hadd2u(h1024(lo, 0x4140u), n1024), dm2, mh[0], ml[0]);
+    hilo(hadd2u(h1024(lo, 0x4342u), n1024), dm2, mh[1], ml[1]);
+    hilo(hadd2u(h1024(hi, 0x4140u), n1024), dm2, mh[2], ml[2]);
+    hilo(hadd2u(h1024(hi, 0x4342u), n1024), dm2, mh[3], ml[3]);
+    return fabsf(dmin) * 2016.0f <= 65504.0f;
+}
+
+// Q4_K (gguf.c:504-529), TG_KMIN: run j = sub-block j; its quants are the low
+// (j even) or high (j odd) nibbles of qs[32 (j/2) + l]. The integer sc_j * q
+// comes from 1024 + q (low nibbles) or 1024 + 16q (high nibbles, not shifted
+// down) by one exact fp16 fused multiply-add -- (1024 + q) sc - 1024 sc or
+// (1024 + 16q) sc/16 - 64 sc -- and A = d (sc_j q) as its exact fp16 hi + lo.
+__device__ __forceinline__ bool dqf_q4k(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
+    const uint4 hd = *reinterpret_cast<const uint4*>(p);
+    const float sc = u2f(k4_scale(hd, j));
+    const bool odd = (j & 1u) != 0;
+    const uint32_t s2 = h2pair(odd ? sc * 0.0625f : sc), c2 = h2pair(odd ? -64.0f * sc : -1024.0f * sc);
+    const uint32_t dh = hd.x & 0xFFFFu, d2 = dh | (dh << 16);
+    const uint32_t mask = odd ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
     const uint8_t* qp = p + 16 + 32 * (j >> 1);
-    const uint32_t sh = (j & 1u) * 4u;
 #pragma unroll
     for (int half = 0; half < 2; half++) {
         const uint4 q = *reinterpret_cast<const uint4*>(qp + 16 * half);
         const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-        for (int sl = 0; sl < 2; sl++) {
-            float w[8];
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const uint32_t n = (qw[2 * sl + e] >> sh) & 0x0F0F0F0Fu;
-#pragma unroll
-                for (int b = 0; b < 4; b++) w[4 * e + b] = __fmaf_rn(d1, magic_byte(n, 0x7440u | (uint32_t)b) - 8388608.0f, -m1);
-            }
-            st8(h + 4 * (2 * half + sl), l + 4 * (2 * half + sl), w);
+        for (int e = 0; e < 4; e++) {
+            const uint32_t n = qw[e] & mask;
+            const int i = 8 * half + 2 * e;
+            hilo(hfma2u(h1024(n, 0x4140u), s2, c2), d2, h[i], l[i]);
+            hilo(hfma2u(h1024(n, 0x4342u), s2, c2), d2, h[i + 1], l[i + 1]);
         }
     }
-    return fabsf(d1) * 15.0f + fabsf(m1) <= 65504.0f;
+    return fabsf(f16_bits(dh)) * 945.0f <= 65504.0f;
 }
 
-// Q6_K (gguf.c:561-590): run j covers elements 128H + 32c + l (H = j/4,
-// c = j%4, l < 32): low 4 bits from nibble c/2 of ql[64H + 32(c%2) + l], high
-// 2 bits from bits 2c of qh[32H + l], scale sc[8H + 2c + l/16]; weight
-// (d*sc)*(q - 32), exact in f32.
-__device__ __forceinline__ bool dq_q6k(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
+// Q5_K (gguf.c:530-560), TG_KMIN: Q4_K plus a high-bit plane: run j's quants
+// are nibble j % 2 of qs[32 (j/2) + l] with bit j of qh[l] as bit 4;
+// A = d (sc_j q) as exact fp16 hi + lo.
+__device__ __forceinline__ bool dqf_q5k(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
+    const uint4 hd = *reinterpret_cast<const uint4*>(p);
+    const float sc = u2f(k4_scale(hd, j));
+    const uint32_t s2 = h2pair(sc), c2 = h2pair(-1024.0f * sc);
+    const uint32_t dh = hd.x & 0xFFFFu, d2 = dh | (dh << 16);
+    const uint8_t* qp = p + 48 + 32 * (j >> 1);
+    const uint8_t* hp = p + 16;
+    const uint32_t sh = (j & 1u) * 4u;
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+        const uint4 q = *reinterpret_cast<const uint4*>(qp + 16 * half);
+        const uint4 hq = *reinterpret_cast<const uint4*>(hp + 16 * half);
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+        const uint32_t hw[4] = {hq.x, hq.y, hq.z, hq.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const uint32_t n = ((qw[e] >> sh) & 0x0F0F0F0Fu) | (((hw[e] >> j) & 0x01010101u) << 4);
+            const int i = 8 * half + 2 * e;
+            hilo(hfma2u(h1024(n, 0x4140u), s2, c2), d2, h[i], l[i]);
+            hilo(hfma2u(h1024(n, 0x4342u), s2, c2), d2, h[i + 1], l[i + 1]);
+        }
+    }
+    return fabsf(f16_bits(dh)) * 1953.0f <= 65504.0f;
+}
+
+// Q6_K (gguf.c:561-590): run j covers elements 128H + 32c + l (H = j/4, c = j%4,
+// l < 32): low 4 bits from nibble c/2 of ql[64H + 32(c%2) + l], high 2 bits
+// from bits 2c of qh[32H + l], scale sc[8H + 2c + l/16]; weight (d sc)(q - 32)
+// with d sc exact in f32 and split into fp16 hi + lo, q - 32 exact in fp16
+// ((1024 + q) - 1056): hi = (q-32) ds_hi rounded, lo = (q-32) ds_lo plus the
+// exact remainder of hi, rounded once (22 significant bits in all).
+__device__ __forceinline__ bool dqf_q6k(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
     const uint32_t H = j >> 2, c = j & 3u;
     uint32_t ql[8], qh[8];
     sm_words<8>(p + 64 * H + 32 * (c & 1u), ql);
@@ -299,69 +424,67 @@ __device__ __forceinline__ bool dq_q6k(const uint8_t* p, uint32_t j, uint32_t* h
     const float d = f16_bits(lds_u16(p + 208));
     const float ds0 = __fmul_rn(d, (float)(int)(int8_t)(uint8_t)(sw & 0xFFu));
     const float ds1 = __fmul_rn(d, (float)(int)(int8_t)(uint8_t)((sw >> 8) & 0xFFu));
+    const uint32_t h0 = h2pair(ds0), h1 = h2pair(ds1);
+    const uint32_t l0 = h2pair(ds0 - __half2float(__ushort_as_half((unsigned short)(h0 & 0xFFFFu))));
+    const uint32_t l1 = h2pair(ds1 - __half2float(__ushort_as_half((unsigned short)(h1 & 0xFFFFu))));
     const uint32_t ns = (c >> 1) * 4u, hs = 2u * c;
+    const uint32_t n1056 = 0xE420E420u;                                            // -1056, -1056
 #pragma unroll
-    for (int sl = 0; sl < 4; sl++) {
-        float w[8];
-        const float ds = sl < 2 ? ds0 : ds1;
+    for (int i = 0; i < 8; i++) {
+        const uint32_t dh = i < 4 ? h0 : h1, dl = i < 4 ? l0 : l1;
+        const uint32_t q6 = ((ql[i] >> ns) & 0x0F0F0F0Fu) | (((qh[i] >> hs) & 0x03030303u) << 4);
 #pragma unroll
-        for (int e = 0; e < 2; e++) {
-            const uint32_t i = 2 * sl + e;
-            const uint32_t q6 = ((ql[i] >> ns) & 0x0F0F0F0Fu) | (((qh[i] >> hs) & 0x03030303u) << 4);
-#pragma unroll
-            for (int b = 0; b < 4; b++) w[4 * e + b] = __fmul_rn(ds, magic_byte(q6, 0x7440u | (uint32_t)b) - 8388640.0f);
+        for (int k = 0; k < 2; k++) {
+            const uint32_t t = hadd2u(h1024(q6, k ? 0x4342u : 0x4140u), n1056);
+            const uint32_t hi = hmul2u(t, dh);
+            h[2 * i + k] = hi;
+            l[2 * i + k] = hfma2u(t, dl, hfma2u(t, dh, hi ^ kHNeg));
         }
-        st8(h + 4 * sl, l + 4 * sl, w);
     }
     return fmaxf(fabsf(ds0), fabsf(ds1)) * 32.0f <= 65504.0f;
 }
 
-// Q8_0 (gguf.c:489-503): run j = block j of the unit, weight q * d (the int8
-// made unsigned by flipping its sign bit, then offset back).
+// Q8_0 (gguf.c:489-503), TG_PLAIN: run j = block j of the unit, weight q * d:
+// q from (1024 + (q ^ 0x80)) - 1152, then hi = q * d rounded and lo = the
+// remainder, the same fp16 pair as rounding the exact f32 weight.
 __device__ __forceinline__ bool dq_q80(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
     const uint8_t* b = p + 34 * j;
-    const float d = f16_bits(lds_u16(b));
+    const uint32_t dh = lds_u16(b);
+    const uint32_t d2 = dh | (dh << 16);
     uint32_t q[8];
     sm_words<8>(b + 2, q);
+    const uint32_t n1152 = 0xE480E480u;                                            // -1152, -1152
 #pragma unroll
-    for (int sl = 0; sl < 4; sl++) {
-        float w[8];
-#pragma unroll
-        for (int e = 0; e < 2; e++) {
-            const uint32_t u = q[2 * sl + e] ^ 0x80808080u;
-#pragma unroll
-            for (int k = 0; k < 4; k++) w[4 * e + k] = __fmul_rn(magic_byte(u, 0x7440u | (uint32_t)k) - 8388736.0f, d);
-        }
-        st8(h + 4 * sl, l + 4 * sl, w);
+    for (int i = 0; i < 8; i++) {
+        const uint32_t u = q[i] ^ 0x80808080u;
+        hilo(hadd2u(h1024(u, 0x4140u), n1152), d2, h[2 * i], l[2 * i]);
+        hilo(hadd2u(h1024(u, 0x4342u), n1152), d2, h[2 * i + 1], l[2 * i + 1]);
     }
-    return fabsf(d) * 128.0f <= 65504.0f;
+    return fabsf(f16_bits(dh)) * 128.0f <= 65504.0f;
 }
 
-// Q4_0 (gguf.c:427-444): run j = block j; element l < 16 is the low nibble of
-// qs[l], element l + 16 its high nibble; weight (q - 8) * d.
+// Q4_0 (gguf.c:427-444), TG_PLAIN: run j = block j; element l < 16 is the low
+// nibble of qs[l], element l + 16 its high nibble; weight (q - 8) * d as hi + lo.
 __device__ __forceinline__ bool dq_q40(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
     const uint8_t* b = p + 18 * j;
-    const float d = f16_bits(lds_u16(b));
+    const uint32_t dh = lds_u16(b);
+    const uint32_t d2 = dh | (dh << 16);
     uint32_t q[4];
     sm_words<4>(b + 2, q);
+    const uint32_t n1032 = 0xE408E408u;                                            // -1032, -1032
 #pragma unroll
-    for (int sl = 0; sl < 4; sl++) {
-        float w[8];
-        const uint32_t sh = sl < 2 ? 0u : 4u;                // elements 16.. are the high nibbles
-#pragma unroll
-        for (int e = 0; e < 2; e++) {
-            const uint32_t n = (q[(2 * sl + e) & 3] >> sh) & 0x0F0F0F0Fu;
-#pragma unroll
-            for (int k = 0; k < 4; k++) w[4 * e + k] = __fmul_rn(magic_byte(n, 0x7440u | (uint32_t)k) - 8388616.0f, d);
-        }
-        st8(h + 4 * sl, l + 4 * sl, w);
+    for (int i = 0; i < 8; i++) {
+        const uint32_t n = (q[i & 3] >> (i < 4 ? 0u : 4u)) & 0x0F0F0F0Fu;       // elements 16.. are the high nibbles
+        hilo(hadd2u(h1024(n, 0x4140u), n1032), d2, h[2 * i], l[2 * i]);
+        hilo(hadd2u(h1024(n, 0x4342u), n1032), d2, h[2 * i + 1], l[2 * i + 1]);
     }
-    return fabsf(d) * 8.0f <= 65504.0f;
+    return fabsf(f16_bits(dh)) * 8.0f <= 65504.0f;
 }
 
-// Q4_1 (gguf.c:445-462): run j = block j; element l < 16 is the low nibble of
-// qs[l], element l + 16 its high nibble; weight q * d + m (q * d is exact, so a
-// fused multiply-add rounds as the reference's multiply-then-add).
+// Q4_1 (gguf.c:445-462), TG_PLAIN: run j = block j; element l < 16 is the low
+// nibble of qs[l], element l + 16 its high nibble; weight q * d + m (q * d is
+// exact, so a fused multiply-add rounds as the reference's multiply-then-add),
+// split into hi + lo.
 __device__ __forceinline__ bool dq_q41(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
     const uint8_t* b = p + 20 * j;
     const uint32_t dm = lds_u32(b);
@@ -383,72 +506,27 @@ __device__ __forceinline__ bool dq_q41(const uint8_t* p, uint32_t j, uint32_t* h
     return fabsf(d) * 15.0f + fabsf(m) <= 65504.0f;
 }
 
-// Q5_0 (gguf.c:463-488): run j = block j; element l < 16 takes the low nibble
-// of qs[l] and bit l of qh, element l + 16 the high nibble and bit l + 16;
-// weight (q - 16) * d, exact.
+// Q5_0 (gguf.c:463-488), TG_PLAIN: run j = block j; element l < 16 takes the
+// low nibble of qs[l] and bit l of qh, element l + 16 the high nibble and bit
+// l + 16; weight (q - 16) * d as hi + lo.
 __device__ __forceinline__ bool dq_q50(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
     const uint8_t* b = p + 22 * j;
-    const float d = f16_bits(lds_u16(b));
+    const uint32_t dh = lds_u16(b);
+    const uint32_t d2 = dh | (dh << 16);
     const uint32_t qh = lds_u32(b + 2);
     uint32_t q[4];
     sm_words<4>(b + 6, q);
+    const uint32_t n1040 = 0xE410E410u;                                            // -1040, -1040
 #pragma unroll
-    for (int sl = 0; sl < 4; sl++) {
-        float w[8];
-        const uint32_t sh = sl < 2 ? 0u : 4u;
-#pragma unroll
-        for (int e = 0; e < 2; e++) {
-            const uint32_t i0 = 4 * ((2 * sl + e) & 3);                  // first qs byte of these 4
-            const uint32_t n = (q[(2 * sl + e) & 3] >> sh) & 0x0F0F0F0Fu;
-            const uint32_t hb = qh >> (i0 + (sl < 2 ? 0u : 16u));       // bits of elements i0 .. i0+3
-            const uint32_t hi = ((hb & 1u) | ((hb & 2u) << 7) | ((hb & 4u) << 14) | ((hb & 8u) << 21)) << 4;
-            const uint32_t q5 = n | hi;
-#pragma unroll
-            for (int k = 0; k < 4; k++) w[4 * e + k] = __fmul_rn(magic_byte(q5, 0x7440u | (uint32_t)k) - 8388624.0f, d);
-        }
-        st8(h + 4 * sl, l + 4 * sl, w);
+    for (int i = 0; i < 8; i++) {
+        const uint32_t i0 = 4 * (i & 3);                                          // first qs byte of these 4
+        const uint32_t n = (q[i & 3] >> (i < 4 ? 0u : 4u)) & 0x0F0F0F0Fu;
+        const uint32_t hb = qh >> (i0 + (i < 4 ? 0u : 16u));                      // bits of elements i0 .. i0+3
+        const uint32_t q5 = n | (((hb & 1u) | ((hb & 2u) << 7) | ((hb & 4u) << 14) | ((hb & 8u) << 21)) << 4);
+        hilo(hadd2u(h1024(q5, 0x4140u), n1040), d2, h[2 * i], l[2 * i]);
+        hilo(hadd2u(h1024(q5, 0x4342u), n1040), d2, h[2 * i + 1], l[2 * i + 1]);
     }
-    return fabsf(d) * 16.0f <= 65504.0f;
-}
-
-// Q5_K (gguf.c:530-560): Q4_K plus a high-bit plane: run j = sub-block j, the
-// quants are nibble j % 2 of qs[32 (j/2) + l] with bit j of qh[l] as bit 4;
-// weight d*sc_j*q - dmin*m_j (the product exact, one fused multiply-add).
-__device__ __forceinline__ bool dq_q5k(const uint8_t* p, uint32_t j, uint32_t* h, uint32_t* l) {
-    const uint4 hd = *reinterpret_cast<const uint4*>(p);
-    const uint32_t sh8 = 8u * (j & 3u);
-    uint32_t sc, mn;
-    if (j < 4) {
-        sc = (hd.y >> sh8) & 63u;
-        mn = (hd.z >> sh8) & 63u;
-    } else {
-        sc = ((hd.w >> sh8) & 15u) | (((hd.y >> (sh8 + 6)) & 3u) << 4);
-        mn = ((hd.w >> (sh8 + 4)) & 15u) | (((hd.z >> (sh8 + 6)) & 3u) << 4);
-    }
-    const float d1 = __fmul_rn(f16_bits(hd.x & 0xFFFFu), u2f(sc));
-    const float m1 = __fmul_rn(f16_bits(hd.x >> 16), u2f(mn));
-    const uint8_t* qp = p + 48 + 32 * (j >> 1);
-    const uint8_t* hp = p + 16;
-    const uint32_t sh = (j & 1u) * 4u;
-#pragma unroll
-    for (int half = 0; half < 2; half++) {
-        const uint4 q = *reinterpret_cast<const uint4*>(qp + 16 * half);
-        const uint4 hq = *reinterpret_cast<const uint4*>(hp + 16 * half);
-        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-        const uint32_t hw[4] = {hq.x, hq.y, hq.z, hq.w};
-#pragma unroll
-        for (int sl = 0; sl < 2; sl++) {
-            float w[8];
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const uint32_t n = ((qw[2 * sl + e] >> sh) & 0x0F0F0F0Fu) | (((hw[2 * sl + e] >> j) & 0x01010101u) << 4);
-#pragma unroll
-                for (int b = 0; b < 4; b++) w[4 * e + b] = __fmaf_rn(d1, magic_byte(n, 0x7440u | (uint32_t)b) - 8388608.0f, -m1);
-            }
-            st8(h + 4 * (2 * half + sl), l + 4 * (2 * half + sl), w);
-        }
-    }
-    return fabsf(d1) * 31.0f + fabsf(m1) <= 65504.0f;
+    return fabsf(f16_bits(dh)) * 16.0f <= 65504.0f;
 }
 
 // F16 rows: the weights are their own hi halves; lo is zero.
@@ -474,7 +552,10 @@ __device__ __forceinline__ bool dq_f16(const uint8_t* p, uint32_t j, uint32_t* h
 // slab sequence, so the shared-memory rings (raw units, A/x stages) and the
 // two tensor-memory accumulators run across tile boundaries without a pause.
 
-__host__ __device__ __forceinline__ uint32_t tg_stage_bytes(uint32_t np) { return 2 * (128 * np); }   // x hi + lo
+// One x stage: x hi + lo of a slab, then (kmin) the super-block's sums.
+__host__ __device__ __forceinline__ uint32_t tg_stage_bytes(uint32_t np, uint32_t kmin) {
+    return 2 * (128 * np) + (kmin ? 32 * np : 0u);
+}
 
 struct TTile {
     uint32_t seg, row0, ks, sl0, sl1;   // segment, first row, K split, slabs [sl0, sl1)
@@ -498,8 +579,11 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
 
     uint8_t* const sbase = smem + ((kTAlign - (smem_u32(smem) & (kTAlign - 1))) & (kTAlign - 1));
-    uint8_t* const xbase = sbase;                                     // NS x (x hi, x lo)
-    uint8_t* const rbase = xbase + NS * 2 * (128 * NP);               // kTRaw raw buffers
+    const uint32_t xsb = tg_stage_bytes(NP, a.kmin);
+    uint8_t* const xbase = sbase;                                     // NS x (x hi, x lo[, sums])
+    uint8_t* const rbase = xbase + NS * xsb;                          // kTRaw raw buffers
+    // TG_KMIN: per A stage the two K = 16 A tiles of the min MMAs (kTMinBytes)
+    uint8_t* const mbase = rbase + kTRaw * a.raw_bytes + kTSlack;
 
     if (tid == 0) {
         for (uint32_t i = 0; i < kTRaw; i++) {
@@ -514,7 +598,7 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
             mbar_init(&S.afull[i], kTGroupWarps);
             mbar_init(&S.aempty[i], kTIssuers);
         }
-        for (uint32_t i = 0; i < 2; i++) { mbar_init(&S.accf[i], kTIssuers); mbar_init(&S.acce[i], kTEpiWarps); }
+        for (uint32_t i = 0; i < kTSets; i++) { mbar_init(&S.accf[i], kTIssuers); mbar_init(&S.acce[i], kTEpiWarps); }
         mbar_init(&S.mdone, kTIssuers);
         S.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -573,18 +657,22 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
         // ------------------------------------------------ staged inputs
         if (lane == 0) {
             const uint32_t xb = 128 * NP;                               // bytes of one half-slab
+            const uint16_t* xsum = a.xh + (uint64_t)a.K * NP;           // the 32-element sums (K-quant min terms)
             uint32_t i = 0;                                             // slabs issued
             bool ok = true;
             for (uint32_t t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
                 const TTile T = tg_tile(a, t);
+                const bool sums = a.seg[T.seg].mode == TG_KMIN;
                 for (uint32_t s = T.sl0; s < T.sl1; s++) {
                     const uint32_t si = i % NS, ph = i / NS;
                     if (ph > 0 && !tg_wait(S, &S.xempty[si], (ph - 1) & 1u, a.err)) { ok = false; break; }
                     const uint64_t off = (uint64_t)s * (kTSlab * NP);   // halves
-                    uint8_t* dst = xbase + si * 2 * xb;
-                    mbar_expect_tx(&S.xfull[si], 2 * xb);
+                    uint8_t* dst = xbase + si * xsb;
+                    const bool sb = sums && s % (256 / kTSlab) == 0;     // first slab of a super-block
+                    mbar_expect_tx(&S.xfull[si], 2 * xb + (sb ? 32 * NP : 0u));
                     bulk_g2s(dst, a.xh + off, xb, &S.xfull[si]);
                     bulk_g2s(dst + xb, a.xl + off, xb, &S.xfull[si]);
+                    if (sb) bulk_g2s(dst + 2 * xb, xsum + (uint64_t)(s / (256 / kTSlab)) * 16 * NP, 32 * NP, &S.xfull[si]);
                     i++;
                 }
             }
@@ -593,8 +681,9 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
         __syncwarp();
     } else if (warp >= kTWarpMma && warp < kTWarpMma + kTIssuers) {
         // ------------------------------------------------ tensor-core issue: chain ch accumulates
-        // w_hi x_hi (0), w_hi x_lo (1) or w_lo x_hi (2); MMAs from several threads
-        // overlap in the tensor pipe where one thread's would wait on each other
+        // A_hi x_hi (0), A_hi x_lo (1) or A_lo x_hi (2) -- chain 2 also the min
+        // terms of TG_KMIN tiles; MMAs from several threads overlap in the
+        // tensor pipe where one thread's would wait on each other
         const uint32_t ch = warp - kTWarpMma;
         if (lane == 0) {
             const uint32_t idesc = umma_idesc_f16(kTRows, NP);
@@ -602,8 +691,10 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
             bool ok = true;
             for (uint32_t t = blockIdx.x; ok && t < ntiles; t += gridDim.x, tl++) {
                 const TTile T = tg_tile(a, t);
-                const bool work = ch != 2 || a.seg[T.seg].type != T_F16;   // F16 weights are exact in hi
-                const uint32_t ab = tl & 1u, aph = tl >> 1;
+                const TSeg& G = a.seg[T.seg];
+                const bool work = ch != 2 || G.type != T_F16;           // F16 weights are exact in hi
+                const bool kmin = ch == 2 && G.mode == TG_KMIN;
+                const uint32_t ab = tl % kTSets, aph = tl / kTSets;
                 if (aph > 0 && !tg_wait(S, &S.acce[ab], (aph - 1) & 1u, a.err)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + ab * kTSetCols + ch * kTAccW;      // this chain's accumulator
@@ -614,13 +705,23 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t at = tmem + kTACol0 + ai * kTACols + (ch == 2 ? kTACols / 2 : 0u);   // A hi or lo
-                    const uint32_t xt = smem_u32(xbase + si * 2 * (128 * NP)) + (ch == 1 ? 128 * NP : 0u);  // x hi or lo
+                    const uint32_t xs = smem_u32(xbase + si * xsb);
                     if (work) {
+                        const uint32_t at = tmem + kTACol0 + ai * kTACols + (ch == 2 ? kTACols / 2 : 0u);   // A hi or lo
+                        const uint32_t xt = xs + (ch == 1 ? 128 * NP : 0u);                            // x hi or lo
 #pragma unroll
                         for (uint32_t kk = 0; kk < kTSlab / 16; kk++)
                             umma_f16_ts(d, at + 8 * kk, umma_desc(xt + kk * 32 * NP, 16 * NP, 128), idesc,
                                         (s != T.sl0 || kk != 0) ? 1u : 0u);
+                    }
+                    if (kmin && s % (256 / kTSlab) == 0) {
+                        // first slab of a super-block: sum_j -32 dmin m_j (S_hi_j + S_lo_j)
+                        // with A = [m_hi, m_hi] then [m_lo, 0] from shared memory and
+                        // B = the staged sums [S_hi, S_lo] after x hi and lo
+                        const uint32_t mb = smem_u32(mbase + ai * kTMinBytes);
+                        const uint64_t bd = umma_desc(xs + 256 * NP, 16 * NP, 128);
+                        umma_f16(d, umma_desc(mb, 16 * kTRows, 128), bd, idesc, 1u);
+                        umma_f16(d, umma_desc(mb + kTMinBytes / 2, 16 * kTRows, 128), bd, idesc, 1u);
                     }
                     umma_commit(&S.aempty[ai]);
                     umma_commit(&S.xempty[si]);
@@ -639,26 +740,37 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
         for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x, tl++) {
             const TTile T = tg_tile(a, t);
             const TSeg& G = a.seg[T.seg];
-            const uint32_t ab = tl & 1u;
-            if (!tg_wait_warp(S, &S.accf[ab], (tl >> 1) & 1u, a.err)) break;
+            const uint32_t ab = tl % kTSets;
+            if (!tg_wait_warp(S, &S.accf[ab], (tl / kTSets) & 1u, a.err)) break;
             tc_fence_after();
             const uint32_t row = T.row0 + 32 * q + lane;
             const bool lo = G.type != T_F16;
             float* part = G.part + (uint64_t)T.ks * a.B * G.rows;
             const uint32_t tb = tmem + ((32u * q) << 16) + ab * kTSetCols;
             for (uint32_t cc = 0; 16 * cc < NP; cc++) {
-                uint32_t vh[16], vx[16], vl[16];
-                tmem_ld16(tb + 16 * cc, vh);
-                tmem_ld16(tb + kTAccW + 16 * cc, vx);
-                if (lo) tmem_ld16(tb + 2 * kTAccW + 16 * cc, vl);
-                if (row < G.rows) {
+                // one load in flight at a time keeps the live registers to 32
+                uint32_t u[16];
+                float v[16];
+                tmem_ld16(tb + 16 * cc, u);
+                tmem_wait_ld(u);
 #pragma unroll
-                    for (int e = 0; e < 16; e++) {
-                        const uint32_t b = 16 * cc + e;
-                        float v = __uint_as_float(vh[e]) + __uint_as_float(vx[e]);
-                        if (lo) v += __uint_as_float(vl[e]);
-                        if (b < a.B) part[(uint64_t)b * G.rows + row] = v * 5.9604644775390625e-08f;
-                    }
+                for (int e = 0; e < 16; e++) v[e] = __uint_as_float(u[e]);
+                tmem_ld16(tb + kTAccW + 16 * cc, u);
+                tmem_wait_ld(u);
+#pragma unroll
+                for (int e = 0; e < 16; e++) v[e] += __uint_as_float(u[e]);
+                if (lo) {
+                    tmem_ld16(tb + 2 * kTAccW + 16 * cc, u);
+                    tmem_wait_ld(u);
+#pragma unroll
+                    for (int e = 0; e < 16; e++) v[e] += __uint_as_float(u[e]);
+                }
+                if (row < G.rows) {
+                    float* dst = part + (uint64_t)(16 * cc) * G.rows + row;
+                    const uint32_t nb = min(16u, a.B - min(a.B, 16 * cc));   // sequences of this chunk
+#pragma unroll
+                    for (int e = 0; e < 16; e++)
+                        if ((uint32_t)e < nb) dst[(uint64_t)e * G.rows] = v[e] * 5.9604644775390625e-08f;
                 }
             }
             tc_fence_before();
@@ -667,7 +779,7 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
         }
     } else {
         // ------------------------------------------------ dequant
-        const uint32_t grp = warp / kTGroupWarps;                      // decodes the slabs i with i % 2 == grp
+        const uint32_t grp = warp / kTGroupWarps;                      // decodes the slabs i with i % kTGroups == grp
         const uint32_t r = tid & (kTRows - 1), c = (tid >> 7) & 1u;    // row, 32-element run of the slab
         uint32_t i = 0, lr = 0;                                         // slabs, raw units consumed
         bool ok = true, inrange = true;
@@ -683,7 +795,7 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
                     cur = lr++;
                     if (!tg_wait_warp(S, &S.raw_full[cur % kTRaw], (cur / kTRaw) & 1u, a.err)) { ok = false; break; }
                 }
-                const bool mine = (i & 1u) == grp;
+                const bool mine = i % kTGroups == grp;
                 if (!mine) {
                     if ((s + 1) % spr == 0) {
                         __syncwarp();
@@ -691,25 +803,29 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
                     }
                     continue;
                 }
-                uint32_t h[16], l[16];
+                uint32_t h[16], l[16], mh[4], ml[4];
+                const bool mins = G.mode == TG_KMIN && c == 0 && s % spr == 0;   // this warp writes the mins
                 if (!valid) {
 #pragma unroll
                     for (int e = 0; e < 16; e++) h[e] = l[e] = 0;
+#pragma unroll
+                    for (int e = 0; e < 4; e++) mh[e] = ml[e] = 0;
                 } else {
                     const uint64_t o = (uint64_t)(T.row0 + r) * G.pitch + (uint64_t)(s / spr) * G.ub;
                     const uint8_t* p = rbase + (cur % kTRaw) * a.raw_bytes + r * G.rrs + (uint32_t)(o & 15u);
                     const uint32_t j = (s % spr) * 2 + c;              // run within the raw unit
                     bool fine;
                     switch (G.type) {
-                    case T_Q4_K: fine = dq_q4k(p, j, h, l); break;
-                    case T_Q6_K: fine = dq_q6k(p, j, h, l); break;
+                    case T_Q4_K: fine = dqf_q4k(p, j, h, l); break;
+                    case T_Q5_K: fine = dqf_q5k(p, j, h, l); break;
+                    case T_Q6_K: fine = dqf_q6k(p, j, h, l); break;
                     case T_Q8_0: fine = dq_q80(p, j, h, l); break;
                     case T_Q4_0: fine = dq_q40(p, j, h, l); break;
                     case T_Q4_1: fine = dq_q41(p, j, h, l); break;
                     case T_Q5_0: fine = dq_q50(p, j, h, l); break;
-                    case T_Q5_K: fine = dq_q5k(p, j, h, l); break;
                     default: fine = dq_f16(p, j, h, l); break;
                     }
+                    if (mins) fine = k4_mins(p, mh, ml) && fine;
                     inrange = inrange && fine;
                 }
                 // the A stage is free once the MMAs of slab i - kTNA have read it
@@ -720,6 +836,17 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
                 const uint32_t ta = tmem + ((32u * (warp & 3u)) << 16) + kTACol0 + ai * kTACols + 16 * c;
                 tmem_st16(ta, h);
                 tmem_st16(ta + kTACols / 2, l);
+                if (mins) {
+                    // row r of the min MMAs' A tiles (K-major core matrices: K
+                    // elements 8g .. 8g + 7 of row r at 2048 g + 16 r): [m_hi, m_hi], [m_lo, 0]
+                    uint8_t* mb = mbase + ai * kTMinBytes + 16 * r;
+                    const uint4 vh4 = make_uint4(mh[0], mh[1], mh[2], mh[3]);
+                    *reinterpret_cast<uint4*>(mb) = vh4;
+                    *reinterpret_cast<uint4*>(mb + 16 * kTRows) = vh4;
+                    *reinterpret_cast<uint4*>(mb + kTMinBytes / 2) = make_uint4(ml[0], ml[1], ml[2], ml[3]);
+                    *reinterpret_cast<uint4*>(mb + kTMinBytes / 2 + 16 * kTRows) = make_uint4(0u, 0u, 0u, 0u);
+                    fence_async_smem();                                // visible to the tensor core's reads
+                }
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
@@ -795,8 +922,12 @@ static bool tg_encode(CUtensorMap* m, const TSeg& S) {
 // At least kTSmemMin: two CTAs never share an SM (each allocates 512
 // tensor-memory columns; a second one would wait for the first to finish).
 constexpr size_t kTSmemMin = 120 * 1024;
+static size_t tg_smem_for(const TGemmArgs& a, uint32_t stages) {
+    return kTAlign + (size_t)stages * tg_stage_bytes(a.NP, a.kmin) + (size_t)kTRaw * a.raw_bytes + kTSlack +
+           (a.kmin ? (size_t)kTNA * kTMinBytes : 0);
+}
 size_t tgemm_smem(const TGemmArgs& a) {
-    const size_t n = kTAlign + (size_t)a.stages * tg_stage_bytes(a.NP) + (size_t)kTRaw * a.raw_bytes + kTSlack;
+    const size_t n = tg_smem_for(a, a.stages);
     return n > kTSmemMin ? n : kTSmemMin;
 }
 
@@ -809,6 +940,7 @@ bool tgemm_init() {
 bool tgemm_plan(TGemmArgs& a, uint32_t sms) {
     if (a.B == 0 || a.B > 64 || a.nseg == 0 || a.nseg > 3 || a.K % kTSlab != 0 || sms == 0) return false;
     a.NP = (a.B + 15) & ~15u;
+    a.kmin = 0;
     bool kq = false;
     uint32_t rbs = 0, raw = 0;
     a.tma = 1;
@@ -820,6 +952,8 @@ bool tgemm_plan(TGemmArgs& a, uint32_t sms) {
         if (S.pitch == 0) S.pitch = S.row_bytes;
         if (S.pitch < S.row_bytes) return false;
         kq = kq || S.type == T_Q4_K || S.type == T_Q5_K || S.type == T_Q6_K;
+        S.mode = S.type == T_Q4_K || S.type == T_Q5_K ? TG_KMIN : TG_PLAIN;
+        a.kmin = a.kmin || S.mode == TG_KMIN;
         S.ru = tg_ru(S.type, a.K);
         S.ub = tg_ub(S.type, S.ru);
         if (S.pitch % 16 != 0) a.tma = 0;                 // TMA needs 16-byte row strides
@@ -830,8 +964,13 @@ bool tgemm_plan(TGemmArgs& a, uint32_t sms) {
         TSeg& S = a.seg[i];
         if (a.tma) {
             // the box starts at the 16-byte boundary at or below each unit (the
-            // byte offset of a unit is even: at most 14 bytes of lead-in)
-            S.rrs = S.ub % 16 == 0 ? S.ub : (S.ub + 14 + 15) & ~15u;
+            // byte offset of a unit is even: at most 14 bytes of lead-in); an odd
+            // count of 16-byte units per row spreads the decoders' loads of 32
+            // rows over all shared-memory banks (the box then reads a few bytes
+            // of the next unit, or zeros past the row's end)
+            uint32_t rrs = S.ub % 16 == 0 ? S.ub : (S.ub + 14 + 15) & ~15u;
+            if ((rrs / 16) % 2 == 0) rrs += 16;
+            S.rrs = rrs;
         } else {
             uint32_t rrs = (S.ub + 15 + 4 + 15) & ~15u;    // alignment delta + one word of over-read
             if ((rrs / 16) % 2 == 0) rrs += 16;            // odd count of 16-byte units: rows over all banks
@@ -855,7 +994,7 @@ bool tgemm_plan(TGemmArgs& a, uint32_t sms) {
     a.raw_bytes = raw;
     a.stages = 0;
     for (uint32_t ns = kTMaxStages; ns >= 2; ns--)
-        if (kTAlign + (size_t)ns * tg_stage_bytes(a.NP) + (size_t)kTRaw * raw + kTSlack <= kTSmemMax) { a.stages = ns; break; }
+        if (tg_smem_for(a, ns) <= kTSmemMax) { a.stages = ns; break; }
     if (a.stages == 0) return false;
     a.tcols = kTCols;                                    // accumulators + A stages
     // K split: the fewest units per CTA among the splits whose waves x units

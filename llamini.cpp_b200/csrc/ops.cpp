@@ -57,7 +57,7 @@ bool gemv_batch_tc(uint32_t type, const uint8_t* w, uint32_t rows, uint32_t cols
     g.seg[0].rows = rows;
     if (g.seg[0].row_bytes == 0 || !lm::tgemm_plan(g, (uint32_t)lm::sm_count())) return true;
     *handled = true;
-    uint16_t* xh = (uint16_t*)g_s[6].get((size_t)g.NP * cols * 2);
+    uint16_t* xh = (uint16_t*)g_s[6].get(lm::tg_xh_halves(cols, g.NP) * 2);
     uint16_t* xl = (uint16_t*)g_s[7].get((size_t)g.NP * cols * 2);
     float* osc = fbuf(8, batch);
     float* part = fbuf(9, (size_t)g.ksplit * batch * rows);

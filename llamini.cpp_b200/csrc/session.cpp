@@ -1471,7 +1471,7 @@ bool batch_alloc(llamini_batch* b) {
     b->ffn_h = (float*)own(s, (size_t)MB * s->ffn * 4);
     b->logits = (float*)own(s, (size_t)MB * s->vocab * 4);
     const size_t xcols = ((size_t)MB + 15) & ~size_t(15);         // the tensor-core layout pads the batch to 16
-    b->xh = (uint16_t*)own(s, xcols * b->kmax * 2);
+    b->xh = (uint16_t*)own(s, tg_xh_halves(b->kmax, xcols) * 2);
     b->xl = (uint16_t*)own(s, xcols * b->kmax * 2);
     b->sx = (float*)own(s, ((size_t)MB * (b->kmax / 16) + MB) * 4);
     b->part = (float*)own(s, pmax * 4);
@@ -1582,7 +1582,7 @@ bool prefill_build(llamini_session* s) {
     pf->attn = (float*)own(s, (size_t)C * s->qd * 4);
     pf->ffn_h = (float*)own(s, (size_t)C * s->ffn * 4);
     pf->osc = (float*)own(s, (size_t)C * 4);
-    pf->xh = (uint16_t*)own(s, (size_t)C * kmax * 2);
+    pf->xh = (uint16_t*)own(s, tg_xh_halves(kmax, C) * 2);
     pf->xl = (uint16_t*)own(s, (size_t)C * kmax * 2);
     pf->part = (float*)own(s, pmax * 4);
     pf->part2 = (float*)own(s, pmax * 4);
