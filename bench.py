@@ -305,6 +305,34 @@ def run_tp7b(args, lm, L, torch, ws, rank, dist, hbm_peak):
     return ms, wb, kvp, pos0
 
 
+def run_perplexity(lm, L, model, n_tok=1024):
+    """compute_perplexity over n_tok seeded tokens (teacher forcing, generate.c:169-197):
+    the chunked path (64 positions per tcgen05 GEMM pass, lm_head for every
+    position, log-softmax on the device) against the one-position-at-a-time
+    path, wall clock around the public call (tokens from host memory, the
+    perplexity back)."""
+    # the model's greedy continuation of one seeded id: seeded random ids give
+    # this random-weight model a loss beyond expf's range on every path
+    toks = np.asarray(model.generate(synthetic().workload_prompt(WORKLOAD, 1), n_tok - 1), np.uint32)[:n_tok]
+    out = {}
+    for name, flag in (("chunked", 1), ("steps", 0)):
+        assert L.llamini_set_prefill(flag) == 0
+        try:
+            model.perplexity(toks[:80])                              # warm: buffers, graphs
+            t = time.perf_counter()
+            p = model.perplexity(toks)
+            out[name] = (time.perf_counter() - t, p)
+        finally:
+            L.llamini_set_prefill(-1)
+        assert p > 0, lm.last_error()
+    (tc, pc), (ts, ps) = out["chunked"], out["steps"]
+    return {"value": round((n_tok - 1) / tc, 1), "unit": "tok/s", "positions": n_tok - 1,
+            "ms": round(tc * 1e3, 3), "ppl": round(pc, 6),
+            "path": "tcgen05 GEMM, 64 positions per chunk, lm_head + log-softmax on the device",
+            "steps_path": {"value": round((n_tok - 1) / ts, 1), "unit": "tok/s", "ppl": round(ps, 6)},
+            "note": "compute_perplexity wall clock over the model's %d-token greedy continuation of a seeded id" % n_tok}
+
+
 def run_ours(args, ws, rank, local):
     import torch
     dist = init_dist(ws, local, "nccl")
@@ -363,6 +391,7 @@ def run_ours(args, ws, rank, local):
         if rank == 0 and not args.no_kernel_roofline:
             gemv_roof = kernel_roofline(lm, torch, stream, hbm_peak, peak_kind)
         bt = None if args.no_batch else run_batch(args, lm, L, model, torch, stream, ws, rank, dist, hbm_peak)
+    ppl = None if (rank != 0 or args.no_ppl) else run_perplexity(lm, L, model)
     model.close()
     tp7 = None if args.no_tp7b else run_tp7b(args, lm, L, torch, ws, rank, dist, hbm_peak)
     t_max, e2e_max = max_over_ranks(dist, [ms, e2e_s])
@@ -400,6 +429,7 @@ def run_ours(args, ws, rank, local):
                         "positions": n_prompt - 1, "ms": round(prefill_ms, 3),
                         "path": "tcgen05 GEMM, 64 positions per chunk" if prefill_path == 1 else "decode steps",
                         "note": "the prompt before the timed decode (device time, second pass)"},
+            "perplexity": ppl,
             "gpu_launches": (1 + (steps + 63) // 64) if decode_kernel else steps * (1 + 5 * 22 + 2),
             "step_kernel": "decode_kernel (persistent, whole step)" if decode_kernel else "per-op graph",
             "clocks": clk.summary(),
@@ -529,6 +559,7 @@ def main():
     ap.add_argument("--no-kernel-roofline", action="store_true", help="skip the isolated GEMV timing")
     ap.add_argument("--prompt", type=int, default=N_PROMPT, help="prompt length before the timed steps")
     ap.add_argument("--no-batch", action="store_true", help="skip the batch-64 decode timing")
+    ap.add_argument("--no-ppl", action="store_true", help="skip the perplexity timing")
     ap.add_argument("--batch-steps", type=int, default=32, help="timed steps of the batch-64 leg")
     ap.add_argument("--no-tp7b", action="store_true", help="skip the 7B-shape tensor-parallel decode timing")
     ap.add_argument("--tp-steps", type=int, default=64, help="timed decode steps of the 7B-shape leg")

@@ -388,7 +388,17 @@ struct PAttnArgs {
     uint32_t out_stride;
     uint32_t n_heads, n_kv, hd, max_seq, p0, C;
 };
+// Teacher-forced scoring of a chunk (compute_perplexity, generate.c:169-197):
+// lp[p] = log softmax(logits of position p)[tokens[p + 1]] for p0 <= p <= last.
+struct PNllArgs {
+    const float* logits;           // [C][ld], position p0 + b at row b
+    uint32_t vocab, ld;
+    const uint32_t* tokens;        // device token ids
+    uint32_t p0, C, last;
+    float* lp;
+};
 bool prefill_init();
+bool launch_pnll(const PNllArgs& a, cudaStream_t st);
 bool launch_pembed(const PEmbedArgs& a, cudaStream_t st);
 bool launch_prope(const PRopeArgs& a, uint32_t C, cudaStream_t st);
 bool launch_pattn(const PAttnArgs& a, cudaStream_t st);

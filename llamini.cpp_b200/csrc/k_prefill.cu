@@ -8,9 +8,11 @@
 // rotation and KV-cache writes of all C positions, then causal attention of
 // every position over the cache up to itself -- per position the arithmetic of
 // model.c:217-260 (scores (q . k) / sqrtf(hd), max-subtracted expf, weighted
-// sum of V), evaluated as an online softmax over 64-key tiles. No lm_head: the
-// last prompt position runs through the decode step, which produces the logits
-// and the first generated token.
+// sum of V), evaluated as an online softmax over 64-key tiles. No lm_head for
+// a prompt: its last position runs through the decode step, which produces
+// the logits and the first generated token. Teacher-forced perplexity adds the
+// final norm and lm_head of every chunk position (a tensor-core GEMM) and
+// scores each position's next token (pnll_kernel).
 #include "internal.h"
 #include "rows.cuh"
 #include "attn_core.cuh"
@@ -156,6 +158,47 @@ __global__ void __launch_bounds__(kPThreads) pattn_kernel(const PAttnArgs a) {
             if (d < hd) out[d] = o[k] / l;
         }
     }
+}
+
+// grid C, 1024 threads: position p0 + b's log-probability of the next token,
+// (logit[t] - max) - log(sum exp(logit - max)) as generate.c:182-188 computes
+// it (the sums in a tree order rather than the reference's left-to-right).
+__global__ void __launch_bounds__(1024) pnll_kernel(const PNllArgs a) {
+    __shared__ float red[32];
+    __shared__ float bval;
+    const uint32_t b = blockIdx.x, pos = a.p0 + b;
+    if (pos > a.last) return;                      // the whole block: no next token to score
+    const float* lg = a.logits + (uint64_t)b * a.ld;
+    const uint32_t tid = threadIdx.x, nw = blockDim.x >> 5;
+    float m = -INFINITY;
+    for (uint32_t i = tid; i < a.vocab; i += blockDim.x) m = fmaxf(m, lg[i]);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((tid & 31u) == 0) red[tid >> 5] = m;
+    __syncthreads();
+    if (tid == 0) {
+        float t = red[0];
+        for (uint32_t i = 1; i < nw; i++) t = fmaxf(t, red[i]);
+        bval = t;
+    }
+    __syncthreads();
+    const float mx = bval;
+    float e = 0.f;
+    for (uint32_t i = tid; i < a.vocab; i += blockDim.x) e += expf(lg[i] - mx);
+    for (int o = 16; o > 0; o >>= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
+    __syncthreads();                               // bval read by every thread before red is reused
+    if ((tid & 31u) == 0) red[tid >> 5] = e;
+    __syncthreads();
+    if (tid == 0) {
+        float t = 0.f;
+        for (uint32_t i = 0; i < nw; i++) t += red[i];
+        const uint32_t tgt = a.tokens[pos + 1];
+        a.lp[pos] = (lg[tgt < a.vocab ? tgt : 0] - mx) - logf(t);
+    }
+}
+
+bool launch_pnll(const PNllArgs& a, cudaStream_t st) {
+    pnll_kernel<<<a.C, 1024, 0, st>>>(a);
+    return LM_CUDA(cudaGetLastError());
 }
 
 bool prefill_init() {

@@ -28,6 +28,10 @@
 struct Prefill {
     float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *ffn_h = nullptr, *osc = nullptr;
     float *part = nullptr, *part2 = nullptr, *part3 = nullptr;
+    // teacher-forced scoring (built on first use): lm_head partials, the
+    // chunk's logits [C][vocab], and per position the next token's log-prob
+    float *hpart = nullptr, *logits = nullptr, *lp = nullptr;
+    int head_state = 0;                  // 0 not built, 1 ready, -1 not available
     uint16_t *xh = nullptr, *xl = nullptr;
     uint32_t* err = nullptr;
     std::unordered_map<const uint8_t*, std::pair<const uint8_t*, uint64_t>> pitched;
@@ -785,6 +789,7 @@ namespace {
 // Prompt positions [pos, pos + n) without logits: chunked prefill when the
 // model allows it, else decode steps (defined with the batched code below).
 bool run_prompt(llamini_session* s, u32 n);
+int prefill_perplexity(llamini_session* s, u32 steps, double* nll);
 }  // namespace
 
 // Shared by forward_step and gpt2_forward_step.
@@ -880,6 +885,20 @@ static f32 perplexity(llamini_session* s, const u32* tokens, u32 n) {
     while (steps + 1 < n && steps < s->max_pos) steps++;
     if (steps == 0) return -1.0f;
     cudaStream_t st = stream();
+    if (steps >= 2) {
+        // 64 positions at a time through the tensor-core GEMMs, when available;
+        // the log-probs are summed here in position order, as the reference does
+        double nll = 0.0;
+        if (!write_state(s, 0, n, true)) return -1.0f;
+        const u32 ncopy = n < s->max_seq + 1 ? n : s->max_seq + 1;
+        if (!LM_CUDA(cudaMemcpyAsync(s->tokens, tokens, (size_t)ncopy * 4, cudaMemcpyHostToDevice, st))) return -1.0f;
+        const int r = prefill_perplexity(s, steps, &nll);
+        if (r < 0) return -1.0f;                     // failed: the error is set
+        if (r > 0) {
+            set_cur_seq(s);
+            return expf((f32)(nll / steps));
+        }
+    }
     if (!s->g_nll && !capture(s, 1, false, true, &s->g_nll)) return -1.0f;
     if (!write_state(s, 0, n, true)) return -1.0f;
     const u32 ncopy = n < s->max_seq + 1 ? n : s->max_seq + 1;
@@ -1595,8 +1614,10 @@ bool prefill_build(llamini_session* s) {
     return true;
 }
 
-// Positions p0 .. p0 + C - 1 through every layer (their cache rows written).
-bool prefill_chunk(llamini_session* s, u32 p0, u32 C, cudaStream_t st) {
+// Positions p0 .. p0 + C - 1 through every layer (their cache rows written);
+// with `score`, also the final norm, lm_head and the log-prob of each scored
+// position's next token (positions up to `last`) into pf->lp.
+bool prefill_chunk(llamini_session* s, u32 p0, u32 C, cudaStream_t st, bool score = false, u32 last = 0) {
     Prefill* pf = s->pf;
     const bool gpt2 = s->kind == 1;
     const u32 qkvd = s->qd + 2 * s->kvd, L = s->n_layers;
@@ -1731,7 +1752,74 @@ bool prefill_chunk(llamini_session* s, u32 p0, u32 C, cudaStream_t st) {
                 return false;
         }
     }
+    if (score) {
+        // final norm + lm_head (head_args' matrix) for every position, then the
+        // next token's log-prob (generate.c:176-188, gpt2.c:240-250)
+        TGemmArgs g;
+        const DevMat* mm[1] = {&s->head};
+        float* pp[1] = {pf->hpart};
+        if (!stage(pf->hidden, s->dim, norm, s->fnw, s->fnb) || !gemm(mm, pp, 1, s->dim, &g) ||
+            !launch_bfinish(fin(g, 0, nullptr, EPI_STORE, nullptr, pf->logits, s->vocab), st))
+            return false;
+        PNllArgs n;
+        n.logits = pf->logits;
+        n.vocab = s->vocab;
+        n.ld = s->vocab;
+        n.tokens = s->tokens;
+        n.p0 = p0;
+        n.C = C;
+        n.last = last;
+        n.lp = pf->lp;
+        if (!launch_pnll(n, st)) return false;
+    }
     return true;
+}
+
+// Buffers of teacher-forced scoring (false, no error: the lm_head has no
+// tensor-core plan, e.g. a K-quant head whose width is not a multiple of 256).
+bool prefill_head_build(llamini_session* s) {
+    Prefill* pf = s->pf;
+    if (pf->head_state) return pf->head_state > 0;
+    pf->head_state = -1;
+    const DevMat* mm[1] = {&s->head};
+    float* none[3] = {nullptr, nullptr, nullptr};
+    TGemmArgs g;
+    if (!plan_tc(nullptr, nullptr, kPfChunk, nullptr, pf->pitched, mm, none, 1, s->dim, &g)) return false;
+    pf->hpart = (float*)own(s, (size_t)g.ksplit * kPfChunk * s->vocab * 4);
+    pf->logits = (float*)own(s, (size_t)kPfChunk * s->vocab * 4);
+    pf->lp = (float*)own(s, (size_t)(s->max_pos + 1) * 4);
+    if (!pf->hpart || !pf->logits || !pf->lp) return false;
+    pf->head_state = 1;
+    return true;
+}
+
+// compute_perplexity's positions 0 .. steps - 1 in chunks (tokens on the device,
+// state at position 0); *nll = the sum of -log p(next token) in position order.
+// 1 done, 0 the chunked path is not available (nothing ran), -1 failed (error set).
+int prefill_perplexity(llamini_session* s, u32 steps, double* nll) {
+    if (s->trace_on || !prefill_enabled() || !prefill_build(s) || !prefill_head_build(s)) return 0;
+    cudaStream_t st = stream();
+    for (u32 done = 0; done < steps;) {
+        const u32 C = steps - done < kPfChunk ? steps - done : kPfChunk;
+        if (!prefill_chunk(s, done, C, st, true, steps - 1)) return -1;
+        done += C;
+    }
+    std::vector<float> lp(steps);
+    uint32_t e = 0;
+    if (!LM_CUDA(cudaMemcpyAsync(lp.data(), s->pf->lp, (size_t)steps * 4, cudaMemcpyDeviceToHost, st)) ||
+        !LM_CUDA(cudaMemcpyAsync(&e, s->pf->err, 4, cudaMemcpyDeviceToHost, st)) || !LM_CUDA(cudaStreamSynchronize(st)))
+        return -1;
+    if (e) {
+        set_error("prefill: tensor-core GEMM: %s", (e & 1u) ? "a pipeline wait ran out" : "a weight outside the fp16 range");
+        return -1;
+    }
+    double sum = 0.0;
+    for (u32 i = 0; i < steps; i++) sum += -(double)lp[i];
+    *nll = sum;
+    s->pos = steps;
+    s->st_host->pos = s->pos;
+    return LM_CUDA(cudaMemcpyAsync(&s->st->pos, &s->st_host->pos, 4, cudaMemcpyHostToDevice, st)) &&
+                   LM_CUDA(cudaStreamSynchronize(st)) ? 1 : -1;
 }
 
 bool run_prompt(llamini_session* s, u32 n) {

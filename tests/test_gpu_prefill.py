@@ -79,3 +79,58 @@ def test_prefill_workload_stream(gpu, synth, golden):
         assert gpu.lib().llamini_session_prefill(m.session()) == 1
     finally:
         m.close()
+
+
+@pytest.mark.parametrize("name", ["tiny_llama", "tiny_mixed", "tiny_gpt2", "tiny_tied", "tiny_gemma", "tiny_qwen2"])
+def test_perplexity_chunked(gpu, orc, tiny, name):
+    """compute_perplexity runs its positions 64 at a time (tensor-core GEMMs, the
+    lm_head for every position, the log-softmax on the device) when the lm_head
+    has a tensor-core plan, else one position at a time; both agree with each
+    other and with a teacher-forced evaluation of the oracle's logits."""
+    path = tiny.ensure(name)
+    m = gpu.Model(path)
+    L = gpu.lib()
+    # the model's own greedy continuation of one token as the text: random ids
+    # would give these random-weight models a loss beyond expf's range (an
+    # infinite perplexity on every path)
+    start = np.random.default_rng(41).integers(3, m.vocab, 1).astype(np.uint32)
+    toks = np.asarray(m.generate(start, m.max_seq - 1), np.uint32)[:m.max_seq]
+    try:
+        assert L.llamini_set_prefill(0) == 0
+        off = m.perplexity(toks)
+        assert L.llamini_set_prefill(1) == 0
+        on = m.perplexity(toks)
+        short = m.perplexity(toks[:3])             # two positions: one partial chunk
+    finally:
+        L.llamini_set_prefill(-1)
+    assert on > 0 and off > 0 and np.isfinite(on), (on, off, gpu.last_error())
+    assert abs(on - off) / off < 1e-4, (on, off)
+    o = orc.oracle_model(path, m.max_seq)
+    nll = []
+    for pos in range(len(toks) - 1):
+        lg = o.forward(pos, int(toks[pos])).astype(np.float64)
+        mx = lg.max()
+        nll.append(-((lg[toks[pos + 1]] - mx) - np.log(np.exp(lg - mx).sum())))
+    want = float(np.exp(np.mean(nll)))
+    assert abs(on - want) / want < TOL, (on, want)
+    want2 = float(np.exp(np.mean(nll[:2])))
+    assert abs(short - want2) / want2 < TOL, (short, want2)
+
+
+def test_perplexity_chunked_llama_1b(gpu, synth):
+    """llama_1b, its greedy continuation of one seeded id, 300 positions (five
+    chunks): the chunked path and the one-position-at-a-time path give the
+    same perplexity."""
+    m = gpu.Model(synth.ensure_workload("llama_1b"), max_seq=512)
+    L = gpu.lib()
+    toks = np.asarray(m.generate(synth.workload_prompt("llama_1b", 1), 299), np.uint32)
+    try:
+        assert L.llamini_set_prefill(0) == 0
+        off = m.perplexity(toks)
+        assert L.llamini_set_prefill(1) == 0
+        on = m.perplexity(toks)
+    finally:
+        L.llamini_set_prefill(-1)
+        m.close()
+    assert on > 0 and off > 0 and np.isfinite(on), (on, off, gpu.last_error())
+    assert abs(on - off) / off < 1e-4, (on, off)
