@@ -333,6 +333,32 @@ def run_perplexity(lm, L, model, n_tok=1024):
             "note": "compute_perplexity wall clock over the model's %d-token greedy continuation of a seeded id" % n_tok}
 
 
+def profile_batch():
+    """A profiler's workload: llama_1b batched decode of 64 sequences with 4-token
+    prompts, 3 batch steps after the model upload, each the same launch sequence
+    (embed, staging, 13 per layer, lm_head finish, token update)."""
+    lm = pkg()
+    L = lm.lib()
+    path = synthetic().ensure_workload(WORKLOAD, os.environ.get("LLAMINI_WORKDIR", "/tmp/llamini_b200"))
+    model = lm.Model(path, max_seq=512)
+    try:
+        b = L.llamini_llama_batch(C.byref(model.model), GLOBAL_BATCH, 512)
+        if not b:
+            raise RuntimeError("batch: " + lm.last_error())
+        try:
+            prompts = np.random.default_rng(1000).integers(3, model.vocab, (GLOBAL_BATCH, 4)).astype(np.uint32)
+            lens = np.full(GLOBAL_BATCH, 4, np.uint32)
+            assert L.llamini_batch_begin(b, GLOBAL_BATCH, lm.ptr(prompts), lm.ptr(lens)) == 0, lm.last_error()
+            assert L.llamini_batch_step(b, 3) == 0, lm.last_error()
+            out = np.zeros(4, np.uint32)
+            assert L.llamini_batch_tokens(b, 0, lm.ptr(out), 4) > 0, lm.last_error()
+        finally:
+            L.llamini_batch_free(b)
+    finally:
+        model.close()
+    print(json.dumps({"profile_batch": "ok", "sequences": GLOBAL_BATCH, "steps": 3}))
+
+
 def run_ours(args, ws, rank, local):
     import torch
     dist = init_dist(ws, local, "nccl")
@@ -563,7 +589,13 @@ def main():
     ap.add_argument("--batch-steps", type=int, default=32, help="timed steps of the batch-64 leg")
     ap.add_argument("--no-tp7b", action="store_true", help="skip the 7B-shape tensor-parallel decode timing")
     ap.add_argument("--tp-steps", type=int, default=64, help="timed decode steps of the 7B-shape leg")
+    ap.add_argument("--profile-batch", action="store_true",
+                    help="no bench line: only a short batch-64 run of llama_1b for profilers "
+                         "(4-token prompts, 3 batch steps of identical launch sequences)")
     args = ap.parse_args()
+    if args.profile_batch:
+        profile_batch()
+        return
     if args.warmup < 3:
         args.warmup = 3
     ws, rank, local = dist_env()
