@@ -102,6 +102,8 @@ attn_batch_kernel(const AttnArgs a, const AttnBatch bt) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ int is_last;
     __shared__ float s_ls;
+    pdl_trigger();
+    pdl_wait();                                   // q/k/v come from the q/k/v finish
     const uint32_t b = blockIdx.z;
     AttnArgs s = a;
     s.qkv = a.qkv + (uint64_t)b * bt.qkv_stride;
@@ -141,9 +143,8 @@ bool launch_attention_batch(const AttnArgs& a, const AttnBatch& bt, uint32_t B, 
     }
     const size_t smem = attn_core_bytes(a.hd, a.kv_f16 != 0) + (size_t)a.n_split * 4;
     const dim3 grid(a.n_heads, a.n_split, B);
-    if (a.kv_f16) attn_batch_kernel<__half><<<grid, kAttnThreads, smem, st>>>(a, bt);
-    else attn_batch_kernel<float><<<grid, kAttnThreads, smem, st>>>(a, bt);
-    return LM_CUDA(cudaGetLastError());
+    if (a.kv_f16) return LM_CUDA(launch_k(attn_batch_kernel<__half>, grid, dim3(kAttnThreads), smem, st, a, bt));
+    return LM_CUDA(launch_k(attn_batch_kernel<float>, grid, dim3(kAttnThreads), smem, st, a, bt));
 }
 
 }  // namespace lm

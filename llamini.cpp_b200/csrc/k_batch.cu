@@ -6,12 +6,15 @@
 // greedy token (generate.c:3-9, from the lm_head finish's argmax key) becomes
 // tokens[b][p + 1] once p + 1 is past its prompt (generate.c:143-156).
 #include "internal.h"
+#include "pdl.cuh"
 #include "rows.cuh"
 
 namespace lm {
 
 // grid B, 256 threads
 __global__ void bembed_kernel(const BEmbedArgs a) {
+    pdl_trigger();
+    pdl_wait();                                    // the position and tokens come from the previous step
     const uint32_t b = blockIdx.x;
     const uint32_t pos = a.st->pos;
     uint32_t t = a.tokens[(uint64_t)b * a.tok_stride + pos];
@@ -27,6 +30,8 @@ __global__ void bembed_kernel(const BEmbedArgs a) {
 
 // one CTA; thread b handles sequence b
 __global__ void btoken_kernel(const BTokenArgs a) {
+    pdl_trigger();
+    pdl_wait();                                    // the argmax keys come from the lm_head finish
     const uint32_t pos = a.st->pos;
     for (uint32_t b = threadIdx.x; b < a.B; b += blockDim.x) {
         const unsigned long long k = a.keys[b];
@@ -39,12 +44,10 @@ __global__ void btoken_kernel(const BTokenArgs a) {
 }
 
 bool launch_bembed(const BEmbedArgs& a, uint32_t B, cudaStream_t st) {
-    bembed_kernel<<<B, 256, 0, st>>>(a);
-    return LM_CUDA(cudaGetLastError());
+    return LM_CUDA(launch_k(bembed_kernel, dim3(B), dim3(256), 0, st, a));
 }
 bool launch_btoken(const BTokenArgs& a, cudaStream_t st) {
-    btoken_kernel<<<1, 256, 0, st>>>(a);
-    return LM_CUDA(cudaGetLastError());
+    return LM_CUDA(launch_k(btoken_kernel, dim3(1), dim3(256), 0, st, a));
 }
 
 }  // namespace lm

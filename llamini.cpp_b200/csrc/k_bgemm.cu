@@ -17,6 +17,7 @@
 //                   optional argmax per sequence
 #include "internal.h"
 #include "bgemm.cuh"
+#include "pdl.cuh"
 
 #include <cuda_fp16.h>
 
@@ -171,6 +172,8 @@ __device__ void stage_core(const BStageArgs& a, float* xf, uint32_t b, float* re
 __global__ void __launch_bounds__(1024) bstage_kernel(const BStageArgs a) {
     extern __shared__ __align__(16) float xf[];          // K floats
     __shared__ float red[32];
+    pdl_trigger();
+    pdl_wait();                                          // x comes from the previous kernel
     const uint32_t b = blockIdx.x;
     const float* x = a.x + (uint64_t)b * a.ldx;
     for (uint32_t i = threadIdx.x; i < a.K; i += blockDim.x) xf[i] = x[i];
@@ -356,6 +359,8 @@ __device__ __forceinline__ float bfin_row(const BFinishArgs& a, uint32_t b, uint
 
 // grid (ceil((rows + rows_b + rows_c) / 256), B)
 __global__ void __launch_bounds__(256) bfinish_kernel(const BFinishArgs a) {
+    pdl_trigger();
+    pdl_wait();                                          // the partial sums come from the GEMM
     const uint32_t b = blockIdx.y, r = blockIdx.x * blockDim.x + threadIdx.x;
     unsigned long long key = 0ull;
     const float sc = a.oscale[b];
@@ -474,14 +479,12 @@ bool launch_bgemm(const BGemmArgs& a, cudaStream_t st) {
 
 bool launch_bstage(const BStageArgs& a, cudaStream_t st) {
     if (a.K % 4 != 0 || a.K > 16384) { set_error("batch staging: K %u", a.K); return false; }
-    bstage_kernel<<<a.B, 1024, (size_t)a.K * 4, st>>>(a);
-    return LM_CUDA(cudaGetLastError());
+    return LM_CUDA(launch_k(bstage_kernel, dim3(a.B), dim3(1024), (size_t)a.K * 4, st, a));
 }
 
 
 bool launch_bfinish(const BFinishArgs& a, cudaStream_t st) {
-    bfinish_kernel<<<dim3((a.rows + a.rows_b + a.rows_c + 255) / 256, a.B), 256, 0, st>>>(a);
-    return LM_CUDA(cudaGetLastError());
+    return LM_CUDA(launch_k(bfinish_kernel, dim3((a.rows + a.rows_b + a.rows_c + 255) / 256, a.B), dim3(256), 0, st, a));
 }
 
 }  // namespace lm

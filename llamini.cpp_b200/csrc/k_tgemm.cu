@@ -55,8 +55,15 @@
 // Every mbarrier wait is bounded (kTWaitNs); a wait that runs out sets an error
 // bit in *err, and every role then leaves its loop, drains the copies and
 // tensor-core work it started, and the CTA frees its tensor memory and exits.
+//
+// Launched with programmatic dependent launch: the set-up, the tensor-memory
+// allocation, the raw warp's weight copies and the decode of the first units
+// may run while the kernel that stages x is still finishing; the x warp waits
+// for it (griddepcontrol.wait) before its first copy, and the epilogue before
+// it writes partial sums that the previous finish may still be reading.
 #include "internal.h"
 #include "mma_gemv.cuh"
+#include "pdl.cuh"
 #include "quant.cuh"
 
 #include <cuda_fp16.h>
@@ -574,6 +581,7 @@ __device__ __forceinline__ TTile tg_tile(const TGemmArgs& a, uint32_t t) {
 __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_constant__ TGemmArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ TShared S;
+    pdl_trigger();
     const uint32_t NS = a.stages, NP = a.NP;
     const uint32_t ntiles = a.rblocks * a.ksplit;
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
@@ -656,6 +664,7 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
     } else if (warp == kTWarpX) {
         // ------------------------------------------------ staged inputs
         if (lane == 0) {
+            pdl_wait();                                                 // x comes from the staging kernel
             const uint32_t xb = 128 * NP;                               // bytes of one half-slab
             const uint16_t* xsum = a.xh + (uint64_t)a.K * NP;           // the 32-element sums (K-quant min terms)
             uint32_t i = 0;                                             // slabs issued
@@ -735,6 +744,7 @@ __global__ void __launch_bounds__(kTThreads, 1) tgemm_kernel(const __grid_consta
         __syncwarp();
     } else if (warp >= kTWarpEpi) {
         // ------------------------------------------------ epilogue
+        pdl_wait();                                                     // earlier kernels are done with part[]
         const uint32_t q = warp & 3u;                                   // tensor-memory lanes 32q..32q+31
         uint32_t tl = 0;
         for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x, tl++) {
@@ -1016,8 +1026,7 @@ bool tgemm_plan(TGemmArgs& a, uint32_t sms) {
 }
 
 bool launch_tgemm(const TGemmArgs& a, cudaStream_t st) {
-    tgemm_kernel<<<a.grid, kTThreads, tgemm_smem(a), st>>>(a);
-    return LM_CUDA(cudaGetLastError());
+    return LM_CUDA(launch_k(tgemm_kernel, dim3(a.grid), dim3(kTThreads), tgemm_smem(a), st, a));
 }
 
 }  // namespace lm
