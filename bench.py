@@ -204,15 +204,21 @@ def kernel_roofline(lm, torch, stream, hbm_peak, peak_kind):
             "traffic": GEMV_GATE_UP_TRAFFIC}
 
 
-def step_kernel_roofline(decode_kernel, step_bytes, t_ms, steps, hbm_peak, peak_kind, gemv_roof):
-    """Roofline of the dominant kernel. With the persistent decode kernel that
-    is the step itself: algorithmic bytes = all weights once + the KV cache
-    read at the step's position, over the device time of the timed steps
-    (one launch covers up to 64 steps, so launch duration = timed region)."""
-    if not decode_kernel:
+STEP_KERNEL_NAMES = {0: "per-op graph", 1: "decode_kernel (persistent, whole step)",
+                     2: "flow_kernel (persistent dataflow, whole step)"}
+
+
+def step_kernel_roofline(kind, step_bytes, t_ms, steps, hbm_peak, peak_kind, gemv_roof):
+    """Roofline of the dominant kernel. With a persistent step kernel (kind 1
+    or 2) that is the step itself: algorithmic bytes = all weights once + the
+    KV cache read at the step's position, over the device time of the timed
+    steps (one launch covers up to 64 steps, so launch duration = timed
+    region)."""
+    if kind == 0:
         return gemv_roof
     achieved = step_bytes / (t_ms / 1e3 / steps) / 1e9
-    return {"kernel": "decode_kernel (22 layers + lm_head + argmax per step)", "bound": "hbm",
+    name = "flow_kernel" if kind == 2 else "decode_kernel"
+    return {"kernel": name + " (22 layers + lm_head + argmax per step)", "bound": "hbm",
             "achieved": round(achieved, 1), "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
             "frac": round(achieved / hbm_peak, 4), "algorithmic_bytes_per_step": int(step_bytes),
             "us_per_step": round(t_ms * 1e3 / steps, 2), "traffic": None}
@@ -373,7 +379,7 @@ def run_ours(args, ws, rank, local):
     stream = torch.cuda.ExternalStream(L.llamini_stream())
     n_prompt = args.prompt
     prompt = synthetic().workload_prompt(WORKLOAD, n_prompt)
-    decode_kernel = L.llamini_session_kernel(sess) == 1
+    step_kind = L.llamini_session_kernel(sess)       # 0 per-op graphs, 1 / 2 persistent kernels
     weight_bytes = L.llamini_session_weight_bytes(sess)
     kv_per_pos = L.llamini_session_kv_bytes_per_pos(sess)
     if n_prompt + args.warmup + args.steps > model.max_seq:
@@ -443,7 +449,7 @@ def run_ours(args, ws, rank, local):
             "weight_stream_gbs": round(step_bytes / step_s / 1e9, 1),
             "step_roofline": {"bytes_per_step": int(step_bytes), "achieved_gbs": round(step_bytes / step_s / 1e9, 1),
                               "peak": hbm_peak, "frac": round(step_bytes / step_s / 1e9 / hbm_peak, 4)},
-            "roofline": step_kernel_roofline(decode_kernel, step_bytes, t_max, steps, hbm_peak, peak_kind, gemv_roof),
+            "roofline": step_kernel_roofline(step_kind, step_bytes, t_max, steps, hbm_peak, peak_kind, gemv_roof),
             "gemv_roofline": gemv_roof,
             "e2e": None if args.no_e2e else {
                 "value": round(ws * e2e_tok / e2e_max, 2), "unit": "tok/s",
@@ -456,8 +462,8 @@ def run_ours(args, ws, rank, local):
                         "path": "tcgen05 GEMM, 64 positions per chunk" if prefill_path == 1 else "decode steps",
                         "note": "the prompt before the timed decode (device time, second pass)"},
             "perplexity": ppl,
-            "gpu_launches": (1 + (steps + 63) // 64) if decode_kernel else steps * (1 + 5 * 22 + 2),
-            "step_kernel": "decode_kernel (persistent, whole step)" if decode_kernel else "per-op graph",
+            "gpu_launches": (1 + (steps + 63) // 64) if step_kind else steps * (1 + 5 * 22 + 2),
+            "step_kernel": STEP_KERNEL_NAMES.get(step_kind, str(step_kind)),
             "clocks": clk.summary(),
         }
         if bt:

@@ -119,10 +119,12 @@ int llamini_session_logits(llamini_session* s, f32* out);
 /* Current position (number of tokens already run through the stack). */
 u32 llamini_session_pos(llamini_session* s);
 
-/* How the session runs its steps: 0 = one graph of per-op kernels per step
- * (the default), 1 = the persistent decode kernel (one cooperative launch for
- * up to 64 steps), chosen when LLAMINI_DECODE_KERNEL=1 was set at session
- * creation and every matrix is Q4_K, Q6_K, Q8_0 or Q4_0; -1 = NULL. */
+/* How the session runs its steps: 2 = the dataflow decode kernel (one
+ * cooperative launch for up to 64 steps; the default for LLaMA-family models
+ * whose matrices are all Q4_K / Q6_K with K a multiple of 256 up to 6144),
+ * 1 = the earlier persistent decode kernel (LLAMINI_DECODE_KERNEL=1 at session
+ * creation, every matrix Q4_K, Q6_K, Q8_0 or Q4_0), 0 = one graph of per-op
+ * kernels per step (every other model, or LLAMINI_DECODE_KERNEL=0); -1 = NULL. */
 int llamini_session_kernel(llamini_session* s);
 
 /* Algorithmic bytes one step reads: every weight matrix once, norms, biases and

@@ -225,6 +225,99 @@ uint32_t decode_ring_bytes(uint32_t kmax, uint32_t hd);
 uint32_t decode_tile_alloc(const GemvSeg& G);    // ring bytes of one tile of G
 bool launch_decode(const DecArgs& a, cudaStream_t st);
 
+// ---------------------------------------------------------------- dataflow decode kernel
+// Batch-1 decode steps as one persistent kernel (k_flow.cu) whose GEMV inputs
+// travel between ops as records: per 16 consecutive elements x_i, the fp16
+// high and low parts of x_i * 2^E (E chosen from the group's largest |x_i|),
+// already in the order of an mma.sync B fragment, plus 2^(24-E) and the sum
+// of the 16 values. The op that produces a vector writes its records in its
+// epilogue (a 16-row tile is one group); the consumers copy their slice of K.
+// An RMS-normalised input carries the norm weight folded in and, per group,
+// the sum of squares of the raw vector; the consumer applies 1/rms to its dot
+// products. The O projection's input is merged from the attention partials by
+// the consumers themselves.
+enum FlowKind : uint32_t { FLOW_GEMV = 0, FLOW_ATTN = 1 };
+constexpr uint32_t kFlowStepStart = 0xFFFFFFFFu;   // the op waits for the step's input embedding
+
+struct FlowRec {
+    uint32_t* w = nullptr;     // [groups][16]: words 0..7 fp16 high pairs, 8..15 low pairs
+    float2* fs = nullptr;      // [groups]: {2^(24-E), sum of the group's values}
+    float* ss = nullptr;       // [groups]: sum of squares of the raw values (normalised inputs), or null
+};
+
+struct FlowSeg {
+    const uint8_t* w = nullptr;     // matrix (gate for GLU)
+    const uint8_t* w2 = nullptr;    // up matrix for GLU
+    uint64_t row_bytes = 0, row_bytes2 = 0;
+    uint32_t type = 0, rows = 0, epi = EPI_STORE, tile0 = 0;
+    float* out = nullptr;            // f32 rows (EPI_RESID: unused, the residual stream takes the sum)
+    const float* bias = nullptr;
+    // rows of an even number of 16-byte units reach shared memory through one
+    // TMA tensor copy per tile whose box is one unit wider than the row (the
+    // padded stride keeps the 8 rows an MMA reads in different banks); other
+    // rows move as one contiguous bulk copy. Set by flow_encode_maps.
+    const CUtensorMap* map = nullptr;
+    const CUtensorMap* map2 = nullptr;
+};
+
+struct FlowOp {
+    uint32_t kind = FLOW_GEMV;
+    uint32_t ntasks = 0;            // tiles, or (head, split) tasks; each completes once per step
+    uint32_t wait = kFlowStepStart; // op whose completion this op needs
+    uint32_t wait_n = 0;            // completions per step of that op
+    // GEMV
+    uint32_t K = 0, nseg = 0;
+    uint32_t in_attn = 0;           // input = merge of at's split partials (else the records `in`)
+    FlowRec in;                     // in.ss != null: RMSNorm of the input (eps below)
+    float eps = 0.f;
+    FlowSeg seg[3];
+    FlowRec out;                    // records of the output for the next GEMV (out.w null: none)
+    const float* out_nw = nullptr;  // norm weight folded into the output records (null: none)
+    uint32_t trace_off = 0xFFFFFFFFu;   // residual-add ops that end a layer: offset in the trace
+    uint32_t argmax = 0;            // the lm_head: argmax key and step finish
+    // attention (kind FLOW_ATTN, and the partials an in_attn op merges)
+    uint32_t n_split = 1;
+    AttnArgs at = {};
+};
+
+struct FlowArgs {
+    const FlowOp* ops = nullptr;
+    uint32_t n_ops = 0;
+    const uint32_t* sched = nullptr;      // CTA c: sched_len[c] entries at sched + c * sched_stride
+    const uint32_t* sched_len = nullptr;  // entry = (op << 16) | task
+    uint32_t sched_stride = 0;
+    uint32_t n_cta = 0;
+    DecSync* sync = nullptr;              // step_done counts finished steps (input embedded)
+    uint32_t* done = nullptr;             // [n_ops] completions (monotonic)
+    StepState* st = nullptr;
+    uint32_t* tokens = nullptr;
+    uint32_t max_tokens = 0;
+    DevMat tok;                           // token embedding table
+    float emb_scale = 1.f;
+    float* hidden = nullptr;              // the residual stream
+    FlowRec in0;                          // records of the first layer's input
+    const float* n1w0 = nullptr;          // the first layer's attention norm weight
+    uint32_t dim = 0;
+    float* trace = nullptr;               // per-layer residual stream, or null
+    uint32_t n_steps = 1;
+    uint32_t ring_bytes = 0;
+    uint32_t hd = 0;
+};
+constexpr uint32_t kFlowMaxOps = 256;         // ops of one step
+constexpr uint32_t kFlowMaxTasks = 512;       // tasks of one CTA per step
+constexpr uint32_t kFlowMaxSb = 3;            // 256-element super-blocks of K per consumer warp (K <= 6144)
+bool flow_init();
+bool flow_supported_type(uint32_t type);
+uint32_t flow_ring_bytes(uint32_t hd);
+uint32_t flow_tile_alloc(const FlowSeg& G);
+// Tensor maps for every padded-row matrix of `ops` (written into `maps`, a
+// device array of n_maps entries, and referenced from the segments); false
+// with an error set when the driver refuses one.
+uint32_t flow_maps_needed(const FlowOp* ops, uint32_t n_ops);
+bool flow_encode_maps(FlowOp* ops, uint32_t n_ops, CUtensorMap* d_maps);
+bool launch_flow(const FlowArgs& a, cudaStream_t st);
+bool launch_flow_embed(const FlowArgs& a, cudaStream_t st);
+
 // ---------------------------------------------------------------- batched GEMM
 // Up to 64 input vectors per weight pass (k_bgemm.cu): staging per sequence,
 // split-K dequant GEMM into raw partials, per-(sequence, row) finish.

@@ -366,7 +366,7 @@ bool kernels_init() {
     // one shared-memory carveout for every kernel of the step, so consecutive
     // kernels never wait for an SM to reconfigure its L1 / shared split
     const int carve = cudaFuncAttributePreferredSharedMemoryCarveout;
-    return gemv_init() && gemv_mma_init() && attn_init() && decode_init() && bgemm_init() && tgemm_init() && prefill_init() &&
+    return gemv_init() && gemv_mma_init() && attn_init() && decode_init() && flow_init() && bgemm_init() && tgemm_init() && prefill_init() &&
            LM_CUDA(cudaFuncSetAttribute(embed_kernel, (cudaFuncAttribute)carve, 100)) &&
            LM_CUDA(cudaFuncSetAttribute(finish_kernel, (cudaFuncAttribute)carve, 100)) &&
            LM_CUDA(cudaFuncSetAttribute(copy_kernel, (cudaFuncAttribute)carve, 100)) &&

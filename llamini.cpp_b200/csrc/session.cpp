@@ -87,6 +87,12 @@ struct llamini_session {
     u32* dec_counters = nullptr;          // DecSync | done[n_ops] | tickets[n_layers][n_heads]
     size_t dec_counter_bytes = 0;
 
+    // dataflow decode kernel (k_flow.cu): op table, schedule, counters, records
+    bool flow_on = false;
+    lm::FlowArgs flow;
+    u32* flow_counters = nullptr;         // DecSync | done[n_ops]
+    size_t flow_counter_bytes = 0;
+
     // host mirror of the device position / prompt length
     u32 pos = 0, n_prompt = 0;
 };
@@ -523,6 +529,195 @@ bool build_decode(llamini_session* s) {
 
 
 
+// Op table, records and per-CTA schedule of the dataflow decode kernel
+// (k_flow.cu). Taken by LLaMA-family models (RMSNorm, no tensor parallelism)
+// whose matrices are all Q4_K or Q6_K with every K a multiple of 256 up to
+// 6144; returns true with flow_on = false for any other model, which keeps
+// the per-op graphs. LLAMINI_DECODE_KERNEL=0 turns it off, =1 selects the
+// earlier persistent kernel instead.
+bool build_flow(llamini_session* s) {
+    s->flow_on = false;
+    const char* env = getenv("LLAMINI_DECODE_KERNEL");
+    if (env && (env[0] == '0' || env[0] == '1')) return true;
+    if (s->kind != 0 || s->tp_world > 1) return true;
+    if (s->hd == 0 || s->hd % 16 != 0 || s->hd > 256 || s->n_split > 32) return true;
+    const u32 kmax = 256 * 8 * kFlowMaxSb;
+    auto k_ok = [&](u32 K) { return K % 256 == 0 && K <= kmax; };
+    if (!k_ok(s->dim) || !k_ok(s->ffn) || !k_ok(s->qd) || s->dim % 16 != 0) return true;
+    auto m_ok = [](const DevMat& m) {
+        return flow_supported_type(m.type) && reinterpret_cast<uintptr_t>(m.ptr) % 16 == 0;
+    };
+    for (const auto& W : s->layers)
+        if (!m_ok(W.q) || !m_ok(W.k) || !m_ok(W.v) || !m_ok(W.o) || !m_ok(W.gate) || !m_ok(W.up) ||
+            !m_ok(W.down) || W.gate.type != W.up.type)
+            return true;
+    if (!m_ok(s->head) || s->tok.ptr == nullptr) return true;
+    const u32 L = s->n_layers;
+    // records: A = the residual stream for QKV and the lm_head, B = for gate/up, C = the FFN activation
+    auto rec = [&](u32 n, bool ss, FlowRec* r) {
+        r->w = (uint32_t*)own(s, (size_t)n * 4);
+        r->fs = (float2*)own(s, (size_t)n / 16 * sizeof(float2));
+        r->ss = ss ? (float*)own(s, (size_t)n / 16 * 4) : nullptr;
+        return r->w && r->fs && (!ss || r->ss);
+    };
+    FlowRec ra, rb, rc;
+    if (!rec(s->dim, true, &ra) || !rec(s->dim, true, &rb) || !rec(s->ffn, false, &rc)) return false;
+    std::vector<FlowOp> ops;
+    auto seg = [](const DevMat& m, u32 epi, float* out, const float* bias) {
+        FlowSeg g;
+        g.w = m.ptr;
+        g.row_bytes = m.row_bytes;
+        g.type = m.type;
+        g.rows = m.rows;
+        g.epi = epi;
+        g.out = out;
+        g.bias = bias;
+        return g;
+    };
+    auto gemv = [&](u32 K, u32 wait) {
+        FlowOp op;
+        op.kind = FLOW_GEMV;
+        op.K = K;
+        op.wait = wait;
+        op.eps = s->eps;
+        return op;
+    };
+    auto finish_op = [&](FlowOp& op) {
+        u32 tiles = 0;
+        for (u32 i = 0; i < op.nseg; i++) {
+            op.seg[i].tile0 = tiles;
+            tiles += (op.seg[i].rows + 15) / 16;
+        }
+        if (op.kind == FLOW_GEMV) op.ntasks = tiles;
+        op.wait_n = op.wait == kFlowStepStart ? 0u : ops[op.wait].ntasks;
+        ops.push_back(op);
+        return (u32)ops.size() - 1;
+    };
+    u32 prev = kFlowStepStart;
+    for (u32 l = 0; l < L; l++) {
+        const auto& W = s->layers[l];
+        FlowOp q = gemv(s->dim, prev);
+        q.nseg = 3;
+        q.seg[0] = seg(W.q, EPI_STORE, s->qkv, W.bq);
+        q.seg[1] = seg(W.k, EPI_STORE, s->qkv + s->qd, W.bk);
+        q.seg[2] = seg(W.v, EPI_STORE, s->qkv + s->qd + s->kvd, W.bv);
+        q.in = ra;
+        const u32 qi = finish_op(q);
+        FlowOp at;
+        at.kind = FLOW_ATTN;
+        at.at = attn_args(s, l);
+        at.at.counter = nullptr;
+        at.n_split = s->n_split;
+        at.ntasks = s->n_heads * s->n_split;
+        at.wait = qi;
+        const u32 ai = finish_op(at);
+        FlowOp o = gemv(s->qd, ai);
+        o.nseg = 1;
+        o.seg[0] = seg(W.o, EPI_RESID, nullptr, W.bo);
+        o.in_attn = 1;
+        o.at = ops[ai].at;
+        o.n_split = s->n_split;
+        o.out = rb;
+        o.out_nw = W.n2w;
+        const u32 oi = finish_op(o);
+        FlowOp f = gemv(s->dim, oi);
+        f.nseg = 1;
+        f.seg[0] = seg(W.gate, s->act_gelu ? (u32)EPI_GLU_GELU : (u32)EPI_GLU_SILU, s->ffn_h, nullptr);
+        f.seg[0].w2 = W.up.ptr;
+        f.seg[0].row_bytes2 = W.up.row_bytes;
+        f.in = rb;
+        f.out = rc;
+        const u32 fi = finish_op(f);
+        FlowOp d = gemv(s->ffn, fi);
+        d.nseg = 1;
+        d.seg[0] = seg(W.down, EPI_RESID, nullptr, W.bdown);
+        d.in = rc;
+        d.out = ra;
+        d.out_nw = l + 1 < L ? s->layers[l + 1].n1w : s->fnw;
+        d.trace_off = l * s->dim;
+        prev = finish_op(d);
+    }
+    FlowOp h = gemv(s->dim, prev);
+    h.nseg = 1;
+    h.seg[0] = seg(s->head, EPI_STORE, s->logits, nullptr);
+    h.in = ra;
+    h.argmax = 1;
+    finish_op(h);
+    if (ops.size() > kFlowMaxOps || ops.size() >= (1u << 16)) return true;
+    for (const FlowOp& op : ops)
+        if (op.ntasks > 0xFFFFu) return true;
+    // shared memory: the ring must hold two of the largest tiles
+    const u32 ring = flow_ring_bytes(s->hd);
+    u32 max_tile = 0;
+    for (const FlowOp& op : ops)
+        for (u32 i = 0; op.kind == FLOW_GEMV && i < op.nseg; i++) {
+            const u32 t = flow_tile_alloc(op.seg[i]);
+            max_tile = max_tile > t ? max_tile : t;
+        }
+    if (ring == 0 || 2 * (u64)max_tile > ring) return true;
+    // schedule: the tasks of each op in turn, dealt round-robin over the CTAs
+    // with the dealing position carried from op to op
+    const u32 n_cta = (u32)sm_count();
+    std::vector<std::vector<u32>> per(n_cta);
+    u32 cursor = 0;
+    for (u32 i = 0; i < (u32)ops.size(); i++)
+        for (u32 t = 0; t < ops[i].ntasks; t++) {
+            per[cursor].push_back((i << 16) | t);
+            cursor = (cursor + 1) % n_cta;
+        }
+    u32 stride = 1;
+    for (auto& v : per) stride = stride > v.size() ? stride : (u32)v.size();
+    if (stride > kFlowMaxTasks) return true;
+    std::vector<u32> sched((size_t)n_cta * stride, 0u), len(n_cta);
+    for (u32 c = 0; c < n_cta; c++) {
+        len[c] = (u32)per[c].size();
+        for (size_t k = 0; k < per[c].size(); k++) sched[(size_t)c * stride + k] = per[c][k];
+    }
+    // one tensor map per matrix whose tiles move through TMA tensor copies
+    const u32 n_maps = flow_maps_needed(ops.data(), (u32)ops.size());
+    if (n_maps) {
+        CUtensorMap* d_maps = (CUtensorMap*)own(s, (size_t)n_maps * sizeof(CUtensorMap));
+        if (!d_maps) return false;
+        if (!flow_encode_maps(ops.data(), (u32)ops.size(), d_maps)) return true;   // keep the per-op graphs
+    }
+    const size_t counter_words = 4 + ops.size();
+    s->flow_counters = (u32*)own(s, counter_words * 4);
+    FlowOp* d_ops = (FlowOp*)own(s, ops.size() * sizeof(FlowOp));
+    u32* d_sched = (u32*)own(s, sched.size() * 4);
+    u32* d_len = (u32*)own(s, len.size() * 4);
+    if (!s->flow_counters || !d_ops || !d_sched || !d_len) return false;
+    s->flow_counter_bytes = counter_words * 4;
+    if (!LM_CUDA(cudaMemcpy(d_ops, ops.data(), ops.size() * sizeof(FlowOp), cudaMemcpyHostToDevice)) ||
+        !LM_CUDA(cudaMemcpy(d_sched, sched.data(), sched.size() * 4, cudaMemcpyHostToDevice)) ||
+        !LM_CUDA(cudaMemcpy(d_len, len.data(), len.size() * 4, cudaMemcpyHostToDevice)) ||
+        !LM_CUDA(cudaMemset(s->flow_counters, 0, s->flow_counter_bytes)))
+        return false;
+    FlowArgs& a = s->flow;
+    a.ops = d_ops;
+    a.n_ops = (u32)ops.size();
+    a.sched = d_sched;
+    a.sched_len = d_len;
+    a.sched_stride = stride;
+    a.n_cta = n_cta;
+    a.sync = reinterpret_cast<DecSync*>(s->flow_counters);
+    a.done = s->flow_counters + 4;
+    a.st = s->st;
+    a.tokens = s->tokens;
+    a.max_tokens = s->max_seq + 1;
+    a.tok = s->tok;
+    a.emb_scale = s->emb_scale;
+    a.hidden = s->hidden;
+    a.in0 = ra;
+    a.n1w0 = s->layers[0].n1w;
+    a.dim = s->dim;
+    a.trace = nullptr;
+    a.n_steps = 1;
+    a.ring_bytes = ring;
+    a.hd = s->hd;
+    s->flow_on = true;
+    return true;
+}
+
 // theta_j = base^(-2j/hd), evaluated exactly as model.c:38 / model.c:50 do
 bool upload_theta(llamini_session* s) {
     std::vector<f32> th(s->hd / 2 ? s->hd / 2 : 1);
@@ -537,7 +732,8 @@ bool finish_build(llamini_session* s) {
     if (!alloc_buffers(s)) return false;
     if (!capture(s, 1, false, false, &s->g_one)) return false;
     if (!capture(s, kStepsPerGraph, false, false, &s->g_many)) return false;
-    return build_decode(s);
+    if (!build_flow(s)) return false;
+    return s->flow_on || build_decode(s);
 }
 
 llamini_session* find(const void* model, KVCache* caches) {
@@ -715,6 +911,7 @@ bool write_state(llamini_session* s, u32 pos, u32 n_prompt, bool reset_nll) {
     const size_t n = reset_nll ? sizeof(StepState) : offsetof(StepState, nll);
     if (!LM_CUDA(cudaMemcpyAsync(s->st, s->st_host, n, cudaMemcpyHostToDevice, st))) return false;
     if (s->dec_on && !LM_CUDA(cudaMemsetAsync(s->dec_counters, 0, s->dec_counter_bytes, st))) return false;
+    if (s->flow_on && !LM_CUDA(cudaMemsetAsync(s->flow_counters, 0, s->flow_counter_bytes, st))) return false;
     s->pos = pos;
     s->n_prompt = n_prompt;
     return true;
@@ -726,6 +923,20 @@ bool run_steps(llamini_session* s, u32 n) {
         return false;
     }
     cudaStream_t st = stream();
+    if (s->flow_on && n > 0) {
+        // the kernel prepares the input of each following step itself; the
+        // first step's input is prepared here
+        FlowArgs a = s->flow;
+        a.trace = s->trace_on ? s->trace : nullptr;
+        if (!launch_flow_embed(a, st)) return false;
+        for (u32 left = n; left > 0;) {
+            a.n_steps = left < kDecStepsPerLaunch ? left : kDecStepsPerLaunch;
+            if (!launch_flow(a, st)) return false;
+            left -= a.n_steps;
+        }
+        s->pos += n;
+        return true;
+    }
     if (s->dec_on && n > 0) {
         // the kernel embeds the input of each following step itself; the first
         // step's input is embedded here
@@ -1950,7 +2161,7 @@ int llamini_session_logits(llamini_session* s, f32* out) {
 }
 
 u32 llamini_session_pos(llamini_session* s) { return s ? s->pos : 0; }
-int llamini_session_kernel(llamini_session* s) { return s ? (s->dec_on ? 1 : 0) : -1; }
+int llamini_session_kernel(llamini_session* s) { return s ? (s->flow_on ? 2 : s->dec_on ? 1 : 0) : -1; }
 u64 llamini_session_weight_bytes(llamini_session* s) { return s ? s->weight_bytes : 0; }
 u64 llamini_session_kv_bytes_per_pos(llamini_session* s) {
     return s ? (u64)s->n_layers * 2 * s->n_kv * s->hd * (s->kv_f16 ? 2 : 4) : 0;
