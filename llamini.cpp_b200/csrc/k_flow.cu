@@ -160,10 +160,12 @@ __device__ __forceinline__ uint32_t wait_target(const FlowOp& op, uint32_t E) {
 
 // ------------------------------------------------------------------ records
 
+// E with max|x| * 2^E in [2^13, 2^14): 14 minus frexp's exponent of the group's
+// largest magnitude, read from the float's exponent field (a zero or subnormal
+// maximum gives the upper clamp, inf or NaN the lower one).
 __device__ __forceinline__ int group_exp(float m) {
-    int e = 0;
-    if (m > 0.f && m < INFINITY) frexpf(m, &e);
-    int E = 14 - e;
+    const int e = (int)((__float_as_uint(m) >> 23) & 0xFFu) - 126;
+    const int E = 14 - e;
     return E > 100 ? 100 : (E < -100 ? -100 : E);
 }
 __device__ __forceinline__ float pow2(int e) { return __int_as_float((e + 127) << 23); }
@@ -312,32 +314,75 @@ __device__ XFrag frag_attn(const FlowOp& op, uint32_t ns, uint32_t sb, uint32_t 
         // heads of 16 or 32: the four groups may span heads; merge each group alone
         return frag_attn_small(op, ns, sb, slot, part, tig);
     }
-    // the splits' (m, l) first (one round trip), then the weighted values
-    // split by split; the same operations in the same order as merge_head4
-    float2 ml[4] = {};
+    // the two lanes holding the same elements (high and low part, lane ^ 4)
+    // weight alternate pairs of splits; with at most four splits one round of
+    // loads brings every (m, l) and both of the lane's splits' values. The sums
+    // are added in a fixed order (every CTA gets the same bits).
+    if (ns <= 4) {
+        float2 ml[4];
+        float4 v0[4], v1[4];
+        const uint32_t s0 = 2 * part, s1 = s0 + 1;
 #pragma unroll
-    for (uint32_t s = 0; s < 4; s++)
-        if (s < ns) ml[s] = __ldcg(reinterpret_cast<const float2*>(src + s * stride));
-    for (uint32_t s = 4; s < ns; s++) M = fmaxf(M, __ldcg(src + s * stride));
-#pragma unroll
-    for (uint32_t s = 0; s < 4; s++)
-        if (s < ns) M = fmaxf(M, ml[s].x);
-    auto add_split = [&](uint32_t s, float2 m) {
-        const float ws = expf(m.x - M);
-        Ls = fmaf(ws, m.y, Ls);
+        for (uint32_t s = 0; s < 4; s++)
+            ml[s] = s < ns ? __ldcg(reinterpret_cast<const float2*>(src + s * stride)) : make_float2(-INFINITY, 0.f);
 #pragma unroll
         for (uint32_t k = 0; k < 4; k++) {
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(src + s * stride + 4 + d0 + 16 * k));
-            acc[k].x = fmaf(v.x, ws, acc[k].x);
-            acc[k].y = fmaf(v.y, ws, acc[k].y);
-            acc[k].z = fmaf(v.z, ws, acc[k].z);
-            acc[k].w = fmaf(v.w, ws, acc[k].w);
+            v0[k] = s0 < ns ? __ldcg(reinterpret_cast<const float4*>(src + s0 * stride + 4 + d0 + 16 * k))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            v1[k] = s1 < ns ? __ldcg(reinterpret_cast<const float4*>(src + s1 * stride + 4 + d0 + 16 * k))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-    };
 #pragma unroll
-    for (uint32_t s = 0; s < 4; s++)
-        if (s < ns) add_split(s, ml[s]);
-    for (uint32_t s = 4; s < ns; s++) add_split(s, __ldcg(reinterpret_cast<const float2*>(src + s * stride)));
+        for (uint32_t s = 0; s < 4; s++) M = fmaxf(M, ml[s].x);
+        const float2 m0 = part ? ml[2] : ml[0], m1 = part ? ml[3] : ml[1];
+        const float w0 = s0 < ns ? expf(m0.x - M) : 0.f, w1 = s1 < ns ? expf(m1.x - M) : 0.f;
+        Ls = fmaf(w1, m1.y, fmaf(w0, m0.y, 0.f));
+#pragma unroll
+        for (uint32_t k = 0; k < 4; k++) {
+            acc[k].x = fmaf(v1[k].x, w1, v0[k].x * w0);
+            acc[k].y = fmaf(v1[k].y, w1, v0[k].y * w0);
+            acc[k].z = fmaf(v1[k].z, w1, v0[k].z * w0);
+            acc[k].w = fmaf(v1[k].w, w1, v0[k].w * w0);
+        }
+    } else {
+        for (uint32_t s = 0; s < ns; s++) M = fmaxf(M, __ldcg(src + s * stride));
+        for (uint32_t s0 = 2 * part; s0 < ns; s0 += 4) {
+            const uint32_t s1 = s0 + 1 < ns ? s0 + 1 : s0;
+            const float2 m0 = __ldcg(reinterpret_cast<const float2*>(src + s0 * stride));
+            const float2 m1 = __ldcg(reinterpret_cast<const float2*>(src + s1 * stride));
+            float4 v0[4], v1[4];
+#pragma unroll
+            for (uint32_t k = 0; k < 4; k++) {
+                v0[k] = __ldcg(reinterpret_cast<const float4*>(src + s0 * stride + 4 + d0 + 16 * k));
+                v1[k] = __ldcg(reinterpret_cast<const float4*>(src + s1 * stride + 4 + d0 + 16 * k));
+            }
+            const float w0 = expf(m0.x - M), w1 = s1 != s0 ? expf(m1.x - M) : 0.f;
+            Ls = fmaf(w1, m1.y, fmaf(w0, m0.y, Ls));
+#pragma unroll
+            for (uint32_t k = 0; k < 4; k++) {
+                acc[k].x = fmaf(v1[k].x, w1, fmaf(v0[k].x, w0, acc[k].x));
+                acc[k].y = fmaf(v1[k].y, w1, fmaf(v0[k].y, w0, acc[k].y));
+                acc[k].z = fmaf(v1[k].z, w1, fmaf(v0[k].z, w0, acc[k].z));
+                acc[k].w = fmaf(v1[k].w, w1, fmaf(v0[k].w, w0, acc[k].w));
+            }
+        }
+    }
+    // part 0 took splits 0, 1, 4, 5, ..., part 1 splits 2, 3, 6, 7, ...: add them
+    // with the part-0 sum first on both lanes
+    {
+        const float o = __shfl_xor_sync(0xffffffffu, Ls, 4);
+        Ls = part == 0 ? Ls + o : o + Ls;
+    }
+#pragma unroll
+    for (uint32_t k = 0; k < 4; k++) {
+        float4 o;
+        o.x = __shfl_xor_sync(0xffffffffu, acc[k].x, 4);
+        o.y = __shfl_xor_sync(0xffffffffu, acc[k].y, 4);
+        o.z = __shfl_xor_sync(0xffffffffu, acc[k].z, 4);
+        o.w = __shfl_xor_sync(0xffffffffu, acc[k].w, 4);
+        acc[k] = part == 0 ? make_float4(acc[k].x + o.x, acc[k].y + o.y, acc[k].z + o.z, acc[k].w + o.w)
+                           : make_float4(o.x + acc[k].x, o.y + acc[k].y, o.z + acc[k].z, o.w + acc[k].w);
+    }
     float4 vk[4];
 #pragma unroll
     for (uint32_t k = 0; k < 4; k++) vk[k] = make_float4(acc[k].x / Ls, acc[k].y / Ls, acc[k].z / Ls, acc[k].w / Ls);
@@ -660,6 +705,7 @@ __device__ void producer(const FlowArgs& a, FlowShared& S, uint8_t* ring) {
                 const uint32_t c = vload(&S.consumed);
                 const uint64_t tail = c == 0 ? 0ull : S.vend[(c - 1) % kQ];
                 if (seq - c < kQ && head + alloc - tail <= R) { ok = true; break; }
+                __nanosleep(64);                  // leave the SM's issue slots to the other warps
                 if ((w & 63u) == 63u && (aborted(a, S) || gtime() - t0 > kWaitNs)) break;
             }
             if (!ok || stopped(S)) {
