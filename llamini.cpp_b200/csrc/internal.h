@@ -315,6 +315,10 @@ uint32_t flow_tile_alloc(const FlowSeg& G);
 // with an error set when the driver refuses one.
 uint32_t flow_maps_needed(const FlowOp* ops, uint32_t n_ops);
 bool flow_encode_maps(FlowOp* ops, uint32_t n_ops, CUtensorMap* d_maps);
+// Tensor map of a matrix's 16-row tiles at the padded shared-memory stride
+// (rows of an even number of 16-byte units, at most 255 units); false when the
+// driver refuses it.
+bool encode_tile_map(CUtensorMap* m, const uint8_t* w, uint64_t row_bytes, uint32_t rows);
 bool launch_flow(const FlowArgs& a, cudaStream_t st);
 bool launch_flow_embed(const FlowArgs& a, cudaStream_t st);
 

@@ -531,26 +531,7 @@ __device__ __forceinline__ void sb_q6k(const uint8_t* bg, const uint8_t* bg8, co
 }
 
 __host__ __device__ __forceinline__ bool flow_glu(uint32_t epi) { return epi == EPI_GLU_SILU || epi == EPI_GLU_GELU; }
-// Rows copied through a tensor map: an even number of 16-byte units (their
-// shared-memory stride is padded by one unit).
-__host__ __device__ __forceinline__ bool padded_rows(uint64_t rb) { return smem_rs(rb) != rb; }
-
-// TMA tensor copy of one 16-row tile: box {8 halves, units + 1, 16 rows} of a
-// rank-3 view {8, units per row, rows} at row row0, written densely, so rows
-// land at the padded stride; the extra unit and rows past the end read as
-// zeros. No multicast.
-__device__ __forceinline__ void tma_tile(void* dst, const CUtensorMap* map, int32_t row0, uint64_t* bar) {
-    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-                 " [%0], [%1, {%2, %3, %4}], [%5];\n"
-                 ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(0), "r"(row0),
-                   "r"(smem_u32(bar)) : "memory");
-}
-// Bytes one tile of G's rows brings into shared memory.
-__host__ __device__ __forceinline__ uint32_t tile_tx(uint64_t rb, uint32_t nrows) {
-    return padded_rows(rb) ? 16u * (uint32_t)smem_rs(rb) : rows_tx(rb, nrows);
-}
 __host__ __device__ __forceinline__ uint32_t sb_bytes(uint32_t type) { return type == T_Q6_K ? 210u : 144u; }
-
 // Ring bytes of a tile (sized for 16 rows; 16 bytes of slack for word reads).
 __host__ __device__ __forceinline__ uint32_t ftile_alloc(const FlowSeg& G) {
     const uint32_t t1 = tile_bytes(G.row_bytes);
@@ -694,8 +675,8 @@ __device__ void producer(const FlowArgs& a, FlowShared& S, uint8_t* ring) {
             const FTile tr = ftile_of(op, ent & 0xFFFFu);
             const FlowSeg& G = op.seg[tr.seg];
             const bool glu = flow_glu(G.epi);
-            const uint32_t n1 = tile_tx(G.row_bytes, tr.nrows);
-            const uint32_t n2 = glu ? tile_tx(G.row_bytes2, tr.nrows) : 0u;
+            const uint32_t n1 = tile_tx(G.row_bytes, tr.nrows, G.map != nullptr);
+            const uint32_t n2 = glu ? tile_tx(G.row_bytes2, tr.nrows, G.map2 != nullptr) : 0u;
             const uint32_t alloc = ftile_alloc(G);
             uint64_t off = head % R;
             if (off + alloc > R) { head += R - off; off = 0; }
@@ -1065,7 +1046,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 flow_encoder() {
 
 // Rank-3 view of a matrix's rows as uint16: {8 (one 16-byte unit), units per
 // row, rows}, strides {16 bytes, row bytes}; box {8, units + 1, 16}.
-static bool encode_tile_map(CUtensorMap* m, const uint8_t* w, uint64_t rb, uint32_t rows) {
+bool encode_tile_map(CUtensorMap* m, const uint8_t* w, uint64_t rb, uint32_t rows) {
     PFN_cuTensorMapEncodeTiled_v12000 fn = flow_encoder();
     if (!fn) return false;
     const uint64_t units = rb / 16;

@@ -145,23 +145,38 @@ __device__ void stage_x(const GemvArgs& a, const MmaSmem& sm, float* s_scale) {
 
 // ------------------------------------------------------------------ tiles
 
-// Thread 0: start the copies of tile t into stage buffer `buf`.
-__device__ __forceinline__ void issue_tile(const GemvArgs& a, uint32_t t, uint8_t* buf, uint64_t* bar) {
+// Tensor maps of the segments whose rows are padded in shared memory (one TMA
+// copy per tile instead of one bulk copy per row); has = 0: bulk copies.
+struct alignas(64) GemvMaps {
+    CUtensorMap m[kMaxSegs][2];
+    uint32_t has[kMaxSegs][2];
+};
+
+// Thread 0: start the copies of tile t into stage buffer `buf` (128-byte aligned).
+__device__ __forceinline__ void issue_tile(const GemvArgs& a, const GemvMaps& maps, uint32_t t, uint8_t* buf,
+                                           uint64_t* bar) {
     const TileRef tr = tile_of(a, t);
     const GemvSeg& G = a.seg[tr.seg];
     const bool glu = G.epi == EPI_GLU_SILU || G.epi == EPI_GLU_GELU;
-    const uint32_t n1 = rows_tx(G.row_bytes, tr.nrows);
-    const uint32_t n2 = glu ? rows_tx(G.row_bytes2, tr.nrows) : 0u;
+    const bool t1 = maps.has[tr.seg][0] != 0, t2 = maps.has[tr.seg][1] != 0;
+    const uint32_t n1 = tile_tx(G.row_bytes, tr.nrows, t1);
+    const uint32_t n2 = glu ? tile_tx(G.row_bytes2, tr.nrows, t2) : 0u;
     mbar_expect_tx(bar, n1 + n2);
-    copy_rows(buf, G.w + (uint64_t)tr.row0 * G.row_bytes, G.row_bytes, tr.nrows, bar);
-    if (glu) copy_rows(buf + up_offset(G), G.w2 + (uint64_t)tr.row0 * G.row_bytes2, G.row_bytes2, tr.nrows, bar);
+    if (t1) tma_tile(buf, &maps.m[tr.seg][0], (int32_t)tr.row0, bar);
+    else copy_rows(buf, G.w + (uint64_t)tr.row0 * G.row_bytes, G.row_bytes, tr.nrows, bar);
+    if (glu) {
+        if (t2) tma_tile(buf + up_offset(G), &maps.m[tr.seg][1], (int32_t)tr.row0, bar);
+        else copy_rows(buf + up_offset(G), G.w2 + (uint64_t)tr.row0 * G.row_bytes2, G.row_bytes2, tr.nrows, bar);
+    }
 }
 
 // ------------------------------------------------------------------ kernel
 
 __global__ void __launch_bounds__(kMThreads)
-gemv_mma_kernel(const __grid_constant__ GemvArgs a, uint32_t stage_bytes) {
-    extern __shared__ __align__(128) uint8_t smem_raw[];
+gemv_mma_kernel(const __grid_constant__ GemvArgs a, uint32_t stage_bytes, const __grid_constant__ GemvMaps maps) {
+    extern __shared__ __align__(128) uint8_t smem_dyn[];
+    // tensor copies need 128-byte aligned destinations
+    uint8_t* const smem_raw = smem_dyn + ((128u - (smem_u32(smem_dyn) & 127u)) & 127u);
     __shared__ float s_scale;
     __shared__ __align__(8) uint64_t bars[kStages];
     __shared__ int s_fail;
@@ -186,7 +201,7 @@ gemv_mma_kernel(const __grid_constant__ GemvArgs a, uint32_t stage_bytes) {
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         for (uint32_t i = 0; i < kStages; i++) {
             const uint32_t t = blockIdx.x + i * gridDim.x;
-            if (t < n_tiles) issue_tile(a, t, stages + i * stage_bytes, &bars[i]);
+            if (t < n_tiles) issue_tile(a, maps, t, stages + i * stage_bytes, &bars[i]);
         }
     }
     pdl_wait();                                                   // x comes from the previous kernel
@@ -238,7 +253,7 @@ gemv_mma_kernel(const __grid_constant__ GemvArgs a, uint32_t stage_bytes) {
         __syncthreads();                          // stage buffer consumed, partials ready
         if (tid == 0) {
             const uint32_t nt = t + kStages * gridDim.x;
-            if (nt < n_tiles) issue_tile(a, nt, buf, &bars[st]);
+            if (nt < n_tiles) issue_tile(a, maps, nt, buf, &bars[st]);
         }
         // epilogue: thread r < 16 finishes row row0 + r
         unsigned long long key = 0ull;
@@ -317,7 +332,7 @@ bool launch_gemv_mma(const GemvArgs& in, cudaStream_t st, bool* handled) {
                                  (in.norm == NORM_LAYER && reinterpret_cast<uintptr_t>(in.norm_b) % 16 != 0)))
         return true;
     if (reinterpret_cast<uintptr_t>(in.x) % 16 != 0) return true;
-    const size_t smem = kStages * stage + x_smem(in.K);
+    const size_t smem = kStages * stage + x_smem(in.K) + 128;    // + alignment slack
     if (smem > kSmemLimit) return true;
     GemvArgs a = in;
     uint32_t tiles = 0;
@@ -336,8 +351,18 @@ bool launch_gemv_mma(const GemvArgs& in, cudaStream_t st, bool* handled) {
     if (per_sm < 1) per_sm = 1;
     uint32_t grid = (uint32_t)sm_count() * per_sm;
     if (grid > tiles) grid = tiles;
+    // one TMA tensor copy per tile for padded rows (bulk copies per row if the
+    // driver refuses a map)
+    GemvMaps maps = {};
+    for (uint32_t i = 0; i < a.nseg; i++) {
+        const GemvSeg& g = a.seg[i];
+        const bool glu = g.epi == EPI_GLU_SILU || g.epi == EPI_GLU_GELU;
+        if (padded_rows(g.row_bytes)) maps.has[i][0] = encode_tile_map(&maps.m[i][0], g.w, g.row_bytes, g.rows);
+        if (glu && padded_rows(g.row_bytes2))
+            maps.has[i][1] = encode_tile_map(&maps.m[i][1], g.w2, g.row_bytes2, g.rows);
+    }
     *handled = true;
-    return LM_CUDA(launch_k(gemv_mma_kernel, dim3(grid), dim3(kMThreads), smem, st, a, (uint32_t)stage));
+    return LM_CUDA(launch_k(gemv_mma_kernel, dim3(grid), dim3(kMThreads), smem, st, a, (uint32_t)stage, maps));
 }
 
 }  // namespace lm

@@ -344,6 +344,28 @@ __host__ __device__ __forceinline__ uint32_t up_offset(const GemvSeg& G) { retur
 __host__ __device__ __forceinline__ uint32_t rows_tx(uint64_t rb, uint32_t nrows) {
     return smem_rs(rb) == rb ? align16((uint64_t)nrows * rb) : (uint32_t)(nrows * rb);
 }
+// Rows copied through a tensor map: an even number of 16-byte units (their
+// shared-memory stride is padded by one unit). Copying such rows one bulk copy
+// per row is slow (the copy engine handles small copies at a few GB/s per SM),
+// so their tiles move as one TMA tensor copy whose box is a unit wider than
+// the row (encode_tile_map), which lands the rows at the padded stride.
+__host__ __device__ __forceinline__ bool padded_rows(uint64_t rb) { return smem_rs(rb) != rb; }
+
+// TMA tensor copy of one 16-row tile: box {8 halves, units + 1, 16 rows} of a
+// rank-3 view {8, units per row, rows} at row row0, written densely; the extra
+// unit and rows past the end read as zeros. dst 128-byte aligned. No multicast.
+__device__ __forceinline__ void tma_tile(void* dst, const CUtensorMap* map, int32_t row0, uint64_t* bar) {
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3, %4}], [%5];\n"
+                 ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(0), "r"(row0),
+                   "r"(smem_u32(bar)) : "memory");
+}
+// Bytes one tile of rows of rb bytes brings into shared memory (a tensor copy
+// delivers the whole box).
+__host__ __device__ __forceinline__ uint32_t tile_tx(uint64_t rb, uint32_t nrows, bool tensor) {
+    return tensor ? 16u * (uint32_t)smem_rs(rb) : rows_tx(rb, nrows);
+}
+
 // One thread: copy rows [0, nrows) at src (row size rb) into dst at stride smem_rs(rb).
 __device__ __forceinline__ void copy_rows(uint8_t* dst, const uint8_t* src, uint64_t rb, uint32_t nrows,
                                           uint64_t* bar) {
