@@ -82,8 +82,10 @@ int llamini_gemv_device(u32 type, const void* d_w, u32 rows, u32 cols,
  * <= 256, head_dim <= 256; larger requests fail with -1 and a message. The
  * counters start at zero and every call returns them to zero. The first call
  * on a device does the set-up (scratch address, kernel attribute) and should
- * come before any stream capture. Calls that overlap in time on one device
- * (two streams, or unordered host threads) share the scratch and race. */
+ * come before any stream capture; it is kept for the life of the process, so
+ * it does not survive a cudaDeviceReset of that device by the application.
+ * Calls that overlap in time on one device (two streams, or unordered host
+ * threads) share the scratch and race. */
 int llamini_causal_mha_noalloc(const f32* d_q, const f32* d_key, const f32* d_val, f32* d_out,
                                u32 pos, u32 n_heads, u32 n_heads_kv, u32 head_dim, void* stream);
 

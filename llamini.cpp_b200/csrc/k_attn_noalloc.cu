@@ -32,6 +32,7 @@
 
 #include <cuda_runtime.h>
 #include <math.h>
+#include <mutex>
 
 namespace lm {
 namespace {
@@ -49,6 +50,7 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) float g_scratch[kScratchFloats];
 
 float* g_base[kMaxDevices];                      // per-device address of g_scratch
+std::mutex g_base_mu;                            // first calls from several host threads
 
 struct NoAllocArgs {
     const float* q;        // [n_heads * hd]
@@ -194,6 +196,7 @@ size_t smem_bytes(uint32_t hd) { return ((size_t)(hd + 1) * (1 + 2 * kChunk) + k
 // Once per device, with that device current: the scratch address and the
 // kernel's shared-memory limit. No allocation.
 float* scratch_base(int dev) {
+    std::lock_guard<std::mutex> lock(g_base_mu);
     if (g_base[dev]) return g_base[dev];
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);

@@ -48,6 +48,35 @@ def test_dequant_rejects_misaligned_count(gpu):
     assert gpu.lib().llamini_dequant_host(12, gpu.ptr(np.zeros(200, np.uint8)), 300, gpu.ptr(out)) == -1
 
 
+@pytest.mark.parametrize("name,row_len,rows", [("blk.0.attn_q.weight", 2048, (0, 64)),         # Q4_K
+                                               ("blk.1.ffn_down.weight", 5632, (32, 96)),     # Q4_K
+                                               ("blk.0.ffn_down.weight", 5632, (2000, 2048)),  # Q6_K
+                                               ("output.weight", 2048, (31936, 32000))])      # Q6_K
+def test_gguf_dequantize_rows_workload_vs_reference(gpu, orc, synth, name, row_len, rows):
+    """gguf_dequantize_rows (gguf.c:602-605) through the drop-in C-ABI on the
+    llama_1b file's quantized tensors: bit-identical to the reference build's
+    own gguf_dequantize_rows on the same file and rows."""
+    ref = orc.reference()
+    if ref is None:
+        pytest.skip("reference build not present (make -C oracle ref)")
+    path = synth.ensure_workload("llama_1b")
+    L = gpu.lib()
+    gf = gpu.GGUFFile()
+    assert L.gguf_open(path.encode(), C.byref(gf)) == 0
+    try:
+        ti = L.gguf_find_tensor(C.byref(gf), name.encode())
+        assert ti
+        r0, r1 = rows
+        got = np.full((r1 - r0) * row_len, np.nan, np.float32)
+        assert L.gguf_dequantize_rows(C.byref(gf), ti, r0, r1, row_len, gpu.ptr(got)) == 0, gpu.last_error()
+        assert ref.drv_open_file(path.encode()) == 0
+        want = np.zeros_like(got)
+        assert ref.drv_dequant_rows(name.encode(), r0, r1, row_len, orc.ptr(want)) == 0
+        assert same_bits(got, want)
+    finally:
+        L.gguf_close(C.byref(gf))
+
+
 def _orc_linear(orc, t, raw, rows, cols, x):
     m = orc.OrcMat(t, rows, cols, raw.ctypes.data)
     y = np.zeros(rows, np.float32)
@@ -121,7 +150,8 @@ def test_ops_reference_kats(gpu, golden):
     L, k = gpu.lib(), golden["kat"]
     x = np.array([1, 2, 3, 4], np.float32)
     o = np.zeros(4, np.float32)
-    L.rms_norm(gpu.ptr(o), gpu.ptr(x), gpu.ptr(np.ones(4, np.float32)), 4, 1e-8)
+    w = np.ones(4, np.float32)                 # held for the call: ptr() keeps no reference
+    L.rms_norm(gpu.ptr(o), gpu.ptr(x), gpu.ptr(w), 4, 1e-8)
     np.testing.assert_allclose(o, k["rms_norm"], rtol=1e-6)
     for neox, key in ((0, "rope_norm"), (1, "rope_neox")):
         v = np.ones(8, np.float32)

@@ -32,7 +32,8 @@ def test_oracle_kats(orc, golden):
     k = golden["kat"]
     x = np.array([1, 2, 3, 4], np.float32)
     o = np.zeros(4, np.float32)
-    L.orc_rms_norm(orc.ptr(o), orc.ptr(x), orc.ptr(np.ones(4, np.float32)), 4, np.float32(1e-8))
+    w = np.ones(4, np.float32)                 # held for the call: ptr() keeps no reference
+    L.orc_rms_norm(orc.ptr(o), orc.ptr(x), orc.ptr(w), 4, np.float32(1e-8))
     assert np.array_equal(o, np.array(k["rms_norm"], np.float32))
     for neox, key in ((0, "rope_norm"), (1, "rope_neox")):
         v = np.ones(8, np.float32)
