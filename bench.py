@@ -440,10 +440,7 @@ def run_ours(args, ws, rank, local):
             "steps": steps, "warmup": args.warmup, "ms_per_step": round(t_max / steps, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
-            "config": {"workload": "llama_1b: LLaMA 1.1B shape (22 layers, dim 2048, 32/4 heads, ffn 5632, "
-                                   "vocab 32000), Q4_K_M mix, seed 0; batch 1 per GPU; 128-token prompt, "
-                                   "timed decode positions %d..%d" % (pos0, pos0 + steps - 1) +
-                                   ("" if n_prompt == N_PROMPT else " (prompt %d)" % n_prompt),
+            "config": {"workload": decode_workload(n_prompt, pos0, steps),
                        "global_batch": ws, "seq_len": pos0 + steps, "parallelism": "replicas x%d" % ws,
                        "l2": "weights %.0f MB > 126 MB L2, streamed every step" % (weight_bytes / 1e6)},
             "weight_stream_gbs": round(step_bytes / step_s / 1e9, 1),
@@ -507,6 +504,13 @@ def run_ours(args, ws, rank, local):
         dist.destroy_process_group()
 
 
+def decode_workload(n_prompt, pos0, steps):
+    """The batch-1 decode workload as both arms name it in `config`."""
+    return ("llama_1b: LLaMA 1.1B shape (22 layers, dim 2048, 32/4 heads, ffn 5632, vocab 32000), Q4_K_M mix, "
+            "seed 0; batch 1 per GPU; %d-token prompt, timed decode positions %d..%d" % (n_prompt, pos0,
+                                                                                         pos0 + steps - 1))
+
+
 # --------------------------------------------------------------------------- reference (CPU)
 
 def _ref_lib():
@@ -552,28 +556,35 @@ def run_reference(args, ws, rank, local):
     path = synthetic().ensure_workload(WORKLOAD)
     os.environ.setdefault("LLAMINI_THREADS", str(os.cpu_count()))
     assert ref.drv_open(path.encode(), 0) == 0
-    prompt = synthetic().workload_prompt(WORKLOAD, 4)
-    for p in range(4):
+    # the GPU arm's context: the same prompt, fed token by token as the
+    # reference's generate does (generate.c:141-150, untimed), then greedy-fed
+    # decode steps from the prompt's last position
+    n_prompt = args.prompt
+    prompt = synthetic().workload_prompt(WORKLOAD, n_prompt)
+    for p in range(n_prompt - 1):
         ref.drv_time_decode(p, int(prompt[p]), 1, None)
-    pos = 4
+    out = np.zeros(1, np.uint32)
+    pos, tok = n_prompt - 1, int(prompt[n_prompt - 1])
     for _ in range(args.warmup):
-        ref.drv_time_decode(pos, 5, 1, None)
-        pos += 1
+        ref.drv_time_decode(pos, tok, 1, O.ptr(out))
+        tok, pos = int(out[0]), pos + 1
     # each step is one decode token; stop early (and say so) past ~240 s
     el, n = 0.0, 0
     while n < args.steps and el < 240.0:
-        el += ref.drv_time_decode(pos, 5, 1, None)
-        pos += 1
+        el += ref.drv_time_decode(pos, tok, 1, O.ptr(out))
+        tok, pos = int(out[0]), pos + 1
         n += 1
     ref.drv_close()
     value = n / el
-    sample = "%d of %d requested decode steps of llama_1b (positions %d..%d, 4-token prompt), single-threaded " \
-             "lazy Q4_K path (model.c:147-158)" % (n, args.steps, pos - n, pos - 1)
+    sample = "%d of %d requested decode steps of llama_1b at positions %d..%d after the %d-token prompt (the GPU " \
+             "arm's context, greedy-fed), single-threaded lazy Q4_K path (model.c:147-158)" % (
+                 n, args.steps, pos - n, pos - 1, n_prompt)
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "tok/s", "n_gpus": ws,
             "steps": n, "warmup": args.warmup, "ms_per_step": round(el / n * 1e3, 2), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "llama_1b decode, batch 1, reference CPU path", "global_batch": 1,
-                       "seq_len": pos, "parallelism": "none"},
+            "config": {"workload": decode_workload(n_prompt, pos - n, n), "global_batch": 1, "seq_len": pos,
+                       "parallelism": "replicas x1", "l2": "the reference reads its weights from the host "
+                                                                 "memory map every step (no GPU)"},
             "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": 1, "kind": "reference",
                              "sample": sample},
             "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
