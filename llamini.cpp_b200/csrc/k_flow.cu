@@ -71,6 +71,12 @@ struct FlowShared {
     uint32_t off[kQ];
     float part[2][kCW][2][16];           // per buffer, warp, (main | up) and row
     uint32_t consumed, issued, abort, epoch;
+    // Producer gate: a GPU-scope release waits for every bulk copy the SM has
+    // in flight (about a microsecond while the weight stream runs), so from the
+    // start of an op's last tile in this CTA until that op's release the
+    // producer issues nothing past tile gate_until. gate_set counts gates
+    // requested (consumer thread 0), gate_clr releases done.
+    uint32_t gate_set, gate_clr, gate_until;
 };
 
 __device__ __forceinline__ void bar_sync(uint32_t id, uint32_t n) {
@@ -685,7 +691,9 @@ __device__ void producer(const FlowArgs& a, FlowShared& S, uint8_t* ring) {
             for (uint32_t w = 0;; w++) {
                 const uint32_t c = vload(&S.consumed);
                 const uint64_t tail = c == 0 ? 0ull : S.vend[(c - 1) % kQ];
-                if (seq - c < kQ && head + alloc - tail <= R) { ok = true; break; }
+                const bool gated = vload(&S.gate_set) != vload(&S.gate_clr) &&
+                                   (int32_t)(seq - vload(&S.gate_until)) > 0;
+                if (seq - c < kQ && head + alloc - tail <= R && !gated) { ok = true; break; }
                 __nanosleep(64);                  // leave the SM's issue slots to the other warps
                 if ((w & 63u) == 63u && (aborted(a, S) || gtime() - t0 > kWaitNs)) break;
             }
@@ -719,6 +727,7 @@ __device__ void consumer(const FlowArgs& a, FlowShared& S, uint8_t* ring, float*
     const uint32_t n_my = a.sched_len[blockIdx.x];
     const FlowOp& op = S.cop;
     uint32_t cseq = 0;
+    uint32_t gset = 0;                   // gates requested (thread 0)
     uint8_t* xs = reinterpret_cast<uint8_t*>(stage) + warp * kXsWarpBytes;   // this warp's fragments
     uint32_t nsb = 0;
     for (uint32_t j = 0; j < a.n_steps; j++) {
@@ -767,6 +776,11 @@ __device__ void consumer(const FlowArgs& a, FlowShared& S, uint8_t* ring, float*
             }
             if (gemv) {
                 const uint32_t b = cseq & 1u;
+                if (tid == 0 && (i + 1 == n_my || (S.tasks[i + 1] >> 16) != op_i)) {
+                    // this CTA's last tile of the op: no new copies until its release
+                    vstore(&S.gate_until, cseq);
+                    vstore(&S.gate_set, ++gset);
+                }
                 bar_sync(kBarFree + b, kPairT);          // partial buffer b was read
                 const uint32_t q = cseq % kQ;
                 bool ok = false;
@@ -812,6 +826,10 @@ __device__ void consumer(const FlowArgs& a, FlowShared& S, uint8_t* ring, float*
                 bar_arrive(kBarDone + b, kPairT);        // partials of buffer b ready
                 cseq++;
             } else {
+                if (tid == 0 && (i + 1 == n_my || (S.tasks[i + 1] >> 16) != op_i)) {
+                    vstore(&S.gate_until, cseq);          // the next GEMV tile may still come
+                    vstore(&S.gate_set, ++gset);
+                }
                 if (!cbar_or(stopped(S))) {
                     if (op.at.kv_f16) attn_task<__half>(a, op, task, stage, prefetched, tid);
                     else attn_task<float>(a, op, task, stage, prefetched, tid);
@@ -821,6 +839,7 @@ __device__ void consumer(const FlowArgs& a, FlowShared& S, uint8_t* ring, float*
                 if (last) {
                     cbar();                               // every thread's partials are written
                     if (tid == 0 && !stopped(S)) signal(&a.done[op_i], run_n);
+                    if (tid == 0) atomicAdd(&S.gate_clr, 1u);
                 }
             }
         }
@@ -943,6 +962,7 @@ __device__ void epilogue(const FlowArgs& a, FlowShared& S, uint32_t lane) {
                     if (__shfl_sync(0xffffffffu, fin, 0)) finish_step(a, lane);
                 }
             }
+            if (last && lane == 0) atomicAdd(&S.gate_clr, 1u);    // the op is released: copies may go
         }
     }
 }
@@ -958,6 +978,9 @@ __global__ void __launch_bounds__(kFT, 1) flow_kernel(const __grid_constant__ Fl
         for (uint32_t q = 0; q < kQ; q++) mbar_init(&S.bar[q], 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         S.consumed = 0;
+        S.gate_set = 0;
+        S.gate_clr = 0;
+        S.gate_until = 0;
         S.issued = 0;
         S.abort = vload(&a.sync->abort);
         S.epoch = ld_acq(&a.sync->epoch);
