@@ -302,13 +302,43 @@ def run_tp7b(args, lm, L, torch, ws, rank, dist, hbm_peak):
         e1.record(stream)
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
-        tk = np.zeros(4, np.uint32)
-        assert L.llamini_session_tokens(s, lm.ptr(tk), 4) >= 0, lm.last_error()   # no step reported an error
+        # every rank's decoded tokens (the first 16 after the prompt) must be
+        # bit-identical: a rank whose shard or sum went wrong decodes differently
+        n_tok = TP_PROMPT + 16
+        tk = np.zeros(n_tok, np.uint32)
+        assert L.llamini_session_tokens(s, lm.ptr(tk), n_tok) >= n_tok, lm.last_error()
+        mine = tk[TP_PROMPT:].astype(np.int64)
+        if ws > 1:
+            t_mine = torch.from_numpy(mine).cuda()
+            t_all = [torch.zeros_like(t_mine) for _ in range(ws)]
+            dist.all_gather(t_all, t_mine)
+            per_rank = [x.cpu().numpy() for x in t_all]
+        else:
+            per_rank = [mine]
+        identical = all(np.array_equal(per_rank[0], x) for x in per_rank)
+        if not identical:
+            raise SystemExit("tp_7b: ranks decoded different tokens: %s" % [x.tolist() for x in per_rank])
+        # the reference's own greedy stream of this file (64-token prompt,
+        # tests/golden/tokens.json, made by the reference's C): the sharded
+        # decode must reproduce it token for token
+        golden = None
+        gpath = os.path.join(ROOT, "tests", "golden", "tokens.json")
+        g = json.load(open(gpath)).get("llama_7b") if os.path.exists(gpath) else None
+        if g is not None:
+            gp = np.asarray(g["prompt"], np.uint32)
+            n_g = len(g["tokens"])
+            assert L.llamini_session_begin(s, lm.ptr(gp), len(gp)) == 0, lm.last_error()
+            assert L.llamini_session_step(s, n_g - 1) == 0, lm.last_error()
+            got = np.zeros(n_g, np.uint32)
+            assert L.llamini_session_tokens(s, lm.ptr(got), n_g) >= n_g, lm.last_error()
+            golden = bool(np.array_equal(got, np.asarray(g["tokens"], np.uint32)))
+            if not golden:
+                raise SystemExit("tp_7b: rank %d's stream differs from the reference's llama_7b golden stream" % rank)
         wb = L.llamini_session_weight_bytes(s)
         kvp = L.llamini_session_kv_bytes_per_pos(s)
     finally:
         m.close()
-    return ms, wb, kvp, pos0
+    return ms, wb, kvp, pos0, per_rank[0].tolist(), golden
 
 
 def run_perplexity(lm, L, model, n_tok=1024):
@@ -494,6 +524,8 @@ def run_ours(args, ws, rank, local):
                 "per_gpu_bytes_per_step": int(tp_bytes),
                 "per_gpu_stream_gbs": round(tp_bytes / t_step_s / 1e9, 1),
                 "frac_of_hbm": round(tp_bytes / t_step_s / 1e9 / hbm_peak, 4),
+                "tokens_after_prompt": tp7[4], "tokens_rank_identical": True,
+                "reference_stream_match": tp7[5],
                 # embed, 5 per layer (+ 2 allreduces per layer when split), lm_head, finish
                 "gpu_launches": args.tp_steps * (1 + 32 * (5 + (2 if ws > 1 else 0)) + 2)}
         if ws == 1 and not args.no_cpu_baseline:

@@ -54,6 +54,13 @@ u64 llamini_type_bytes(u32 type, u64 n_elems);
  * out, on the GPU. Bit-identical to gguf.c:409-594. */
 int llamini_dequant_host(u32 type, const void* blocks, u64 n_elems, f32* out);
 
+/* One sample_token draw (generate.c:25-60) by the device sampler that the
+ * sampled generate path uses: logits in host memory (vocab floats), temp > 0,
+ * top_p, and u = rand() / (RAND_MAX + 1) as the reference computes it (the
+ * caller draws it, so the host rand() stream is consumed in the reference's
+ * order). Returns the token id, or 0xFFFFFFFF on error. */
+u32 llamini_sample_host(const f32* logits, u32 vocab, f32 temp, f32 top_p, f32 u);
+
 /* Same decode between device buffers, enqueued on llamini_stream(). */
 int llamini_dequant_device(u32 type, const void* d_blocks, u64 n_elems, f32* d_out);
 
@@ -208,6 +215,13 @@ int llamini_tp_handle(void* out64);
  * arrive within 2 s sets the session's error). world = 1 leaves the group setting
  * at one rank. Batched sessions are refused in a group. */
 int llamini_tp_join(u32 rank, u32 world, const void* handles);
+/* The shard a LLaMA session of rank `rank` in a group of `world` holds (the
+ * plan llamini_tp_join's sessions use; no device needed): out[0..8) = {first
+ * head, end head, first kv head, end kv head, first FFN column, end FFN column,
+ * first o-proj column, end o-proj column}. FFN columns split on 256-column
+ * super-block boundaries as evenly as they allow (first = 256 * floor(n_sb *
+ * rank / world)). Returns 0, or -1 when the shapes do not split. */
+int llamini_tp_plan(u32 world, u32 rank, u32 n_heads, u32 n_kv, u32 head_dim, u32 ffn, u32* out);
 int llamini_tp_rank(void);
 int llamini_tp_world(void);
 

@@ -142,6 +142,7 @@ SIGNATURES = {
     "llamini_release": (None, []),
     "llamini_type_bytes": (u64, [u32, u64]),
     "llamini_dequant_host": (C.c_int, [u32, P, u64, P]),
+    "llamini_sample_host": (u32, [P, u32, f32, f32, f32]),
     "llamini_dequant_device": (C.c_int, [u32, P, u64, P]),
     "llamini_gemv_host": (C.c_int, [u32, P, u32, u32, P, u32, P]),
     "llamini_gemv_device": (C.c_int, [u32, P, u32, u32, P, u32, P]),
@@ -166,6 +167,7 @@ SIGNATURES = {
     "llamini_session_prefill": (C.c_int, [P]),
     "llamini_tp_handle": (C.c_int, [P]),
     "llamini_tp_join": (C.c_int, [C.c_uint32, C.c_uint32, P]),
+    "llamini_tp_plan": (C.c_int, [u32, u32, u32, u32, u32, u32, P]),
     "llamini_tp_rank": (C.c_int, []),
     "llamini_tp_world": (C.c_int, []),
     "llamini_batch_free": (None, [P]),
@@ -255,14 +257,17 @@ class Model:
         self._closed = False
 
     # reference-API calls -------------------------------------------------
-    def generate(self, prompt, max_gen: int, eos: int = 0xFFFFFFFF) -> np.ndarray:
+    def generate(self, prompt, max_gen: int, eos: int = 0xFFFFFFFF, temp: float = 0.0,
+                 top_p: float = 0.0) -> np.ndarray:
+        """generate_autoregressive (generate.c:122-167); temp > 0 samples with
+        the process's rand() stream, as the reference does."""
         L = lib()
         p = np.ascontiguousarray(prompt, dtype=np.uint32)
         out = np.zeros(len(p) + max_gen + 1, dtype=np.uint32)
         for i in range(self.n_layers):
             L.kv_cache_reset(C.byref(self.caches[i]))
         fn = L.gpt2_generate if self.is_gpt2 else L.generate_autoregressive
-        n = fn(C.byref(self.model), self.caches, ptr(p), len(p), ptr(out), max_gen, eos, 0.0, 0.0)
+        n = fn(C.byref(self.model), self.caches, ptr(p), len(p), ptr(out), max_gen, eos, temp, top_p)
         return out[:n]
 
     def forward(self, pos: int, token: int) -> np.ndarray:

@@ -322,6 +322,12 @@ bool encode_tile_map(CUtensorMap* m, const uint8_t* w, uint64_t row_bytes, uint3
 bool launch_flow(const FlowArgs& a, cudaStream_t st);
 bool launch_flow_embed(const FlowArgs& a, cudaStream_t st);
 
+// sample_token (generate.c:25-60) on the device (k_sample.cu): one draw from
+// the logits at d_logits with u = rand() / (RAND_MAX + 1) drawn by the caller;
+// the token id is written to *d_tok. d_scratch holds vocab floats.
+bool launch_sample(const float* d_logits, uint32_t vocab, float temp, float top_p, float u, float* d_scratch,
+                   uint32_t* d_tok, cudaStream_t st);
+
 // ---------------------------------------------------------------- batched GEMM
 // Up to 64 input vectors per weight pass (k_bgemm.cu): staging per sequence,
 // split-K dequant GEMM into raw partials, per-(sequence, row) finish.

@@ -67,6 +67,7 @@ struct llamini_session {
     // buffers (device)
     std::vector<void*> owned;
     float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *ffn_h = nullptr, *logits = nullptr;
+    float* probs = nullptr;               // the device sampler's scratch (vocab floats)
     float *part = nullptr, *trace = nullptr;
     float* tp_part = nullptr;           // tensor parallel: this rank's o / down partial sums
     u32 tp_world = 1;                   // ranks the weights are split over
@@ -153,6 +154,29 @@ const float* vec(llamini_session* s, const Tensor* t, u32 n) {
     return upload_f32(s, t->data, n);
 }
 
+// The shard of rank R of W: heads [R H/W, (R+1) H/W) and the matching kv heads
+// (so the o-proj columns are the rank's heads), FFN columns [f0, f1) on
+// 256-column super-block boundaries, split as evenly as the super-blocks allow
+// (f0 = 256 floor(nsb R / W)). out = {head0, head1, kv0, kv1, f0, f1, ocol0,
+// ocol1}; -1 with an error when the shapes do not split.
+int tp_plan(u32 W, u32 R, u32 n_heads, u32 n_kv, u32 hd, u32 ffn, u32* out) {
+    if (W == 0 || R >= W || n_heads == 0 || n_kv == 0 || n_heads % W != 0 || n_kv % W != 0 || ffn % 256 != 0 ||
+        ffn / 256 < W) {
+        set_error("tensor parallel over %u ranks: heads %u, kv heads %u, ffn %u do not split", W, n_heads, n_kv, ffn);
+        return -1;
+    }
+    const u32 hw = n_heads / W, kw = n_kv / W, nsb = ffn / 256;
+    out[0] = R * hw;
+    out[1] = (R + 1) * hw;
+    out[2] = R * kw;
+    out[3] = (R + 1) * kw;
+    out[4] = 256 * (u32)((uint64_t)nsb * R / W);
+    out[5] = 256 * (u32)((uint64_t)nsb * (R + 1) / W);
+    out[6] = R * hw * hd;
+    out[7] = (R + 1) * hw * hd;
+    return 0;
+}
+
 // Tensor parallelism: keep rows [r0, r0 + n) of m (a view, no copy).
 void shard_rows(llamini_session* s, DevMat* m, u32 r0, u32 n) {
     s->weight_bytes -= m->row_bytes * (m->rows - n);
@@ -185,6 +209,7 @@ bool alloc_buffers(llamini_session* s) {
     s->attn = (float*)own(s, (size_t)s->qd * 4);
     s->ffn_h = (float*)own(s, (size_t)s->ffn * 4);
     s->logits = (float*)own(s, (size_t)s->vocab * 4);
+    s->probs = (float*)own(s, (size_t)s->vocab * 4);
     s->part = (float*)own(s, (size_t)s->n_heads * s->n_split * (s->hd + 4) * 4);
     s->trace = (float*)own(s, (size_t)L * s->dim * 4);
     s->counters = (u32*)own(s, (size_t)s->n_heads * 4);
@@ -194,7 +219,7 @@ bool alloc_buffers(llamini_session* s) {
     s->vc = own(s, kv_bytes);
     s->st = (StepState*)own(s, sizeof(StepState));
     if (s->tp_world > 1 && !(s->tp_part = (float*)own(s, (size_t)s->dim * 4))) return false;
-    if (!s->hidden || !s->qkv || !s->attn || !s->ffn_h || !s->logits || !s->part || !s->trace ||
+    if (!s->hidden || !s->qkv || !s->attn || !s->ffn_h || !s->logits || !s->probs || !s->part || !s->trace ||
         !s->counters || !s->tokens || !s->kc || !s->vc || !s->st)
         return false;
     if (!LM_CUDA(cudaMallocHost((void**)&s->st_host, sizeof(StepState)))) return false;
@@ -774,18 +799,14 @@ bool bind_llama(llamini_session* s, LLaMAModel* m, u32 max_seq) {
     u32 f0 = 0, f1 = c.ffn_dim;
     if (ok && W > 1) {
         s->tp_world = W;
-        if (s->n_heads % W != 0 || s->n_kv % W != 0 || c.ffn_dim % 256 != 0 || c.ffn_dim / 256 < W) {
-            set_error("tensor parallel over %u ranks: heads %u, kv heads %u, ffn %u do not split", W, s->n_heads, s->n_kv,
-                      c.ffn_dim);
-            return false;
-        }
+        u32 plan[8];
+        if (tp_plan(W, R, s->n_heads, s->n_kv, s->hd, c.ffn_dim, plan) != 0) return false;
         s->n_heads /= W;
         s->n_kv /= W;
         s->qd /= W;
         s->kvd /= W;
-        const u32 nsb = c.ffn_dim / 256;
-        f0 = 256 * (u32)((uint64_t)nsb * R / W);
-        f1 = 256 * (u32)((uint64_t)nsb * (R + 1) / W);
+        f0 = plan[4];
+        f1 = plan[5];
         s->ffn = f1 - f0;
     }
     ok = ok && weight(s, m->embeddings, c.vocab_size, c.dim, &s->tok);
@@ -1029,14 +1050,28 @@ static u32 generate(llamini_session* s, u32* input, u32 n_in, u32* out, u32 max_
     u32 total = n_in;
     cudaStream_t st = stream();
     if (temp > 0.0f) {
-        // sampled decoding: the draw uses the host rand() stream (generate.c:50)
-        std::vector<f32> logits(s->vocab);
-        for (u32 pos = 0; pos < s->max_pos; pos++) {
-            forward_one(s, pos, out[pos], logits.data());
-            if (pos + 1 < n_in) continue;
-            u32 t = sample_token(logits.data(), s->vocab, temp, top_p);
-            out[total++] = t;
-            if (t == eos || total - n_in >= max_gen) break;
+        // Sampled decoding (generate.c:122-167 with sample_token): the prompt as
+        // in the greedy path, then per token one step, one draw from the host
+        // rand() stream (generate.c:50; one per token, in the reference's order)
+        // and the device sampler (k_sample.cu), whose pick is the next step's
+        // input; only the token comes back to the host.
+        const u32 first = n_in > 0 ? n_in : 1;
+        if (!write_state(s, 0, first, true)) return total;
+        if (!LM_CUDA(cudaMemcpyAsync(s->tokens, out, (size_t)first * 4, cudaMemcpyHostToDevice, st))) return total;
+        u32 pre = n_in > 1 ? n_in - 1 : 0;
+        if (pre > s->max_pos) pre = s->max_pos;
+        if (pre && !run_prompt(s, pre)) return total;
+        u32 tok = 0;
+        while (s->pos < s->max_pos) {
+            const f32 u = (f32)rand() / ((f32)RAND_MAX + 1.0f);
+            const u32 p = s->pos;
+            if (!run_steps(s, 1)) break;
+            if (!launch_sample(s->logits, s->vocab, temp, top_p, u, s->probs, s->tokens + p + 1, st) ||
+                !LM_CUDA(cudaMemcpyAsync(&tok, s->tokens + p + 1, 4, cudaMemcpyDeviceToHost, st)) ||
+                !LM_CUDA(cudaStreamSynchronize(st)))
+                break;
+            out[total++] = tok;
+            if (tok == eos || total - n_in >= max_gen) break;
         }
     } else {
         // Forward passes the reference runs without an early EOS: every prompt
@@ -1150,6 +1185,7 @@ struct llamini_batch {
     u32 max_batch = 0, max_seq = 0, B = 0;
     u32 n_split = 1, kv_f16 = 0, kmax = 0;
     float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *ffn_h = nullptr, *logits = nullptr;
+    float* probs = nullptr;               // the device sampler's scratch (vocab floats)
     float *sx = nullptr, *part = nullptr, *part2 = nullptr, *part3 = nullptr, *apart = nullptr;
     uint16_t *xh = nullptr, *xl = nullptr;
     u32 *counters = nullptr, *tokens = nullptr, *n_prompt = nullptr;
@@ -2304,6 +2340,10 @@ int llamini_tp_join(u32 rank, u32 world, const void* handles) {
     return 0;
 }
 
+int llamini_tp_plan(u32 world, u32 rank, u32 n_heads, u32 n_kv, u32 head_dim, u32 ffn, u32* out) {
+    if (!out) { lm::set_error("tp_plan: null output"); return -1; }
+    return lm::tp_plan(world, rank, n_heads, n_kv, head_dim, ffn, out);
+}
 int llamini_tp_rank(void) { return (int)lm::tp().rank; }
 int llamini_tp_world(void) { return (int)lm::tp().world; }
 

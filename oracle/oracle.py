@@ -107,6 +107,10 @@ def _bind_driver(L: C.CDLL) -> C.CDLL:
     L.drv_forward.argtypes = [u32, u32, P]
     L.drv_generate.argtypes = [P, u32, P, u32, u32]
     L.drv_generate.restype = u32
+    L.drv_generate_sampled.argtypes = [P, u32, P, u32, u32, f32, f32, u32]
+    L.drv_generate_sampled.restype = u32
+    L.sample_token.argtypes = [P, u32, f32, f32]
+    L.sample_token.restype = u32
     L.drv_perplexity.argtypes = [P, u32]
     L.drv_perplexity.restype = f32
     L.drv_time_decode.argtypes = [u32, u32, u32, P]

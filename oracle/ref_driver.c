@@ -106,6 +106,15 @@ u32 drv_generate(u32* prompt, u32 n_prompt, u32* out, u32 max_gen, u32 eos) {
     return generate_autoregressive(&g_llama, g_caches, prompt, n_prompt, out, max_gen, eos, 0.0f, 0.0f);
 }
 
+/* generate_autoregressive / gpt2_generate with sampling (temp > 0): srand(seed)
+ * first, so the draws are rand()'s stream from that seed (generate.c:50). */
+u32 drv_generate_sampled(u32* prompt, u32 n_prompt, u32* out, u32 max_gen, u32 eos, f32 temp, f32 top_p, u32 seed) {
+    drv_reset();
+    srand(seed);
+    if (g_is_gpt2) return gpt2_generate(&g_gpt2, g_caches, prompt, n_prompt, out, max_gen, eos, temp, top_p);
+    return generate_autoregressive(&g_llama, g_caches, prompt, n_prompt, out, max_gen, eos, temp, top_p);
+}
+
 f32 drv_perplexity(const u32* tokens, u32 n) {
     if (g_is_gpt2) return gpt2_compute_perplexity(&g_gpt2, g_caches, tokens, n);
     return compute_perplexity(&g_llama, g_caches, tokens, n);

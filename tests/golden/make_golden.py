@@ -13,8 +13,10 @@ stores what it returned:
                 and of the llama_1b / gpt2_124m workloads
   logits.npz    full logits of the tiny models at a few positions
 
-Usage: python tests/golden/make_golden.py [--skip-large]
-The llama_1b run takes a few minutes on the single-threaded lazy path.
+Usage: python tests/golden/make_golden.py [--skip-large | --full-size-only]
+The llama_1b run takes a few minutes on the single-threaded lazy path;
+--full-size-only adds the qwen2_05b (512-token prompt) and llama_7b (64-token
+prompt) streams to tokens.json, which takes tens of minutes.
 """
 from __future__ import annotations
 
@@ -128,6 +130,21 @@ def main():
         v = 1000
         prompts.append((tiny.ensure(name), np.random.default_rng(7).integers(3, 500, 16).astype(np.uint32)))
         del v
+    if "--full-size-only" in sys.argv:
+        # the full-size Qwen2-0.5B stream after its 512-token prompt and the
+        # LLaMA-7B-shape stream after a 64-token prompt (tens of minutes on the
+        # single-threaded lazy path), merged into the existing file
+        names, prompts = [], []
+        for name, n_prompt in (("qwen2_05b", 512), ("llama_7b", 64)):
+            names.append(name)
+            prompts.append((S.ensure_workload(name), S.workload_prompt(name, n_prompt)))
+        toks, _ = streams(ref, names, prompts)
+        path = os.path.join(HERE, "tokens.json")
+        old = json.load(open(path))
+        old.update(toks)
+        with open(path, "w") as f:
+            json.dump(old, f)
+        return
     if "--skip-large" not in sys.argv:
         for name, n_prompt in (("gpt2_124m", 64), ("llama_1b", 128)):
             names.append(name)
