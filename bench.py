@@ -263,6 +263,118 @@ def run_batch(args, lm, L, model, torch, stream, ws, rank, dist, hbm_peak):
     return ms, weight_bytes + B * kv_per_pos * ctx_mean, B, tc
 
 
+QWEN_PROMPT, QWEN_STEPS, QWEN_BATCH = 512, 512, 32
+
+
+def run_qwen2(args, lm, L, torch, hbm_peak):
+    """Qwen2-0.5B (24 layers, dim 896, 14/2 heads, ffn 4864, vocab 151936, q/k/v
+    biases, Q5_0 attn_v in odd layers): a 512-token prompt through the chunked
+    tcgen05 prefill, then 512 greedy decode steps at batch 1; and 32 independent
+    sequences, each after its own 512-token prompt, 512 batched steps. Device
+    time of the decode steps (rank 0 only)."""
+    S = synthetic()
+    path = S.ensure_workload("qwen2_05b", os.environ.get("LLAMINI_WORKDIR", "/tmp/llamini_b200"))
+    m = lm.Model(path, max_seq=QWEN_PROMPT + QWEN_STEPS + 8)
+    try:
+        s = m.session()
+        stream = torch.cuda.ExternalStream(L.llamini_stream())
+        prompt = S.workload_prompt("qwen2_05b", QWEN_PROMPT)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        assert L.llamini_session_begin(s, lm.ptr(prompt), QWEN_PROMPT) == 0, lm.last_error()
+        ev[0].record(stream)
+        assert L.llamini_session_step(s, QWEN_PROMPT - 1) == 0, lm.last_error()
+        ev[1].record(stream)
+        assert L.llamini_session_step(s, QWEN_STEPS) == 0, lm.last_error()
+        ev[2].record(stream)
+        torch.cuda.synchronize()
+        prefill_ms, decode_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+        wb = L.llamini_session_weight_bytes(s)
+        kvp = L.llamini_session_kv_bytes_per_pos(s)
+        step_bytes = wb + kvp * (QWEN_PROMPT + QWEN_STEPS / 2)
+        b1 = {"value": round(QWEN_STEPS / (decode_ms / 1e3), 1), "unit": "tok/s", "batch": 1,
+              "ms_per_step": round(decode_ms / QWEN_STEPS, 4),
+              "weight_stream_gbs": round(step_bytes / (decode_ms / 1e3 / QWEN_STEPS) / 1e9, 1),
+              "frac_of_hbm": round(step_bytes / (decode_ms / 1e3 / QWEN_STEPS) / 1e9 / hbm_peak, 4),
+              "prefill": {"value": round((QWEN_PROMPT - 1) / (prefill_ms / 1e3), 1), "unit": "tok/s",
+                          "positions": QWEN_PROMPT - 1, "path": "tcgen05 GEMM" if L.llamini_session_prefill(s) == 1
+                          else "decode steps"}}
+        B = QWEN_BATCH
+        b = L.llamini_llama_batch(C.byref(m.model), B, QWEN_PROMPT + QWEN_STEPS + 8)
+        if not b:
+            raise RuntimeError("qwen2 batch: " + lm.last_error())
+        try:
+            rng = np.random.default_rng(3)
+            prompts = rng.integers(3, m.vocab, (B, QWEN_PROMPT)).astype(np.uint32)
+            lens = np.full(B, QWEN_PROMPT, np.uint32)
+            assert L.llamini_batch_begin(b, B, lm.ptr(prompts), lm.ptr(lens)) == 0, lm.last_error()
+            ev[0].record(stream)
+            assert L.llamini_batch_step(b, QWEN_PROMPT - 1) == 0, lm.last_error()
+            ev[1].record(stream)
+            assert L.llamini_batch_step(b, QWEN_STEPS) == 0, lm.last_error()
+            ev[2].record(stream)
+            torch.cuda.synchronize()
+            bp_ms, bd_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+            bwb = L.llamini_batch_weight_bytes(b)
+        finally:
+            L.llamini_batch_free(b)
+        bbytes = bwb + B * kvp * (QWEN_PROMPT + QWEN_STEPS / 2)
+        b32 = {"value": round(B * QWEN_STEPS / (bd_ms / 1e3), 1), "unit": "tok/s", "batch": B,
+               "ms_per_step": round(bd_ms / QWEN_STEPS, 4),
+               "frac_of_hbm": round(bbytes / (bd_ms / 1e3 / QWEN_STEPS) / 1e9 / hbm_peak, 4),
+               "prompt_ms": round(bp_ms, 2), "prompt_path": "batched decode steps, one position at a time"}
+    finally:
+        m.close()
+    return {"workload": "qwen2_05b: Qwen2 0.5B shape (24 layers, dim 896, 14/2 heads, ffn 4864, vocab 151936), "
+                        "Q4_K_M mix with Q5_0 attn_v, seed 3; %d-token prompt, %d greedy decode steps" %
+                        (QWEN_PROMPT, QWEN_STEPS), "batch1": b1, "batch32": b32}
+
+
+GEMV_SWEEP = [(2048, 2048), (5632, 2048), (2048, 5632), (32000, 2048), (11008, 4096), (4096, 11008)]
+GEMV_TYPES = [("Q4_0", 2), ("Q4_1", 3), ("Q5_0", 6), ("Q8_0", 8), ("Q4_K", 12), ("Q5_K", 13), ("Q6_K", 14)]
+
+
+def run_gemv_sweep(lm, L, torch, stream, hbm_peak):
+    """The isolated fused dequant-GEMV sweep: every shape x format x batch
+    {1, 8, 64} (seed 1 blocks), y = W x through llamini_gemv_device. Each
+    timing cycles over copies of W totalling more than the 126 MB L2, so every
+    launch streams its weights from HBM. GB/s = (weight + x + y bytes) per
+    launch / device time per launch."""
+    S = synthetic()
+    table = {}
+    for tname, t in GEMV_TYPES:
+        row = {}
+        for rows, cols in GEMV_SWEEP:
+            raw = S.random_blocks(np.random.default_rng(1), t, rows * cols)
+            nb = raw.size
+            copies = max(2, -(-(256 << 20) // nb))
+            w = torch.empty((copies, nb + 16), dtype=torch.uint8, device="cuda")
+            w[0, :nb].copy_(torch.from_numpy(raw))
+            for i in range(1, copies):
+                w[i].copy_(w[0])
+            res = []
+            for batch in (1, 8, 64):
+                x = torch.randn(batch * cols, device="cuda", dtype=torch.float32)
+                y = torch.empty(batch * rows, device="cuda", dtype=torch.float32)
+                with torch.cuda.stream(stream):
+                    for i in range(min(copies, 4)):
+                        assert L.llamini_gemv_device(t, w[i].data_ptr(), rows, cols, x.data_ptr(), batch,
+                                                     y.data_ptr()) == 0, lm.last_error()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    for i in range(copies):
+                        L.llamini_gemv_device(t, w[i].data_ptr(), rows, cols, x.data_ptr(), batch, y.data_ptr())
+                    e1.record(stream)
+                torch.cuda.synchronize()
+                per = e0.elapsed_time(e1) / 1e3 / copies
+                res.append(round((nb + batch * (cols + rows) * 4) / per / 1e9, 1))
+            row["%dx%d" % (rows, cols)] = res
+            del w
+        table[tname] = row
+    best = max(v for row in table.values() for r in row.values() for v in r)
+    return {"unit": "GB/s", "columns": "batch 1, 8, 64", "peak": hbm_peak, "best_frac": round(best / hbm_peak, 4),
+            "note": "weights cycled over copies > L2; bytes = weights + x + y per launch", "table": table}
+
+
 TP_PROMPT = 1024
 
 
@@ -456,6 +568,10 @@ def run_ours(args, ws, rank, local):
     ppl = None if (rank != 0 or args.no_ppl) else run_perplexity(lm, L, model)
     model.close()
     tp7 = None if args.no_tp7b else run_tp7b(args, lm, L, torch, ws, rank, dist, hbm_peak)
+    qwen = None if (rank != 0 or args.no_qwen2) else run_qwen2(args, lm, L, torch, hbm_peak)
+    sweep = None if (rank != 0 or args.no_sweep) else run_gemv_sweep(lm, L, torch,
+                                                                     torch.cuda.ExternalStream(L.llamini_stream()),
+                                                                     hbm_peak)
     t_max, e2e_max = max_over_ranks(dist, [ms, e2e_s])
     b_max = max_over_ranks(dist, [bt[0]])[0] if bt else None
     tp_max = max_over_ranks(dist, [tp7[0]])[0] if tp7 else None
@@ -528,6 +644,10 @@ def run_ours(args, ws, rank, local):
                 "reference_stream_match": tp7[5],
                 # embed, 5 per layer (+ 2 allreduces per layer when split), lm_head, finish
                 "gpu_launches": args.tp_steps * (1 + 32 * (5 + (2 if ws > 1 else 0)) + 2)}
+        if qwen:
+            line["qwen2_05b"] = qwen
+        if sweep:
+            line["gemv_sweep"] = sweep
         if ws == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(path)
         print(json.dumps(line), flush=True)
@@ -637,6 +757,8 @@ def main():
     ap.add_argument("--no-ppl", action="store_true", help="skip the perplexity timing")
     ap.add_argument("--batch-steps", type=int, default=32, help="timed steps of the batch-64 leg")
     ap.add_argument("--no-tp7b", action="store_true", help="skip the 7B-shape tensor-parallel decode timing")
+    ap.add_argument("--no-qwen2", action="store_true", help="skip the Qwen2-0.5B batch 1 / batch 32 legs")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the isolated GEMV sweep (6 shapes x 7 formats x 3 batches)")
     ap.add_argument("--tp-steps", type=int, default=64, help="timed decode steps of the 7B-shape leg")
     ap.add_argument("--profile-batch", action="store_true",
                     help="no bench line: only a short batch-64 run of llama_1b for profilers "
