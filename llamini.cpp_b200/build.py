@@ -42,17 +42,22 @@ def _stale(out, deps):
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(verbose: bool = False, ptxas_info: bool = False) -> str:
-    """Compile every source that changed and relink; returns the .so path."""
-    os.makedirs(LIB, exist_ok=True)
-    os.makedirs(OBJ, exist_ok=True)
+def build(verbose: bool = False, ptxas_info: bool = False, timeline: bool = False) -> str:
+    """Compile every source that changed and relink; returns the .so path.
+    timeline = True builds the profiling variant (per-op stamps in the flow
+    kernel, flow_timeline.py) into lib_timeline/ instead."""
+    lib_dir, obj_dir = (os.path.join(HERE, "lib_timeline"), os.path.join(HERE, "_build_timeline")) if timeline \
+        else (LIB, OBJ)
+    nvcc_flags = NVCC_FLAGS + (["-DLLAMINI_FLOW_TIMELINE"] if timeline else [])
+    os.makedirs(lib_dir, exist_ok=True)
+    os.makedirs(obj_dir, exist_ok=True)
     headers = glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh")) + \
         glob.glob(os.path.join(ROOT, "include", "*.h"))
     jobs = []
     for src in sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp"))):
-        obj = os.path.join(OBJ, os.path.basename(src) + ".o")
+        obj = os.path.join(obj_dir, os.path.basename(src) + ".o")
         if src.endswith(".cu"):
-            flags = NVCC_FLAGS + (["-Xptxas", "-v"] if ptxas_info else [])
+            flags = nvcc_flags + (["-Xptxas", "-v"] if ptxas_info else [])
             cmd = [NVCC] + flags + ["-c", src, "-o", obj]
         else:
             cmd = ["g++"] + CXX_FLAGS + ["-c", src, "-o", obj]
@@ -62,7 +67,7 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
         for (src, _, _), out in zip(todo, ex.map(lambda j: _run(j[2]), todo)):
             if verbose and out.strip():
                 print("==", os.path.basename(src), "\n" + out)
-    so = os.path.join(LIB, "libllamini_cuda.so")
+    so = os.path.join(lib_dir, "libllamini_cuda.so")
     objs = [j[1] for j in jobs]
     if todo or _stale(so, objs):
         _run([NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", so] + objs + ["-lpthread", "-ldl", "-lrt"])

@@ -48,6 +48,27 @@
 #include <vector>
 
 namespace lm {
+#ifdef LLAMINI_FLOW_TIMELINE
+// Profiling build only (flow_timeline.py): %globaltimer stamps per (CTA, op,
+// point) of the last step of a launch, into g_tl[cta][op][8]: 0 the op's inputs
+// are ready (consumer thread 0), 1 its fragments are staged, 2 its first weight
+// tile is in shared memory, 3 the consumers' last MMAs are done, 4 the epilogue
+// warp has the last tile's partials, 5 just before the op's release, 6 just
+// after it, 7 the producer issues the op's first tile.
+__device__ unsigned long long* g_tl = nullptr;
+#define FLOW_TL(j, n, op, slot)                                                            \
+    do {                                                                                 \
+        if (g_tl != nullptr && (j) + 1 == (n)) {                                         \
+            unsigned long long t_;                                                       \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                       \
+            g_tl[((unsigned long long)blockIdx.x * 128 + (op)) * 8 + (slot)] = t_;       \
+        }                                                                                \
+    } while (0)
+#else
+#define FLOW_TL(j, n, op, slot) \
+    do {                        \
+    } while (0)
+#endif
 namespace {
 
 constexpr int kCW = 8;                              // consumer warps
@@ -702,6 +723,7 @@ __device__ void producer(const FlowArgs& a, FlowShared& S, uint8_t* ring) {
                 vstore(&S.abort, 1u);
                 return;
             }
+            if (i == 0 || (S.tasks[i - 1] >> 16) != (ent >> 16)) FLOW_TL(j, a.n_steps, ent >> 16, 7);
             const uint32_t q = seq % kQ;
             S.off[q] = (uint32_t)off;
             S.vend[q] = head + alloc;
@@ -758,6 +780,7 @@ __device__ void consumer(const FlowArgs& a, FlowShared& S, uint8_t* ring, float*
                 bool ok = true;
                 if (tid == 0 && !stopped(S)) ok = dep_wait(a, S, wait_ctr(a, op), wait_target(op, E));
                 cbar_or(!ok);
+                if (tid == 0) FLOW_TL(j, a.n_steps, op_i, 0);
                 run_op = op_i;
                 run_n = 0;
                 if (gemv && !warp_stopped(S)) {
@@ -771,6 +794,7 @@ __device__ void consumer(const FlowArgs& a, FlowShared& S, uint8_t* ring, float*
                         if (op.in_attn) stage_frag(frag_attn(op, ns, sb, slot, part, tig), xs + s * kXsSbBytes, slot, part, tig, g8);
                         else stage_rec(op.in, sb, xs + s * kXsSbBytes, lane);
                     }
+                    if (tid == 0) FLOW_TL(j, a.n_steps, op_i, 1);
                     __syncwarp();
                 }
             }
@@ -786,6 +810,7 @@ __device__ void consumer(const FlowArgs& a, FlowShared& S, uint8_t* ring, float*
                 bool ok = false;
                 if (!stopped(S)) ok = tile_wait(a, S, &S.bar[q], (cseq / kQ) & 1u);
                 ok = __all_sync(0xffffffffu, ok);
+                if (tid == 0 && (i == 0 || (S.tasks[i - 1] >> 16) != op_i)) FLOW_TL(j, a.n_steps, op_i, 2);
                 float acc[4] = {0.f, 0.f, 0.f, 0.f};
                 if (ok) {
                     const FTile tr = ftile_of(op, task);
@@ -812,6 +837,7 @@ __device__ void consumer(const FlowArgs& a, FlowShared& S, uint8_t* ring, float*
                         }
                     }
                 }
+                if (tid == 0) FLOW_TL(j, a.n_steps, op_i, 3);
 #pragma unroll
                 for (int r = 0; r < 4; r++) {
                     acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 1);
@@ -838,7 +864,9 @@ __device__ void consumer(const FlowArgs& a, FlowShared& S, uint8_t* ring, float*
                 const bool last = i + 1 == n_my || (S.tasks[i + 1] >> 16) != op_i;
                 if (last) {
                     cbar();                               // every thread's partials are written
+                    if (tid == 0) FLOW_TL(j, a.n_steps, op_i, 5);
                     if (tid == 0 && !stopped(S)) signal(&a.done[op_i], run_n);
+                    if (tid == 0) FLOW_TL(j, a.n_steps, op_i, 6);
                     if (tid == 0) atomicAdd(&S.gate_clr, 1u);
                 }
             }
@@ -901,6 +929,7 @@ __device__ void epilogue(const FlowArgs& a, FlowShared& S, uint32_t lane) {
             }
             const uint32_t b = cseq & 1u;
             bar_sync(kBarDone + b, kPairT);
+            if (lane == 0) FLOW_TL(j, a.n_steps, op_i, 4);
             float v = 0.f, u = 0.f;
             if (lane < 16) {
 #pragma unroll
@@ -944,7 +973,9 @@ __device__ void epilogue(const FlowArgs& a, FlowShared& S, uint32_t lane) {
                 // release (cumulative at GPU scope)
                 __syncwarp();
                 if (!op.argmax) {
+                    if (lane == 0) FLOW_TL(j, a.n_steps, op_i, 5);
                     if (lane == 0) signal(&a.done[op_i], run_n);
+                    if (lane == 0) FLOW_TL(j, a.n_steps, op_i, 6);
                 } else {
                     // lm_head: fold the keys, then the CTA completing the op finishes the step
 #pragma unroll
@@ -1154,3 +1185,21 @@ bool launch_flow_embed(const FlowArgs& a, cudaStream_t st) {
 }
 
 }  // namespace lm
+
+#ifdef LLAMINI_FLOW_TIMELINE
+// Profiling build only: enable = 1 clears and arms the stamp buffer (148 CTAs x
+// 128 ops x 8 points), enable = 0 disarms it and copies it to host_out.
+extern "C" int llamini_flow_timeline(int enable, void* host_out) {
+    static unsigned long long* d = nullptr;
+    const size_t n = 148ull * 128 * 8;
+    if (enable) {
+        if (!d && cudaMalloc(&d, n * 8) != cudaSuccess) return -1;
+        if (cudaMemset(d, 0, n * 8) != cudaSuccess) return -1;
+        return cudaMemcpyToSymbol(lm::g_tl, &d, sizeof(d)) == cudaSuccess ? 0 : -1;
+    }
+    if (!d || cudaDeviceSynchronize() != cudaSuccess) return -1;
+    unsigned long long* z = nullptr;
+    if (cudaMemcpyToSymbol(lm::g_tl, &z, sizeof(z)) != cudaSuccess) return -1;
+    return cudaMemcpy(host_out, d, n * 8, cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -1;
+}
+#endif
