@@ -423,16 +423,21 @@ constexpr uint32_t kXsSbBytes = 16 * 64 + 16 * 8;
 constexpr uint32_t kXsWarpBytes = kFlowMaxSb * kXsSbBytes;
 __host__ __device__ __forceinline__ uint32_t xs_bytes() { return kCW * kXsWarpBytes; }
 
-// Copy the records of super-block sb (global) into slot s of the warp's slice.
-__device__ __forceinline__ void stage_rec(const FlowRec& R, uint32_t sb, uint8_t* xs, uint32_t lane) {
-    const uint4* src = reinterpret_cast<const uint4*>(R.w + (uint64_t)sb * 256);
-    uint4* dst = reinterpret_cast<uint4*>(xs);
-    const uint4 v0 = __ldcg(src + lane), v1 = __ldcg(src + lane + 32);
-    float2 f = make_float2(0.f, 0.f);
-    if (lane < 16) f = __ldcg(R.fs + (uint64_t)sb * 16 + lane);
-    dst[lane] = v0;
-    dst[lane + 32] = v1;
-    if (lane < 16) reinterpret_cast<float2*>(xs + 16 * 64)[lane] = f;
+// The records of the warp's nsb (<= kFlowMaxSb) super-blocks warp, warp + 8, ...
+// into its slots with cp.async (no registers), every copy in flight at once: one
+// L2 round trip for all of them. Records are 16-byte aligned (256-word groups of
+// words, 16-entry groups of scales) and so are the slots.
+__device__ __forceinline__ void stage_recs(const FlowRec& R, uint32_t warp, uint32_t nsb, uint8_t* xs, uint32_t lane) {
+    for (uint32_t s = 0; s < nsb; s++) {
+        const uint32_t sb = warp + kCW * s;
+        const uint8_t* w = reinterpret_cast<const uint8_t*>(R.w + (uint64_t)sb * 256);
+        const uint8_t* f = reinterpret_cast<const uint8_t*>(R.fs + (uint64_t)sb * 16);
+        uint8_t* d = xs + s * kXsSbBytes;
+        cp_async16(d + 16 * lane, w + 16 * lane);
+        cp_async16(d + 512 + 16 * lane, w + 512 + 16 * lane);
+        if (lane < 8) cp_async16(d + 1024 + 16 * lane, f + 16 * lane);
+    }
+    cp_async_wait_all();
 }
 // Store a lane's fragment (computed in registers) into slot s of the slice.
 __device__ __forceinline__ void stage_frag(const XFrag& X, uint8_t* xs, uint32_t slot, uint32_t part, uint32_t tig,
@@ -789,10 +794,12 @@ __device__ void consumer(const FlowArgs& a, FlowShared& S, uint8_t* ring, float*
                     nsb = warp < nsbt ? (nsbt - warp + kCW - 1) / kCW : 0;
                     uint32_t ns = 1;
                     if (op.in_attn) ns = split_range(vload(&a.st->pos), op.n_split, 0).ns;
-                    for (uint32_t s = 0; s < nsb; s++) {
-                        const uint32_t sb = warp + kCW * s;
-                        if (op.in_attn) stage_frag(frag_attn(op, ns, sb, slot, part, tig), xs + s * kXsSbBytes, slot, part, tig, g8);
-                        else stage_rec(op.in, sb, xs + s * kXsSbBytes, lane);
+                    if (op.in_attn) {
+                        for (uint32_t s = 0; s < nsb; s++)
+                            stage_frag(frag_attn(op, ns, warp + kCW * s, slot, part, tig), xs + s * kXsSbBytes, slot,
+                                       part, tig, g8);
+                    } else {
+                        stage_recs(op.in, warp, nsb, xs, lane);
                     }
                     if (tid == 0) FLOW_TL(j, a.n_steps, op_i, 1);
                     __syncwarp();
@@ -909,7 +916,16 @@ __device__ void epilogue(const FlowArgs& a, FlowShared& S, uint32_t lane) {
                     // sums, added in a fixed order (every CTA gets the same bits)
                     const uint32_t ng = op.K / 16;
                     float s = 0.f;
-                    for (uint32_t g = lane; g < ng; g += 32) s += __ldcg(op.in.ss + g);
+                    // four loads in flight at a time (one L2 round trip for K <= 2048),
+                    // added in group order
+                    for (uint32_t g0 = lane; g0 < ng; g0 += 128) {
+                        float sv[4];
+#pragma unroll
+                        for (uint32_t i = 0; i < 4; i++) sv[i] = g0 + 32 * i < ng ? __ldcg(op.in.ss + g0 + 32 * i) : 0.f;
+#pragma unroll
+                        for (uint32_t i = 0; i < 4; i++)
+                            if (g0 + 32 * i < ng) s += sv[i];
+                    }
                     s = wsum(s);
                     inv = 1.0f / sqrtf(s / (float)op.K + op.eps);
                 }
