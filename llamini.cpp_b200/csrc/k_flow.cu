@@ -92,6 +92,7 @@ struct FlowShared {
     uint32_t off[kQ];
     float part[2][kCW][2][16];           // per buffer, warp, (main | up) and row
     uint32_t consumed, issued, abort, epoch;
+    uint32_t pos;                        // the current step's position (read once per step)
     // Producer gate: a GPU-scope release waits for every bulk copy the SM has
     // in flight (about a microsecond while the weight stream runs), so from the
     // start of an op's last tile in this CTA until that op's release the
@@ -587,11 +588,10 @@ __device__ __forceinline__ FTile ftile_of(const FlowOp& op, uint32_t t) {
 // ------------------------------------------------------------------ attention task
 
 template <typename KV>
-__device__ void attn_prefetch(const FlowArgs& a, const FlowOp& op, uint32_t task, float* stage, uint32_t tid) {
+__device__ void attn_prefetch(const FlowOp& op, uint32_t task, uint32_t pos, float* stage, uint32_t tid) {
     const AttnArgs& at = op.at;
     const uint32_t h = task / op.n_split, split = task - h * op.n_split;
     const uint32_t g = h / (at.n_heads / at.n_kv);
-    const uint32_t pos = vload(&a.st->pos);
     const SplitRange r = split_range(pos, op.n_split, split);
     if (split >= r.ns) return;
     const uint32_t hd = at.hd;
@@ -607,11 +607,10 @@ __device__ void attn_prefetch(const FlowArgs& a, const FlowOp& op, uint32_t task
 // RoPE of q and the new k, the cache write (one writer per kv head), the
 // split's partial (m, l, o) for the O projection's merge.
 template <typename KV>
-__device__ void attn_task(const FlowArgs& a, const FlowOp& op, uint32_t task, float* stage, bool staged, uint32_t tid) {
+__device__ void attn_task(const FlowOp& op, uint32_t task, uint32_t pos, float* stage, bool staged, uint32_t tid) {
     const AttnArgs& at = op.at;
     const uint32_t h = task / op.n_split, split = task - h * op.n_split;
     const uint32_t g = h / (at.n_heads / at.n_kv);
-    const uint32_t pos = vload(&a.st->pos);
     const SplitRange r = split_range(pos, op.n_split, split);
     if (split >= r.ns) return;
     const uint32_t hd = at.hd, G = at.n_heads / at.n_kv;
@@ -772,13 +771,21 @@ __device__ void consumer(const FlowArgs& a, FlowShared& S, uint8_t* ring, float*
                     for (uint32_t w = tid; w < (uint32_t)(sizeof(FlowOp) / 4); w += kCT) dst[w] = __ldg(src + w);
                 }
                 cbar();
+                if (run_op == 0xFFFFFFFFu) {
+                    // the step has started (acquire): its position, read here once (it
+                    // changes only between steps), and the cache rows of earlier steps
+                    bool ok = true;
+                    if (tid == 0 && !stopped(S)) {
+                        ok = dep_wait(a, S, &a.sync->step_done, E);
+                        vstore(&S.pos, vload(&a.st->pos));
+                    }
+                    cbar_or(!ok);
+                }
                 if (!gemv) {
                     // cached K/V rows depend only on the step having started
-                    bool ok = true;
-                    if (run_op == 0xFFFFFFFFu && tid == 0 && !stopped(S)) ok = dep_wait(a, S, &a.sync->step_done, E);
-                    if (!cbar_or(!ok || stopped(S))) {
-                        if (op.at.kv_f16) attn_prefetch<__half>(a, op, task, stage, tid);
-                        else attn_prefetch<float>(a, op, task, stage, tid);
+                    if (!cbar_or(stopped(S))) {
+                        if (op.at.kv_f16) attn_prefetch<__half>(op, task, vload(&S.pos), stage, tid);
+                        else attn_prefetch<float>(op, task, vload(&S.pos), stage, tid);
                         prefetched = true;
                     }
                 }
@@ -793,7 +800,7 @@ __device__ void consumer(const FlowArgs& a, FlowShared& S, uint8_t* ring, float*
                     const uint32_t nsbt = op.K / 256;
                     nsb = warp < nsbt ? (nsbt - warp + kCW - 1) / kCW : 0;
                     uint32_t ns = 1;
-                    if (op.in_attn) ns = split_range(vload(&a.st->pos), op.n_split, 0).ns;
+                    if (op.in_attn) ns = split_range(vload(&S.pos), op.n_split, 0).ns;
                     if (op.in_attn) {
                         for (uint32_t s = 0; s < nsb; s++)
                             stage_frag(frag_attn(op, ns, warp + kCW * s, slot, part, tig), xs + s * kXsSbBytes, slot,
@@ -864,8 +871,8 @@ __device__ void consumer(const FlowArgs& a, FlowShared& S, uint8_t* ring, float*
                     vstore(&S.gate_set, ++gset);
                 }
                 if (!cbar_or(stopped(S))) {
-                    if (op.at.kv_f16) attn_task<__half>(a, op, task, stage, prefetched, tid);
-                    else attn_task<float>(a, op, task, stage, prefetched, tid);
+                    if (op.at.kv_f16) attn_task<__half>(op, task, vload(&S.pos), stage, prefetched, tid);
+                    else attn_task<float>(op, task, vload(&S.pos), stage, prefetched, tid);
                 }
                 run_n++;
                 const bool last = i + 1 == n_my || (S.tasks[i + 1] >> 16) != op_i;
