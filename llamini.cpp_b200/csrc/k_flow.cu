@@ -814,11 +814,6 @@ __device__ void consumer(const FlowArgs& a, FlowShared& S, uint8_t* ring, float*
             }
             if (gemv) {
                 const uint32_t b = cseq & 1u;
-                if (tid == 0 && (i + 1 == n_my || (S.tasks[i + 1] >> 16) != op_i)) {
-                    // this CTA's last tile of the op: no new copies until its release
-                    vstore(&S.gate_until, cseq);
-                    vstore(&S.gate_set, ++gset);
-                }
                 bar_sync(kBarFree + b, kPairT);          // partial buffer b was read
                 const uint32_t q = cseq % kQ;
                 bool ok = false;
@@ -852,6 +847,12 @@ __device__ void consumer(const FlowArgs& a, FlowShared& S, uint8_t* ring, float*
                     }
                 }
                 if (tid == 0) FLOW_TL(j, a.n_steps, op_i, 3);
+                if (tid == 0 && (i + 1 == n_my || (S.tasks[i + 1] >> 16) != op_i)) {
+                    // this CTA's last tile of the op is computed (by warp 0 at least):
+                    // no new copies until the op's release
+                    vstore(&S.gate_until, cseq);
+                    vstore(&S.gate_set, ++gset);
+                }
 #pragma unroll
                 for (int r = 0; r < 4; r++) {
                     acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 1);
