@@ -452,22 +452,32 @@ struct alignas(64) TGemmArgs {
 // with tp_allreduce_kernel (k_tp.cu) over peer memory.
 constexpr uint32_t kTpMaxRanks = 8;
 constexpr uint32_t kTpSlotFloats = 16384;
+// The wide allreduce (batches and prefill chunks: one vector per column):
+// slices of kTpWideSlice floats, one CTA each, at most kTpWideCtas of them.
+constexpr uint32_t kTpWideCtas = 256;
+constexpr uint32_t kTpWideSlice = 2048;
+constexpr uint32_t kTpWideFloats = kTpWideCtas * kTpWideSlice;   // 64 columns of 8192
 struct TpState {
     uint32_t rank = 0, world = 1;
     float* local = nullptr;                  // this rank's exported buffer
     float* peer[kTpMaxRanks] = {};           // every rank's buffer, mapped here (this rank's included)
     uint32_t* gen = nullptr;                 // allreduces this rank has finished (device)
+    uint32_t* wgen = nullptr;                // wide allreduces finished, per slice (device, kTpWideCtas)
 };
 TpState& tp();
 size_t tp_buffer_bytes();
 bool tp_alloc_buffer();
 // out[i] += sum over ranks of part[i] (rank order), i < n; part is this rank's.
 bool launch_tp_allreduce(const float* part, float* out, uint32_t n, uint32_t* err, cudaStream_t st);
+// out[i] += the sum over ranks of part[i], i < n <= kTpWideFloats, slice by slice.
+bool launch_tp_allreduce_wide(const float* part, float* out, uint32_t n, uint32_t* err, cudaStream_t st);
 
 // ---------------------------------------------------------------- prefill (k_prefill.cu)
+// A chunk's columns are ns sequences x cp positions: column b is position
+// p0 + b % cp of sequence b / cp (one sequence: cp = C, strides 0).
 struct PEmbedArgs {
-    const uint32_t* tokens;        // token of position p at tokens[p]
-    uint32_t p0, C;
+    const uint32_t* tokens;        // token of sequence i, position p at tokens[i * tok_stride + p]
+    uint32_t p0, C, cp, tok_stride;
     DevMat tok, pos;               // token table, learned positions (or ptr == nullptr)
     float scale;
     float* hidden;                 // [C][dim]
@@ -476,9 +486,10 @@ struct PEmbedArgs {
 struct PRopeArgs {
     float* qkv;                    // [C][qkv_stride]: q | k | v of each position
     uint32_t qkv_stride;
-    void* kc;                      // this layer's cache [n_kv][max_seq][hd]
+    void* kc;                      // this layer's cache [n_kv][max_seq][hd] of sequence 0
     void* vc;
-    uint32_t kv_f16, n_heads, n_kv, hd, max_seq, p0, rope;
+    uint32_t kv_f16, n_heads, n_kv, hd, max_seq, p0, rope, cp;
+    uint64_t seq_elems;            // cache elements from one sequence's layer to the next's
     const float* theta;
 };
 struct PAttnArgs {
@@ -489,7 +500,8 @@ struct PAttnArgs {
     uint32_t kv_f16;
     float* out;                    // [C][out_stride]
     uint32_t out_stride;
-    uint32_t n_heads, n_kv, hd, max_seq, p0, C;
+    uint32_t n_heads, n_kv, hd, max_seq, p0, C, cp;
+    uint64_t seq_elems;
 };
 // Teacher-forced scoring of a chunk (compute_perplexity, generate.c:169-197):
 // lp[p] = log softmax(logits of position p)[tokens[p + 1]] for p0 <= p <= last.

@@ -2,8 +2,9 @@
 //
 // generate_autoregressive (generate.c:122-167) runs every prompt position
 // through the decode step and discards the logits of all but the last one.
-// Here up to 64 consecutive prompt positions p0 .. p0 + C - 1 go through each
-// layer together: the matrices as tcgen05 GEMMs with the C positions as the
+// Here up to 64 prompt positions go through each layer together (p0 .. p0 +
+// C - 1 of one sequence, or cp consecutive positions of each of ns sequences
+// of a batch: column b is position p0 + b % cp of sequence b / cp): the matrices as tcgen05 GEMMs with the C positions as the
 // columns (k_tgemm.cu, same staging and finish kernels as batched decode), the
 // rotation and KV-cache writes of all C positions, then causal attention of
 // every position over the cache up to itself -- per position the arithmetic of
@@ -21,11 +22,11 @@
 
 namespace lm {
 
-// grid C, 256 threads: position p0 + b embeds tokens[p0 + b] (tensor_get_row,
+// grid C, 256 threads: column b embeds its position's token (tensor_get_row,
 // tensor.c:24-30; GPT-2 adds the learned position row, gpt2.c:155-160).
 __global__ void pembed_kernel(const PEmbedArgs a) {
-    const uint32_t b = blockIdx.x, p = a.p0 + b;
-    uint32_t t = a.tokens[p];
+    const uint32_t b = blockIdx.x, i = b / a.cp, p = a.p0 + (b - i * a.cp);
+    uint32_t t = a.tokens[(uint64_t)i * a.tok_stride + p];
     if (t >= a.tok.rows) t = 0;                    // out-of-range ids read row 0
     float* h = a.hidden + (uint64_t)b * a.dim;
     decode_row_part(a.tok, t, h, a.scale, false, threadIdx.x, blockDim.x);
@@ -36,11 +37,11 @@ __global__ void pembed_kernel(const PEmbedArgs a) {
     }
 }
 
-// grid (C, n_heads + n_kv): query head h of position p0 + b rotated in place,
-// or kv head h - n_heads rotated and written with its V row to the cache at
-// position p0 + b (model.c:31-58 then 222-224).
+// grid (C, n_heads + n_kv): query head h of column b rotated in place, or kv
+// head h - n_heads rotated and written with its V row to the column's
+// sequence's cache at its position (model.c:31-58 then 222-224).
 __global__ void prope_kernel(const PRopeArgs a) {
-    const uint32_t b = blockIdx.x, h = blockIdx.y, p = a.p0 + b, hd = a.hd;
+    const uint32_t b = blockIdx.x, h = blockIdx.y, i = b / a.cp, p = a.p0 + (b - i * a.cp), hd = a.hd;
     float* row = a.qkv + (uint64_t)b * a.qkv_stride;
     if (h < a.n_heads) {
         rope_pairs(row + (uint64_t)h * hd, hd, p, a.rope, a.theta, threadIdx.x, blockDim.x);
@@ -51,7 +52,7 @@ __global__ void prope_kernel(const PRopeArgs a) {
     const float* v = row + (uint64_t)(a.n_heads + a.n_kv) * hd + (uint64_t)j * hd;
     rope_pairs(k, hd, p, a.rope, a.theta, threadIdx.x, blockDim.x);
     __syncthreads();                               // the rotated row, written by other threads
-    const uint64_t off = ((uint64_t)j * a.max_seq + p) * hd;
+    const uint64_t off = (uint64_t)i * a.seq_elems + ((uint64_t)j * a.max_seq + p) * hd;
     for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) {
         if (a.kv_f16) {
             reinterpret_cast<__half*>(a.kc)[off + i] = __float2half_rn(k[i]);
@@ -72,14 +73,17 @@ __host__ __device__ __forceinline__ size_t pattn_smem(uint32_t hd) {
     return ((size_t)kPQ * hd + (size_t)kPK * (hd + 1) + (size_t)kPK * hd + (size_t)kPQ * kPK) * sizeof(float);
 }
 
-// grid (n_heads, ceil(C / kPQ)). Thread t serves query t / 16 of the CTA:
-// scores of keys t % 16 + 16 u (u < 4) of each tile, then output elements
-// t % 16 + 16 k of the head.
+// grid (n_heads, ns * ceil(cp / kPQ)): a CTA takes up to kPQ consecutive
+// positions of one sequence. Thread t serves query t / 16 of the CTA: scores
+// of keys t % 16 + 16 u (u < 4) of each tile, then output elements t % 16 +
+// 16 k of the head.
 template <typename KV>
 __global__ void __launch_bounds__(kPThreads) pattn_kernel(const PAttnArgs a) {
     extern __shared__ __align__(16) float psm[];
     const uint32_t hd = a.hd, h = blockIdx.x, g = h / (a.n_heads / a.n_kv);
-    const uint32_t q0 = blockIdx.y * kPQ, nq = min(kPQ, a.C - q0);
+    const uint32_t qb = (a.cp + kPQ - 1) / kPQ, si = blockIdx.y / qb;
+    const uint32_t q0 = (blockIdx.y - si * qb) * kPQ, nq = min(kPQ, a.cp - q0);
+    const uint32_t c0col = si * a.cp + q0;         // the CTA's first column
     float* qs = psm;                               // [kPQ][hd]
     float* ks = qs + kPQ * hd;                     // [kPK][hd + 1]
     float* vs = ks + kPK * (hd + 1);               // [kPK][hd]
@@ -87,10 +91,10 @@ __global__ void __launch_bounds__(kPThreads) pattn_kernel(const PAttnArgs a) {
     const uint32_t tid = threadIdx.x, qi = tid >> 4, lj = tid & 15u;
     for (uint32_t i = tid; i < kPQ * hd; i += kPThreads) {
         const uint32_t r = i / hd, d = i - r * hd;
-        qs[i] = r < nq ? a.qkv[(uint64_t)(q0 + r) * a.qkv_stride + (uint64_t)h * hd + d] : 0.f;
+        qs[i] = r < nq ? a.qkv[(uint64_t)(c0col + r) * a.qkv_stride + (uint64_t)h * hd + d] : 0.f;
     }
-    const KV* kc = reinterpret_cast<const KV*>(a.kc) + (uint64_t)g * a.max_seq * hd;
-    const KV* vc = reinterpret_cast<const KV*>(a.vc) + (uint64_t)g * a.max_seq * hd;
+    const KV* kc = reinterpret_cast<const KV*>(a.kc) + (uint64_t)si * a.seq_elems + (uint64_t)g * a.max_seq * hd;
+    const KV* vc = reinterpret_cast<const KV*>(a.vc) + (uint64_t)si * a.seq_elems + (uint64_t)g * a.max_seq * hd;
     const uint32_t my_pos = a.p0 + q0 + qi;        // this lane group's query position
     const uint32_t last = a.p0 + q0 + nq - 1;      // last key any query here needs
     const float rscale = sqrtf((float)hd);         // model.c:243
@@ -151,7 +155,7 @@ __global__ void __launch_bounds__(kPThreads) pattn_kernel(const PAttnArgs a) {
         }
     }
     if (qi < nq) {
-        float* out = a.out + (uint64_t)(q0 + qi) * a.out_stride + (uint64_t)h * hd;
+        float* out = a.out + (uint64_t)(c0col + qi) * a.out_stride + (uint64_t)h * hd;
 #pragma unroll
         for (uint32_t k = 0; k < kPMaxHd / 16; k++) {
             const uint32_t d = lj + 16 * k;
@@ -209,11 +213,13 @@ bool prefill_init() {
 }
 
 bool launch_pembed(const PEmbedArgs& a, cudaStream_t st) {
+    if (a.cp == 0 || a.C % a.cp != 0) { set_error("prefill: %u columns are not whole runs of %u positions", a.C, a.cp); return false; }
     pembed_kernel<<<a.C, 256, 0, st>>>(a);
     return LM_CUDA(cudaGetLastError());
 }
 
 bool launch_prope(const PRopeArgs& a, uint32_t C, cudaStream_t st) {
+    if (a.cp == 0 || C % a.cp != 0) { set_error("prefill: %u columns are not whole runs of %u positions", C, a.cp); return false; }
     const uint32_t nt = a.hd < 32 ? 32u : (a.hd + 31) / 32 * 32;
     prope_kernel<<<dim3(C, a.n_heads + a.n_kv), nt > 1024 ? 1024 : nt, 0, st>>>(a);
     return LM_CUDA(cudaGetLastError());
@@ -224,7 +230,11 @@ bool launch_pattn(const PAttnArgs& a, cudaStream_t st) {
         set_error("prefill attention: head size %u (at most %u), heads %u / %u", a.hd, kPMaxHd, a.n_heads, a.n_kv);
         return false;
     }
-    const dim3 grid(a.n_heads, (a.C + kPQ - 1) / kPQ);
+    if (a.cp == 0 || a.C % a.cp != 0) {
+        set_error("prefill attention: %u columns are not whole runs of %u positions", a.C, a.cp);
+        return false;
+    }
+    const dim3 grid(a.n_heads, a.C / a.cp * ((a.cp + kPQ - 1) / kPQ));
     if (a.kv_f16) pattn_kernel<__half><<<grid, kPThreads, pattn_smem(a.hd), st>>>(a);
     else pattn_kernel<float><<<grid, kPThreads, pattn_smem(a.hd), st>>>(a);
     return LM_CUDA(cudaGetLastError());

@@ -18,6 +18,14 @@
 // A rank reuses slot n % 2 at allreduce n + 2 only after allreduce n + 1, which
 // needs every peer's flag n + 1 -- set after that peer finished reading slot
 // n % 2 -- so no copy overwrites data a peer still reads.
+//
+// The wide allreduce (a batch's or a prefill chunk's columns, up to
+// kTpWideFloats floats) has slots, flags and counters of its own after these,
+// and runs the same protocol per slice of kTpWideSlice floats: CTA c copies,
+// flags, waits for and adds slice c only, so slices need no grid-wide barrier.
+// The next allreduce's kernel starts after this one has finished on this rank
+// (programmatic launch waits for it), so a peer's flag n + 1 for slice c again
+// means that peer has read every rank's slice c of allreduce n.
 #include "internal.h"
 #include "pdl.cuh"
 
@@ -35,6 +43,11 @@ struct TpArgs {
 };
 
 __device__ __forceinline__ uint32_t* tp_flags(float* buf) { return reinterpret_cast<uint32_t*>(buf + 2 * kTpSlotFloats); }
+// wide slots: after the flags (16-byte aligned), then the wide flags [rank][slice]
+__host__ __device__ __forceinline__ float* tp_wide(float* buf) { return buf + 2 * kTpSlotFloats + kTpMaxRanks; }
+__device__ __forceinline__ uint32_t* tp_wflags(float* buf) {
+    return reinterpret_cast<uint32_t*>(tp_wide(buf) + 2 * kTpWideFloats);
+}
 __device__ __forceinline__ uint64_t tp_time() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
@@ -95,6 +108,48 @@ __global__ void __launch_bounds__(1024) tp_allreduce_kernel(const TpArgs a) {
     if (tid == 0) *reinterpret_cast<volatile uint32_t*>(a.gen) = n;
 }
 
+// grid ceil(n / kTpWideSlice), 256 threads: CTA c takes floats [c S, c S + S).
+__global__ void __launch_bounds__(256) tp_allreduce_wide_kernel(const TpArgs a) {
+    __shared__ uint32_t s_n, s_fail;
+    pdl_trigger();
+    pdl_wait();                                       // the partial sums come from the previous kernel
+    const uint32_t tid = threadIdx.x, c = blockIdx.x;
+    const uint32_t i0 = c * kTpWideSlice, i1 = min(a.n, i0 + kTpWideSlice);
+    if (tid == 0) {
+        s_n = *reinterpret_cast<volatile uint32_t*>(a.gen + c) + 1u;
+        s_fail = 0;
+    }
+    __syncthreads();
+    const uint32_t n = s_n, par = n & 1u;
+    float* mine = tp_wide(a.buf[a.rank]) + par * kTpWideFloats;
+    for (uint32_t i = i0 + tid; i < i1; i += blockDim.x) mine[i] = a.part[i];
+    __threadfence_system();                           // this thread's slot writes before any flag
+    __syncthreads();
+    if (tid < a.world && tid != a.rank) {
+        st_release_sys(tp_wflags(a.buf[tid]) + a.rank * kTpWideCtas + c, n);
+        const uint32_t* f = tp_wflags(a.buf[a.rank]) + tid * kTpWideCtas + c;
+        const uint64_t t0 = tp_time();
+        for (uint32_t i = 0;; i++) {
+            if ((int32_t)(ld_acquire_sys(f) - n) >= 0) break;
+            if ((i & 63u) == 63u && tp_time() - t0 > kTpWaitNs) {
+                atomicOr(a.err, kErrWaitTimeout);
+                s_fail = 1;
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    if (s_fail) return;
+    for (uint32_t i = i0 + tid; i < i1; i += blockDim.x) {
+        float s = 0.f;
+        for (uint32_t j = 0; j < a.world; j++)
+            s += j == a.rank ? mine[i] : ld_relaxed_sys(tp_wide(a.buf[j]) + par * kTpWideFloats + i);
+        a.out[i] += s;
+    }
+    __syncthreads();
+    if (tid == 0) *reinterpret_cast<volatile uint32_t*>(a.gen + c) = n;
+}
+
 // ---------------------------------------------------------------- host side
 
 namespace {
@@ -103,7 +158,10 @@ TpState g_tp;
 
 TpState& tp() { return g_tp; }
 
-size_t tp_buffer_bytes() { return 2 * kTpSlotFloats * sizeof(float) + kTpMaxRanks * sizeof(uint32_t); }
+size_t tp_buffer_bytes() {
+    return (2 * kTpSlotFloats + kTpMaxRanks + 2 * kTpWideFloats) * sizeof(float) +
+           (size_t)kTpMaxRanks * kTpWideCtas * sizeof(uint32_t);
+}
 
 bool tp_alloc_buffer() {
     if (g_tp.local) return true;
@@ -112,9 +170,13 @@ bool tp_alloc_buffer() {
     if (!LM_CUDA(cudaMalloc(&p, tp_buffer_bytes()))) return false;
     if (!LM_CUDA(cudaMemset(p, 0, tp_buffer_bytes()))) { cudaFree(p); return false; }
     uint32_t* gen = nullptr;
-    if (!LM_CUDA(cudaMalloc((void**)&gen, 4)) || !LM_CUDA(cudaMemset(gen, 0, 4))) { cudaFree(p); return false; }
+    if (!LM_CUDA(cudaMalloc((void**)&gen, 4 * (1 + kTpWideCtas))) || !LM_CUDA(cudaMemset(gen, 0, 4 * (1 + kTpWideCtas)))) {
+        cudaFree(p);
+        return false;
+    }
     g_tp.local = (float*)p;
     g_tp.gen = gen;
+    g_tp.wgen = gen + 1;
     return true;
 }
 
@@ -131,6 +193,21 @@ bool launch_tp_allreduce(const float* part, float* out, uint32_t n, uint32_t* er
     a.gen = g_tp.gen;
     a.err = err;
     return LM_CUDA(launch_k(tp_allreduce_kernel, dim3(1), dim3(1024), 0, st, a));
+}
+
+bool launch_tp_allreduce_wide(const float* part, float* out, uint32_t n, uint32_t* err, cudaStream_t st) {
+    if (g_tp.world < 2) { set_error("allreduce without a tensor-parallel group"); return false; }
+    if (n == 0 || n > kTpWideFloats) { set_error("wide allreduce of %u floats (1..%u)", n, kTpWideFloats); return false; }
+    TpArgs a;
+    a.part = part;
+    a.out = out;
+    a.n = n;
+    a.rank = g_tp.rank;
+    a.world = g_tp.world;
+    for (uint32_t j = 0; j < kTpMaxRanks; j++) a.buf[j] = j < g_tp.world ? g_tp.peer[j] : nullptr;
+    a.gen = g_tp.wgen;
+    a.err = err;
+    return LM_CUDA(launch_k(tp_allreduce_wide_kernel, dim3((n + kTpWideSlice - 1) / kTpWideSlice), dim3(256), 0, st, a));
 }
 
 }  // namespace lm

@@ -27,6 +27,7 @@
 // Buffers and weight copies of chunked prefill (session.cpp, prefill section).
 struct Prefill {
     float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *ffn_h = nullptr, *osc = nullptr;
+    float* tp_part = nullptr;            // tensor parallel: the chunk's o / down partial sums
     float *part = nullptr, *part2 = nullptr, *part3 = nullptr;
     // teacher-forced scoring (built on first use): lm_head partials, the
     // chunk's logits [C][vocab], and per position the next token's log-prob
@@ -317,6 +318,7 @@ GemvArgs o_args(llamini_session* s, u32 l) {
     if (s->tp_world > 1) {                            // partial sums; the allreduce adds them to hidden
         o.seg[0].epi = EPI_STORE;
         o.seg[0].out = s->tp_part;
+        if (tp().rank != 0) o.seg[0].bias = nullptr;  // the bias enters the sum once
     }
     return o;
 }
@@ -354,6 +356,7 @@ GemvArgs down_args(llamini_session* s, u32 l) {
     if (s->tp_world > 1) {
         d.seg[0].epi = EPI_STORE;
         d.seg[0].out = s->tp_part;
+        if (tp().rank != 0) d.seg[0].bias = nullptr;
     }
     return d;
 }
@@ -1186,6 +1189,7 @@ struct llamini_batch {
     u32 n_split = 1, kv_f16 = 0, kmax = 0;
     float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *ffn_h = nullptr, *logits = nullptr;
     float* probs = nullptr;               // the device sampler's scratch (vocab floats)
+    float* tp_part = nullptr;             // tensor parallel: the batch's o / down partial sums
     float *sx = nullptr, *part = nullptr, *part2 = nullptr, *part3 = nullptr, *apart = nullptr;
     uint16_t *xh = nullptr, *xl = nullptr;
     u32 *counters = nullptr, *tokens = nullptr, *n_prompt = nullptr;
@@ -1589,12 +1593,22 @@ bool batch_enqueue_step_tc(llamini_batch* b, cudaStream_t st) {
             a.ldx = s->qd;
             if (!launch_bstage(a, st)) return false;
         }
+        // the residual add, then the next matrix's staging; in a tensor-parallel
+        // group the ranks' partial sums first go through the wide allreduce
+        auto resid = [&](const BPlan& gg, const float* bias, const float* nw, const float* nb) {
+            if (s->tp_world == 1) return finstage(fin_args(gg, 0, nullptr, EPI_RESID, bias, b->hidden, s->dim), norm, nw, nb);
+            if (!launch_bfinish(fin_args(gg, 0, nullptr, EPI_STORE, tp().rank == 0 ? bias : nullptr, b->tp_part, s->dim), st) ||
+                !launch_tp_allreduce_wide(b->tp_part, b->hidden, b->B * s->dim, b->err, st))
+                return false;
+            BStageArgs a = stage_args(s->dim, norm, nw, nb);
+            a.x = b->hidden;
+            a.ldx = s->dim;
+            return launch_bstage(a, st);
+        };
         {
             const DevMat* mm[1] = {&W.o};
             float* pp[1] = {b->part};
-            if (!gemm(mm, pp, 1, s->qd, &g) ||
-                !finstage(fin_args(g, 0, nullptr, EPI_RESID, W.bo, b->hidden, s->dim), norm, W.n2w, W.n2b))
-                return false;
+            if (!gemm(mm, pp, 1, s->qd, &g) || !resid(g, W.bo, W.n2w, W.n2b)) return false;
         }
         if (gpt2) {
             const DevMat* mm[1] = {&W.up};
@@ -1615,9 +1629,7 @@ bool batch_enqueue_step_tc(llamini_batch* b, cudaStream_t st) {
             float* pp[1] = {b->part};
             const float* nw = l + 1 < L ? s->layers[l + 1].n1w : s->fnw;
             const float* nb = l + 1 < L ? s->layers[l + 1].n1b : s->fnb;
-            if (!gemm(mm, pp, 1, s->ffn, &g) ||
-                !finstage(fin_args(g, 0, nullptr, EPI_RESID, W.bdown, b->hidden, s->dim), norm, nw, nb))
-                return false;
+            if (!gemm(mm, pp, 1, s->ffn, &g) || !resid(g, W.bdown, nw, nb)) return false;
         }
     }
     {
@@ -1751,6 +1763,7 @@ bool batch_alloc(llamini_batch* b) {
     b->kc = own(s, cache);
     b->vc = own(s, cache);
     b->st = (StepState*)own(s, sizeof(StepState));
+    if (s->tp_world > 1 && !(b->tp_part = (float*)own(s, (size_t)MB * s->dim * 4))) return false;
     if (!b->hidden || !b->qkv || !b->attn || !b->ffn_h || !b->logits || !b->xh || !b->xl || !b->sx || !b->part ||
         !b->part2 || !b->part3 || !b->apart || !b->counters || !b->tokens || !b->n_prompt || !b->keys || !b->kc || !b->vc || !b->st)
         return false;
@@ -1764,13 +1777,26 @@ template <class M, class Bind>
 llamini_batch* batch_create(M* model, u32 max_batch, u32 max_seq, Bind bind) {
     if (!ensure_device()) return nullptr;
     if (max_batch == 0 || max_batch > 64) { set_error("batched decode: batch %u outside 1..64", max_batch); return nullptr; }
-    if (tp().world > 1) { set_error("batched decode: not available in a tensor-parallel group"); return nullptr; }
     if (max_seq == 0) { set_error("batched decode: max_seq 0"); return nullptr; }
     auto* b = new llamini_batch();
     b->w = new llamini_session();
     b->max_batch = max_batch;
     b->max_seq = max_seq;
-    if (!bind(b->w, model, max_seq) || !batch_alloc(b)) { batch_destroy(b); return nullptr; }
+    if (!bind(b->w, model, max_seq)) { batch_destroy(b); return nullptr; }
+    // a tensor-parallel group: LLaMA-family models (the shards bind_llama cuts)
+    // on the tensor-core GEMM, the batch's columns allreduced after o and down
+    if (tp().world > 1 && (b->w->tp_world < 2 || (u64)max_batch * b->w->dim > kTpWideFloats)) {
+        set_error("batched decode: a tensor-parallel group takes LLaMA-family batches of at most %u x dim floats",
+                  kTpWideFloats);
+        batch_destroy(b);
+        return nullptr;
+    }
+    if (!batch_alloc(b)) { batch_destroy(b); return nullptr; }
+    if (b->w->tp_world > 1 && !b->tc) {
+        set_error("batched decode: a tensor-parallel group needs the tensor-core GEMM");
+        batch_destroy(b);
+        return nullptr;
+    }
     b->B = 0;
     return b;
 }
@@ -1806,7 +1832,8 @@ bool prefill_enabled() {
 bool prefill_build(llamini_session* s) {
     if (s->pf_state) return s->pf_state > 0;
     s->pf_state = -1;
-    if (s->tp_world > 1 || (s->kind != 0 && s->kind != 1)) return false;
+    if ((s->kind != 0 && s->kind != 1) || (s->tp_world > 1 && (s->kind != 0 || (u64)kPfChunk * s->dim > kTpWideFloats)))
+        return false;
     Prefill* pf = new Prefill();
     s->pf = pf;
     if (!make_pitched_all(s, pf->pitched)) return false;
@@ -1854,6 +1881,7 @@ bool prefill_build(llamini_session* s) {
     pf->part2 = (float*)own(s, pmax * 4);
     pf->part3 = (float*)own(s, pmax * 4);
     pf->err = (uint32_t*)own(s, 4);
+    if (s->tp_world > 1 && !(pf->tp_part = (float*)own(s, (size_t)C * s->dim * 4))) return false;
     if (!pf->hidden || !pf->qkv || !pf->attn || !pf->ffn_h || !pf->osc || !pf->xh || !pf->xl || !pf->part ||
         !pf->part2 || !pf->part3 || !pf->err || !LM_CUDA(cudaMemset(pf->err, 0, 4)))
         return false;
@@ -1861,19 +1889,54 @@ bool prefill_build(llamini_session* s) {
     return true;
 }
 
-// Positions p0 .. p0 + C - 1 through every layer (their cache rows written);
-// with `score`, also the final norm, lm_head and the log-prob of each scored
-// position's next token (positions up to `last`) into pf->lp.
-bool prefill_chunk(llamini_session* s, u32 p0, u32 C, cudaStream_t st, bool score = false, u32 last = 0) {
+// The columns of a prefill chunk: cp consecutive positions of each of ns
+// sequences (column i * cp + j is position p0 + j of sequence i), with where
+// their tokens and cache rows live.
+struct PfCols {
+    const u32* tokens = nullptr;          // sequence i's tokens at tokens + i * tok_stride
+    u32 tok_stride = 0;
+    void *kc = nullptr, *vc = nullptr;    // layer 0 of sequence 0
+    size_t layer_bytes = 0;               // from one layer's cache to the next
+    size_t seq_bytes = 0;                 // from one sequence's cache to the next (same layer)
+    u32 ns = 1, cp = 0, kv_f16 = 0, max_seq = 0;
+};
+
+// A single session's chunk of C positions.
+PfCols session_cols(const llamini_session* s, u32 C) {
+    PfCols c;
+    c.tokens = s->tokens;
+    c.kc = s->kc;
+    c.vc = s->vc;
+    c.layer_bytes = (size_t)s->n_kv * s->max_seq * s->hd * (s->kv_f16 ? 2 : 4);
+    c.cp = C;
+    c.kv_f16 = s->kv_f16;
+    c.max_seq = s->max_seq;
+    return c;
+}
+
+// The chunk's positions p0 .. p0 + cp - 1 of each of its sequences through
+// every layer (their cache rows written); with `score` (one sequence), also
+// the final norm, lm_head and the log-prob of each scored position's next
+// token (positions up to `last`) into pf->lp.
+bool prefill_chunk(llamini_session* s, const PfCols& cols, u32 p0, cudaStream_t st, bool score = false,
+                   u32 last = 0) {
     Prefill* pf = s->pf;
     const bool gpt2 = s->kind == 1;
     const u32 qkvd = s->qd + 2 * s->kvd, L = s->n_layers;
     const u32 norm = gpt2 ? NORM_LAYER : NORM_RMS;
+    const u32 C = cols.ns * cols.cp;
     const u32 np = (C + 15) & ~15u;
+    const uint64_t seq_elems = cols.seq_bytes / (cols.kv_f16 ? 2 : 4);
+    if (C == 0 || C > kPfChunk || (score && cols.ns != 1)) {
+        set_error("prefill: a chunk of %u x %u columns", cols.ns, cols.cp);
+        return false;
+    }
     PEmbedArgs e;
-    e.tokens = s->tokens;
+    e.tokens = cols.tokens;
     e.p0 = p0;
     e.C = C;
+    e.cp = cols.cp;
+    e.tok_stride = cols.tok_stride;
     e.tok = s->tok;
     e.pos = s->pos_tab;
     e.scale = s->emb_scale;
@@ -1917,7 +1980,6 @@ bool prefill_chunk(llamini_session* s, u32 p0, u32 C, cudaStream_t st, bool scor
         f.ldo = ldo;
         return f;
     };
-    const size_t per_layer = (size_t)s->n_kv * s->max_seq * s->hd * (s->kv_f16 ? 2 : 4);
     for (u32 l = 0; l < L; l++) {
         const llamini_session::Layer& W = s->layers[l];
         TGemmArgs g;
@@ -1940,20 +2002,22 @@ bool prefill_chunk(llamini_session* s, u32 p0, u32 C, cudaStream_t st, bool scor
             f.bias_c = W.bv;
             if (!launch_bfinish(f, st)) return false;
         }
-        void* kc = (uint8_t*)s->kc + l * per_layer;
-        void* vc = (uint8_t*)s->vc + l * per_layer;
+        void* kc = (uint8_t*)cols.kc + l * cols.layer_bytes;
+        void* vc = (uint8_t*)cols.vc + l * cols.layer_bytes;
         PRopeArgs r;
         r.qkv = pf->qkv;
         r.qkv_stride = qkvd;
         r.kc = kc;
         r.vc = vc;
-        r.kv_f16 = s->kv_f16;
+        r.kv_f16 = cols.kv_f16;
         r.n_heads = s->n_heads;
         r.n_kv = s->n_kv;
         r.hd = s->hd;
-        r.max_seq = s->max_seq;
+        r.max_seq = cols.max_seq;
         r.p0 = p0;
         r.rope = s->rope_mode;
+        r.cp = cols.cp;
+        r.seq_elems = seq_elems;
         r.theta = s->theta;
         if (!launch_prope(r, C, st)) return false;
         PAttnArgs at;
@@ -1961,21 +2025,29 @@ bool prefill_chunk(llamini_session* s, u32 p0, u32 C, cudaStream_t st, bool scor
         at.qkv_stride = qkvd;
         at.kc = kc;
         at.vc = vc;
-        at.kv_f16 = s->kv_f16;
+        at.kv_f16 = cols.kv_f16;
         at.out = pf->attn;
         at.out_stride = s->qd;
         at.n_heads = s->n_heads;
         at.n_kv = s->n_kv;
         at.hd = s->hd;
-        at.max_seq = s->max_seq;
+        at.max_seq = cols.max_seq;
         at.p0 = p0;
         at.C = C;
+        at.cp = cols.cp;
+        at.seq_elems = seq_elems;
         if (!launch_pattn(at, st)) return false;
+        // the residual adds after o and down; in a tensor-parallel group the
+        // ranks' partial sums are added by the wide allreduce (bias on rank 0)
+        auto resid = [&](const TGemmArgs& gg, const float* bias) {
+            if (s->tp_world == 1) return launch_bfinish(fin(gg, 0, nullptr, EPI_RESID, bias, pf->hidden, s->dim), st);
+            return launch_bfinish(fin(gg, 0, nullptr, EPI_STORE, tp().rank == 0 ? bias : nullptr, pf->tp_part, s->dim), st) &&
+                   launch_tp_allreduce_wide(pf->tp_part, pf->hidden, C * s->dim, pf->err, st);
+        };
         {
             const DevMat* mm[1] = {&W.o};
             float* pp[1] = {pf->part};
-            if (!stage(pf->attn, s->qd, NORM_NONE, nullptr, nullptr) || !gemm(mm, pp, 1, s->qd, &g) ||
-                !launch_bfinish(fin(g, 0, nullptr, EPI_RESID, W.bo, pf->hidden, s->dim), st))
+            if (!stage(pf->attn, s->qd, NORM_NONE, nullptr, nullptr) || !gemm(mm, pp, 1, s->qd, &g) || !resid(g, W.bo))
                 return false;
         }
         if (!stage(pf->hidden, s->dim, norm, W.n2w, W.n2b)) return false;
@@ -1995,7 +2067,7 @@ bool prefill_chunk(llamini_session* s, u32 p0, u32 C, cudaStream_t st, bool scor
             const DevMat* mm[1] = {&W.down};
             float* pp[1] = {pf->part};
             if (!stage(pf->ffn_h, s->ffn, NORM_NONE, nullptr, nullptr) || !gemm(mm, pp, 1, s->ffn, &g) ||
-                !launch_bfinish(fin(g, 0, nullptr, EPI_RESID, W.bdown, pf->hidden, s->dim), st))
+                !resid(g, W.bdown))
                 return false;
         }
     }
@@ -2012,7 +2084,7 @@ bool prefill_chunk(llamini_session* s, u32 p0, u32 C, cudaStream_t st, bool scor
         n.logits = pf->logits;
         n.vocab = s->vocab;
         n.ld = s->vocab;
-        n.tokens = s->tokens;
+        n.tokens = cols.tokens;
         n.p0 = p0;
         n.C = C;
         n.last = last;
@@ -2048,7 +2120,7 @@ int prefill_perplexity(llamini_session* s, u32 steps, double* nll) {
     cudaStream_t st = stream();
     for (u32 done = 0; done < steps;) {
         const u32 C = steps - done < kPfChunk ? steps - done : kPfChunk;
-        if (!prefill_chunk(s, done, C, st, true, steps - 1)) return -1;
+        if (!prefill_chunk(s, session_cols(s, C), done, st, true, steps - 1)) return -1;
         done += C;
     }
     std::vector<float> lp(steps);
@@ -2078,7 +2150,7 @@ bool run_prompt(llamini_session* s, u32 n) {
     cudaStream_t st = stream();
     for (u32 done = 0; done < n;) {
         const u32 C = n - done < kPfChunk ? n - done : kPfChunk;
-        if (!prefill_chunk(s, s->pos + done, C, st)) return false;
+        if (!prefill_chunk(s, session_cols(s, C), s->pos + done, st)) return false;
         done += C;
     }
     // the decode steps continue at the position after the prompt chunk
@@ -2095,10 +2167,60 @@ bool run_prompt(llamini_session* s, u32 n) {
            LM_CUDA(cudaStreamSynchronize(st));
 }
 
+// Lockstep positions pos .. pos + n - 1 of a batch whose next token is still
+// every sequence's prompt (no sequence writes a token there): prefill chunks
+// of cp positions x ns sequences (64 columns; cp = 64 / B), written into the
+// batch's caches. The next lockstep step starts at the position after them.
+bool batch_prefill(llamini_batch* b, u32 n) {
+    llamini_session* s = b->w;
+    cudaStream_t st = stream();
+    const u32 B = b->B, cp = B >= kPfChunk ? 1u : kPfChunk / B, ns_max = kPfChunk / cp;
+    const size_t per_seq = batch_cache_bytes_per_seq(b);
+    const u32 stride = b->max_seq + 1;
+    for (u32 done = 0; done < n;) {
+        const u32 c = n - done < cp ? n - done : cp;
+        for (u32 i0 = 0; i0 < B; i0 += ns_max) {
+            PfCols pc;
+            pc.tokens = b->tokens + (size_t)i0 * stride;
+            pc.tok_stride = stride;
+            pc.kc = (uint8_t*)b->kc + (size_t)i0 * per_seq;
+            pc.vc = (uint8_t*)b->vc + (size_t)i0 * per_seq;
+            pc.layer_bytes = (size_t)b->max_batch * per_seq;
+            pc.seq_bytes = per_seq;
+            pc.ns = B - i0 < ns_max ? B - i0 : ns_max;
+            pc.cp = c;
+            pc.kv_f16 = b->kv_f16;
+            pc.max_seq = b->max_seq;
+            if (!prefill_chunk(s, pc, b->pos + done, st)) return false;
+        }
+        done += c;
+    }
+    if (!LM_CUDA(cudaStreamSynchronize(st))) return false;
+    uint32_t e = 0;
+    if (!LM_CUDA(cudaMemcpy(&e, s->pf->err, 4, cudaMemcpyDeviceToHost))) return false;
+    if (e) {
+        set_error("prefill: tensor-core GEMM: %s", (e & 1u) ? "a pipeline wait ran out" : "a weight outside the fp16 range");
+        return false;
+    }
+    b->pos += n;
+    const u32 pos = b->pos;
+    return LM_CUDA(cudaMemcpy(&b->st->pos, &pos, 4, cudaMemcpyHostToDevice));
+}
+
 bool batch_run(llamini_batch* b, u32 n) {
     if ((u64)b->pos + n > b->w->max_pos) {
         set_error("batched decode: position %u + %u steps passes the capacity %u", b->pos, n, b->w->max_pos);
         return false;
+    }
+    // positions before every sequence's last prompt token: prefill
+    u32 common = 0xFFFFFFFFu;
+    for (u32 L : b->lens) common = L < common ? L : common;
+    u32 pre = b->pos + 1 < common ? common - 1 - b->pos : 0;
+    if (pre > n) pre = n;
+    if (pre >= 2 && prefill_enabled() && prefill_build(b->w)) {
+        if (!batch_prefill(b, pre)) return false;
+        n -= pre;
+        if (n == 0) return true;
     }
     cudaStream_t st = stream();
     if (b->plan_B != b->B) {

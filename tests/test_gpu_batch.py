@@ -148,3 +148,86 @@ def test_batch_workload_golden_stream(gpu, synth, golden, name):
     finally:
         L.llamini_batch_free(b)
         m.close()
+
+
+def _run_batch(gpu, m, prompts, calls, max_batch):
+    """Tokens of every sequence after llamini_batch_step(b, n) for each n of `calls`."""
+    L = gpu.lib()
+    b = _batch(gpu, m, max_batch, m.max_seq)
+    try:
+        _begin(gpu, b, prompts)
+        for n in calls:
+            assert L.llamini_batch_step(b, n) == 0, gpu.last_error()
+        steps = sum(calls)
+        assert L.llamini_batch_pos(b) == steps
+        toks = [_tokens(gpu, b, s, steps + 1) for s in range(len(prompts))]
+        lg = np.zeros(m.vocab, np.float32)
+        assert L.llamini_batch_logits(b, 0, gpu.ptr(lg)) == 0, gpu.last_error()
+        return toks, lg
+    finally:
+        L.llamini_batch_free(b)
+
+
+@pytest.mark.parametrize("name,n_seq", [("tiny_llama", 3), ("tiny_gpt2", 3), ("tiny_qwen2", 8), ("tiny_llama", 64)])
+def test_batch_prompt_prefill(gpu, orc, tiny, golden, name, n_seq):
+    """Lockstep positions inside every sequence's prompt run as prefill chunks of
+    64 / B positions x B sequences (B = 3: 21 x 3, B = 8: 8 x 8, B = 64: 1 x 64)
+    into the batch's caches. The streams equal the one-position-at-a-time batch
+    (prefill off), the single-sequence path and, for the golden prompt, the
+    reference's; the last step's logits stay within 1e-3 of the oracle. Steps
+    come in calls that stop inside the prompt, at its end and past it."""
+    path = tiny.ensure(name)
+    m = gpu.Model(path)
+    L = gpu.lib()
+    g = golden["tokens"][name]
+    rng = np.random.default_rng(11)
+    base = list(g["prompt"]) + rng.integers(3, m.vocab, 20).tolist()       # 36 tokens
+    prompts = [base] + [rng.integers(3, m.vocab, int(rng.integers(24, 40))).tolist() for _ in range(n_seq - 1)]
+    common = min(len(p) for p in prompts)
+    steps = min(m.max_seq, 64) - 1
+    calls = [5, common - 1 - 5 - 3, 3 + 4, steps - (common - 1) - 4]
+    assert all(c > 0 for c in calls)
+    try:
+        got, lg = _run_batch(gpu, m, prompts, calls, n_seq)
+        assert L.llamini_set_prefill(0) == 0
+        try:
+            want, lg_off = _run_batch(gpu, m, prompts, calls, n_seq)
+        finally:
+            L.llamini_set_prefill(-1)
+        assert got == want
+        for s in range(min(n_seq, 4)):
+            alone = m.generate(np.array(prompts[s], np.uint32), steps + 1 - len(prompts[s])).tolist()
+            assert got[s] == alone[:steps + 1], s
+        # the golden prompt's first 16 tokens, then the sequence's own prompt
+        o = orc.oracle_model(path)
+        want_lg = None
+        for pos in range(steps):
+            want_lg = o.forward(pos, got[0][pos])
+        assert rel_l2(lg, want_lg) < TOL, rel_l2(lg, want_lg)
+        assert rel_l2(lg_off, want_lg) < TOL
+    finally:
+        m.close()
+
+
+def test_batch_prefill_workload_golden(gpu, synth, golden):
+    """llama_1b, 4 sequences sharing the golden 128-token prompt's length: 126
+    positions of prefill (16 x 4 columns per chunk), then the reference's
+    stream for 24 generated tokens on the golden sequence."""
+    g = golden["tokens"]["llama_1b"]
+    m = gpu.Model(synth.ensure_workload("llama_1b"), max_seq=512)
+    L = gpu.lib()
+    rng = np.random.default_rng(5)
+    n = len(g["prompt"])
+    prompts = [g["prompt"]] + [rng.integers(3, m.vocab, n + d).tolist() for d in (0, 3, 9)]
+    steps = n - 1 + 24
+    b = _batch(gpu, m, 4, 512)
+    try:
+        _begin(gpu, b, prompts)
+        assert L.llamini_batch_step(b, steps) == 0, gpu.last_error()
+        assert _tokens(gpu, b, 0, steps + 1) == g["tokens"][:steps + 1]
+        got = _tokens(gpu, b, 2, steps + 1)
+        alone = m.generate(np.array(prompts[2], np.uint32), steps + 1 - len(prompts[2])).tolist()
+        assert got == alone[:steps + 1]
+    finally:
+        L.llamini_batch_free(b)
+        m.close()

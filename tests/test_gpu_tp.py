@@ -96,3 +96,106 @@ def test_tp_two_ranks_match_oracle(orc, tiny):
         for pos in range(6):
             assert rel_l2(lgs[pos], want[pos]) < TOL, (rank, pos, rel_l2(lgs[pos], want[pos]))
     assert np.array_equal(res[0][2].view(np.uint32), res[1][2].view(np.uint32))
+
+
+def _rank_batch(rank, world, port, path, long_prompt, n_gen, prompts, steps, q):
+    """One rank: a long-prompt generate (chunked prefill with the wide
+    allreduce) and a batch of ragged prompts (prefill chunks, then lockstep
+    steps) in the tensor-parallel group."""
+    import datetime
+    import importlib.util
+    import ctypes as C
+    import torch.distributed as dist
+    import torch
+    spec = importlib.util.spec_from_file_location("llamini_b200", os.path.join(ROOT, "llamini.cpp_b200", "__init__.py"))
+    lm = importlib.util.module_from_spec(spec)
+    sys.modules["llamini_b200"] = lm
+    spec.loader.exec_module(lm)
+    L = lm.lib()
+    try:
+        assert L.llamini_set_device(rank) == 0, lm.last_error()
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:%d" % port, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120))
+        h = np.zeros(64, np.uint8)
+        assert L.llamini_tp_handle(lm.ptr(h)) == 0, lm.last_error()
+        mine = torch.from_numpy(h)
+        hs = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(hs, mine)
+        allh = np.ascontiguousarray(np.concatenate([x.numpy() for x in hs]))
+        assert L.llamini_tp_join(rank, world, lm.ptr(allh)) == 0, lm.last_error()
+        m = lm.Model(path)
+        long_toks = m.generate(np.array(long_prompt, np.uint32), n_gen).tolist()
+        b = L.llamini_llama_batch(C.byref(m.model), len(prompts), m.max_seq)
+        assert b, lm.last_error()
+        flat = np.concatenate([np.asarray(p, np.uint32) for p in prompts])
+        lens = np.array([len(p) for p in prompts], np.uint32)
+        assert L.llamini_batch_begin(b, len(prompts), lm.ptr(flat), lm.ptr(lens)) == 0, lm.last_error()
+        assert L.llamini_batch_step(b, steps) == 0, lm.last_error()
+        btoks = []
+        for s in range(len(prompts)):
+            out = np.zeros(steps + 1, np.uint32)
+            assert L.llamini_batch_tokens(b, s, lm.ptr(out), steps + 1) >= 0, lm.last_error()
+            btoks.append(out.tolist())
+        lg = np.zeros(m.vocab, np.float32)
+        assert L.llamini_batch_logits(b, 0, lm.ptr(lg)) == 0, lm.last_error()
+        L.llamini_batch_free(b)
+        m.close()
+        dist.barrier()
+        q.put((rank, long_toks, btoks, lg, ""))
+        dist.destroy_process_group()
+    except Exception as e:                            # report, then leave: the parent fails the test
+        q.put((rank, None, None, None, repr(e)))
+
+
+def _oracle_stream(o, prompt, total):
+    toks = list(prompt)
+    lg = None
+    for pos in range(total - 1):
+        lg = o.forward(pos, toks[pos])
+        if pos + 1 >= len(prompt):
+            toks.append(int(np.argmax(lg)))
+    return toks, lg
+
+
+def test_tp_two_ranks_prefill_and_batch(orc, tiny):
+    """Two ranks: a 70-token prompt (two prefill chunks whose o / down sums go
+    through the wide allreduce) and a batch of three ragged prompts (prefill
+    chunks of 21 positions x 3 sequences, then lockstep steps with the batch's
+    columns allreduced) both reproduce the oracle's greedy streams; the ranks'
+    tokens and logits are identical."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("tensor parallelism needs two GPUs")
+    path = tiny.ensure("tiny_tp")
+    rng = np.random.default_rng(33)
+    long_prompt = rng.integers(3, 1000, 70).tolist()
+    n_gen = 16
+    prompts = [rng.integers(3, 1000, n).tolist() for n in (24, 31, 27)]
+    steps = 47
+    o = orc.oracle_model(path)
+    want_long, _ = _oracle_stream(o, long_prompt, len(long_prompt) + n_gen)
+    want_b = []
+    want_lg = None
+    for i, p in enumerate(prompts):
+        o = orc.oracle_model(path)
+        t, lg = _oracle_stream(o, p, steps + 1)
+        want_b.append(t)
+        if i == 0:
+            want_lg = lg
+    ctx = mp.get_context("spawn")
+    qq = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_rank_batch, args=(r, 2, port, path, long_prompt, n_gen, prompts, steps, qq))
+          for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted((qq.get(timeout=600) for _ in ps), key=lambda r: r[0])
+    for p in ps:
+        p.join(timeout=120)
+    for rank, lt, bt, lg, err in res:
+        assert lt is not None, (rank, err)
+        assert lt == want_long, (rank, lt, want_long)
+        assert bt == want_b, (rank, bt, want_b)
+        assert rel_l2(lg, want_lg) < TOL, (rank, rel_l2(lg, want_lg))
+    assert np.array_equal(res[0][3].view(np.uint32), res[1][3].view(np.uint32))
