@@ -450,7 +450,112 @@ def run_tp7b(args, lm, L, torch, ws, rank, dist, hbm_peak):
         kvp = L.llamini_session_kv_bytes_per_pos(s)
     finally:
         m.close()
+        if ws > 1:
+            assert L.llamini_tp_leave() == 0, lm.last_error()
+            dist.barrier()
     return ms, wb, kvp, pos0, per_rank[0].tolist(), golden
+
+
+TPDP_BATCH = 64
+
+
+def tp_dp_split(ws, rank, tp_size=0):
+    """The 7B batch-64 leg's split of ws ranks: tensor-parallel groups of T
+    consecutive ranks (T = tp_size, default min(ws, 4)), TPDP_BATCH sequences
+    shared evenly by the ws / T groups. Returns (T, DP, group, rank in group,
+    sequences per group)."""
+    T = tp_size or min(ws, 4)
+    if ws % T or TPDP_BATCH % (ws // T):
+        raise SystemExit("tp_dp_7b_b64: %d ranks do not split into tensor-parallel groups of %d" % (ws, T))
+    DP = ws // T
+    return T, DP, rank // T, rank % T, TPDP_BATCH // DP
+
+
+def tp_dp_groups(dist, ws, T):
+    """Every rank creates every group's process group, in the same order."""
+    return [dist.new_group(list(range(g * T, (g + 1) * T))) for g in range(ws // T)]
+
+
+def run_tp_dp_7b(args, lm, L, torch, ws, rank, dist):
+    """LLaMA at 7B shape, batch 64: tensor parallel over groups of T ranks
+    (T = --b64-tp, default min(ws, 4)) and the 64 sequences split
+    data-parallel over the ws / T groups. Each sequence has its own seeded
+    1024-token prompt, run through the batch's prefill chunks; then warm-up
+    and timed lockstep decode steps. Returns this rank's device time of the
+    timed steps and of the prompt, and the split."""
+    import ctypes as C
+    T, DP, grp, r_in, B = tp_dp_split(ws, rank, args.b64_tp)
+    S = synthetic()
+    directory = os.environ.get("LLAMINI_WORKDIR", "/tmp/llamini_b200")
+    if rank == 0:
+        S.ensure_workload("llama_7b", directory)
+    if dist:
+        dist.barrier()
+    path = S.ensure_workload("llama_7b", directory)
+    group = None
+    if dist and ws > 1:
+        group = tp_dp_groups(dist, ws, T)[grp]
+    if T > 1:
+        h = np.zeros(64, np.uint8)
+        assert L.llamini_tp_handle(lm.ptr(h)) == 0, lm.last_error()
+        mine = torch.from_numpy(h).cuda()
+        hs = [torch.zeros_like(mine) for _ in range(T)]
+        dist.all_gather(hs, mine, group=group)
+        allh = np.ascontiguousarray(np.concatenate([x.cpu().numpy() for x in hs]))
+        assert L.llamini_tp_join(r_in, T, lm.ptr(allh)) == 0, lm.last_error()
+    max_seq = TP_PROMPT + args.warmup + args.b64_steps + 2
+    m = lm.Model(path, max_seq=max_seq)
+    b = None
+    try:
+        b = L.llamini_llama_batch(C.byref(m.model), B, max_seq)
+        assert b, lm.last_error()
+        prompts = np.stack([np.random.default_rng(4000 + grp * B + i).integers(3, m.vocab, TP_PROMPT)
+                            for i in range(B)]).astype(np.uint32)
+        lens = np.full(B, TP_PROMPT, np.uint32)
+        flat = np.ascontiguousarray(prompts.reshape(-1))
+        assert L.llamini_batch_begin(b, B, lm.ptr(flat), lm.ptr(lens)) == 0, lm.last_error()
+        stream = torch.cuda.ExternalStream(L.llamini_stream())
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        assert L.llamini_batch_step(b, TP_PROMPT - 1) == 0, lm.last_error()
+        p1.record(stream)
+        assert L.llamini_batch_step(b, args.warmup) == 0, lm.last_error()
+        torch.cuda.synchronize()
+        prompt_ms = p0.elapsed_time(p1)
+        if dist:
+            dist.barrier()
+        pos0 = L.llamini_batch_pos(b)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        assert L.llamini_batch_step(b, args.b64_steps) == 0, lm.last_error()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        # the group's ranks must have decoded the same tokens (first sequence)
+        n_tok = TP_PROMPT + 8
+        tk = np.zeros(n_tok, np.uint32)
+        assert L.llamini_batch_tokens(b, 0, lm.ptr(tk), n_tok) >= n_tok, lm.last_error()
+        if T > 1:
+            t_mine = torch.from_numpy(tk[TP_PROMPT:].astype(np.int64)).cuda()
+            t_all = [torch.zeros_like(t_mine) for _ in range(T)]
+            dist.all_gather(t_all, t_mine, group=group)
+            if not all(torch.equal(t_all[0], x) for x in t_all):
+                raise SystemExit("tp_dp_7b_b64: group %d's ranks decoded different tokens" % grp)
+        wb = L.llamini_batch_weight_bytes(b)
+        # f32 K and V rows of this rank's kv heads, all layers, per position per sequence
+        kvp = 2 * 32 * (4096 // T) * 4
+    finally:
+        if b:
+            L.llamini_batch_free(b)
+        m.close()
+        if T > 1:
+            assert L.llamini_tp_leave() == 0, lm.last_error()
+        if dist:
+            dist.barrier()
+    return ms, prompt_ms, T, DP, B, wb, kvp, pos0
 
 
 def run_perplexity(lm, L, model, n_tok=1024):
@@ -568,6 +673,7 @@ def run_ours(args, ws, rank, local):
     ppl = None if (rank != 0 or args.no_ppl) else run_perplexity(lm, L, model)
     model.close()
     tp7 = None if args.no_tp7b else run_tp7b(args, lm, L, torch, ws, rank, dist, hbm_peak)
+    tpdp = None if args.no_b64_7b else run_tp_dp_7b(args, lm, L, torch, ws, rank, dist)
     qwen = None if (rank != 0 or args.no_qwen2) else run_qwen2(args, lm, L, torch, hbm_peak)
     sweep = None if (rank != 0 or args.no_sweep) else run_gemv_sweep(lm, L, torch,
                                                                      torch.cuda.ExternalStream(L.llamini_stream()),
@@ -575,6 +681,7 @@ def run_ours(args, ws, rank, local):
     t_max, e2e_max = max_over_ranks(dist, [ms, e2e_s])
     b_max = max_over_ranks(dist, [bt[0]])[0] if bt else None
     tp_max = max_over_ranks(dist, [tp7[0]])[0] if tp7 else None
+    tpdp_max = max_over_ranks(dist, [tpdp[0], tpdp[1]]) if tpdp else None
     if rank == 0:
         steps = args.steps
         value = whole_job_rate(ws, steps, t_max)
@@ -644,6 +751,26 @@ def run_ours(args, ws, rank, local):
                 "reference_stream_match": tp7[5],
                 # embed, 5 per layer (+ 2 allreduces per layer when split), lm_head, finish
                 "gpu_launches": args.tp_steps * (1 + 32 * (5 + (2 if ws > 1 else 0)) + 2)}
+        if tpdp:
+            d_ms, d_pms = tpdp_max
+            T, DP, B, wb, kvp, dpos0 = tpdp[2:]
+            d_step_s = d_ms / 1e3 / args.b64_steps
+            d_bytes = wb + kvp * B * (dpos0 + (args.b64_steps - 1) / 2 + 1)
+            line["tp_dp_7b_b64"] = {
+                "value": round(TPDP_BATCH * args.b64_steps / (d_ms / 1e3), 1), "unit": "tok/s",
+                "tp": T, "dp": DP, "batch": TPDP_BATCH, "per_group_batch": B, "steps": args.b64_steps,
+                "ms_per_step": round(d_ms / args.b64_steps, 4), "scaling": "strong",
+                "workload": "llama_7b (7B shape, Q4_K_M mix, seed 4), 64 sequences with seeded 1024-token "
+                            "prompts; timed lockstep decode positions %d..%d; tensor parallel over %d rank(s) "
+                            "per group, %d group(s) with %d sequences each" %
+                            (dpos0, dpos0 + args.b64_steps - 1, T, DP, B),
+                "per_gpu_bytes_per_step": int(d_bytes),
+                "per_gpu_stream_gbs": round(d_bytes / d_step_s / 1e9, 1),
+                "prompt": {"value": round(TPDP_BATCH * (TP_PROMPT - 1) / (d_pms / 1e3), 1), "unit": "positions/s",
+                           "ms": round(d_pms, 1),
+                           "path": ("prefill chunks of %d positions x %d sequences (tcgen05 GEMM)" % (64 // B, B))
+                           if B <= 32 else "lockstep batch steps (64 columns per weight pass either way)"},
+                "tokens_rank_identical": True}
         if qwen:
             line["qwen2_05b"] = qwen
         if sweep:
@@ -760,6 +887,10 @@ def main():
     ap.add_argument("--no-qwen2", action="store_true", help="skip the Qwen2-0.5B batch 1 / batch 32 legs")
     ap.add_argument("--no-sweep", action="store_true", help="skip the isolated GEMV sweep (6 shapes x 7 formats x 3 batches)")
     ap.add_argument("--tp-steps", type=int, default=64, help="timed decode steps of the 7B-shape leg")
+    ap.add_argument("--no-b64-7b", action="store_true", help="skip the 7B-shape batch-64 TP x DP leg")
+    ap.add_argument("--b64-steps", type=int, default=16, help="timed decode steps of the 7B batch-64 leg")
+    ap.add_argument("--b64-tp", type=int, default=0, help="tensor-parallel group size of the 7B batch-64 leg "
+                                                           "(default min(gpus, 4))")
     ap.add_argument("--profile-batch", action="store_true",
                     help="no bench line: only a short batch-64 run of llama_1b for profilers "
                          "(4-token prompts, 3 batch steps of identical launch sequences)")

@@ -213,8 +213,17 @@ int llamini_tp_handle(void* out64);
  * computes the same logits. After the o projection and after ffn_down the
  * ranks' partial sums are added over NVLink (bounded waits; a rank that does not
  * arrive within 2 s sets the session's error). world = 1 leaves the group setting
- * at one rank. Batched sessions are refused in a group. */
+ * at one rank. Prompt chunks (prefill) and batched sessions (LLaMA family, on
+ * the tensor-core GEMM, at most 524288 / dim sequences) add their columns'
+ * partial sums the same way, slice by slice. */
 int llamini_tp_join(u32 rank, u32 world, const void* handles);
+/* Leave the group (after the device has finished every step of the group's
+ * sessions): unmaps the peers' buffers and clears this rank's buffer and
+ * counters, so the process can join another group. Every rank of the group
+ * leaves, and the ranks pass a host barrier before any of them joins again.
+ * Sessions built in the group must not step afterwards. Returns 0 (also when
+ * not in a group), -1 on a CUDA error. */
+int llamini_tp_leave(void);
 /* The shard a LLaMA session of rank `rank` in a group of `world` holds (the
  * plan llamini_tp_join's sessions use; no device needed): out[0..8) = {first
  * head, end head, first kv head, end kv head, first FFN column, end FFN column,

@@ -167,6 +167,7 @@ SIGNATURES = {
     "llamini_session_prefill": (C.c_int, [P]),
     "llamini_tp_handle": (C.c_int, [P]),
     "llamini_tp_join": (C.c_int, [C.c_uint32, C.c_uint32, P]),
+    "llamini_tp_leave": (C.c_int, []),
     "llamini_tp_plan": (C.c_int, [u32, u32, u32, u32, u32, u32, P]),
     "llamini_tp_rank": (C.c_int, []),
     "llamini_tp_world": (C.c_int, []),

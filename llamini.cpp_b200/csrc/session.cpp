@@ -2171,6 +2171,7 @@ bool run_prompt(llamini_session* s, u32 n) {
 // every sequence's prompt (no sequence writes a token there): prefill chunks
 // of cp positions x ns sequences (64 columns; cp = 64 / B), written into the
 // batch's caches. The next lockstep step starts at the position after them.
+// (batch_run takes this path for batches of up to 32 sequences.)
 bool batch_prefill(llamini_batch* b, u32 n) {
     llamini_session* s = b->w;
     cudaStream_t st = stream();
@@ -2217,7 +2218,10 @@ bool batch_run(llamini_batch* b, u32 n) {
     for (u32 L : b->lens) common = L < common ? L : common;
     u32 pre = b->pos + 1 < common ? common - 1 - b->pos : 0;
     if (pre > n) pre = n;
-    if (pre >= 2 && prefill_enabled() && prefill_build(b->w)) {
+    // at most 32 sequences (two or more positions per sequence in a chunk):
+    // with one position per sequence a chunk reads the weights as often as the
+    // lockstep steps, and the lockstep's split attention is the faster one
+    if (pre >= 2 && b->B <= kPfChunk / 2 && prefill_enabled() && prefill_build(b->w)) {
         if (!batch_prefill(b, pre)) return false;
         n -= pre;
         if (n == 0) return true;
@@ -2460,6 +2464,21 @@ int llamini_tp_join(u32 rank, u32 world, const void* handles) {
     T.rank = rank;
     T.world = world;
     return 0;
+}
+
+int llamini_tp_leave(void) {
+    lm::TpState& T = lm::tp();
+    if (T.world < 2) return 0;
+    if (!LM_CUDA(cudaDeviceSynchronize())) return -1;
+    for (u32 j = 0; j < T.world; j++)
+        if (j != T.rank && T.peer[j]) cudaIpcCloseMemHandle(T.peer[j]);
+    for (u32 j = 0; j < lm::kTpMaxRanks; j++) T.peer[j] = nullptr;
+    T.rank = 0;
+    T.world = 1;
+    // flags and counters from zero for the next group
+    return LM_CUDA(cudaMemset(T.local, 0, lm::tp_buffer_bytes())) &&
+                   LM_CUDA(cudaMemset(T.gen, 0, 4 * (1 + lm::kTpWideCtas))) && LM_CUDA(cudaDeviceSynchronize())
+               ? 0 : -1;
 }
 
 int llamini_tp_plan(u32 world, u32 rank, u32 n_heads, u32 n_kv, u32 head_dim, u32 ffn, u32* out) {

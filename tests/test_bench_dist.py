@@ -68,3 +68,45 @@ def test_single_rank_helpers():
     b = _bench()
     assert b.max_over_ranks(None, [1.5, float("nan")])[0] == 1.5
     assert b.whole_job_rate(1, 256, 1000.0) == pytest.approx(256.0)
+
+
+def _rank_groups(rank, ws, port, out):
+    import torch
+    import torch.distributed as dist
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "RANK": str(rank),
+                       "WORLD_SIZE": str(ws), "LOCAL_RANK": str(rank)})
+    b = _bench()
+    d = b.init_dist(ws, rank, "gloo")
+    T, DP, grp, r_in, B = b.tp_dp_split(ws, rank, 2)
+    group = b.tp_dp_groups(d, ws, T)[grp]
+    mine = torch.tensor([rank])
+    got = [torch.zeros_like(mine) for _ in range(T)]
+    dist.all_gather(got, mine, group=group)
+    out.put((rank, (T, DP, grp, r_in, B), [int(x) for x in got]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_four_ranks_tp_dp_groups():
+    """The 7B batch-64 leg on 4 ranks with tensor-parallel groups of 2: groups
+    {0, 1} and {2, 3}, 32 sequences each; a group's all_gather sees only its
+    own ranks (the handle exchange of llamini_tp_join)."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_rank_groups, args=(r, 4, port, q)) for r in range(4)]
+    for p in ps:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in ps)
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, split, members in res:
+        assert split == (2, 2, rank // 2, rank % 2, 32)
+        assert members == [2 * (rank // 2), 2 * (rank // 2) + 1]
+    b = _bench()
+    assert b.tp_dp_split(8, 5) == (4, 2, 1, 1, 32)
+    assert b.tp_dp_split(1, 0) == (1, 1, 0, 0, 64)
+    with pytest.raises(SystemExit):
+        b.tp_dp_split(6, 0, 4)

@@ -168,14 +168,16 @@ def _run_batch(gpu, m, prompts, calls, max_batch):
         L.llamini_batch_free(b)
 
 
-@pytest.mark.parametrize("name,n_seq", [("tiny_llama", 3), ("tiny_gpt2", 3), ("tiny_qwen2", 8), ("tiny_llama", 64)])
+@pytest.mark.parametrize("name,n_seq", [("tiny_llama", 3), ("tiny_gpt2", 3), ("tiny_qwen2", 8), ("tiny_llama", 32),
+                                        ("tiny_llama", 64)])
 def test_batch_prompt_prefill(gpu, orc, tiny, golden, name, n_seq):
     """Lockstep positions inside every sequence's prompt run as prefill chunks of
-    64 / B positions x B sequences (B = 3: 21 x 3, B = 8: 8 x 8, B = 64: 1 x 64)
-    into the batch's caches. The streams equal the one-position-at-a-time batch
-    (prefill off), the single-sequence path and, for the golden prompt, the
-    reference's; the last step's logits stay within 1e-3 of the oracle. Steps
-    come in calls that stop inside the prompt, at its end and past it."""
+    64 / B positions x B sequences (B = 3: 21 x 3, B = 8: 8 x 8, B = 32: 2 x
+    32) into the batch's caches; B = 64 keeps the lockstep steps. The streams
+    equal the one-position-at-a-time batch (prefill off), the single-sequence
+    path and, for the golden prompt, the reference's; the last step's logits
+    stay within 1e-3 of the oracle. Steps come in calls that stop inside the
+    prompt, at its end and past it."""
     path = tiny.ensure(name)
     m = gpu.Model(path)
     L = gpu.lib()
