@@ -612,6 +612,37 @@ def profile_batch():
     print(json.dumps({"profile_batch": "ok", "sequences": GLOBAL_BATCH, "steps": 3}))
 
 
+def profile_prefill(name):
+    """A profiler's workload: one prompt of a named workload (qwen2_05b: 512
+    tokens, llama_7b: 1024) through the chunked prefill (tcgen05 GEMMs, 64
+    positions per chunk), run twice; prints the second run's device time."""
+    import torch
+    lm = pkg()
+    L = lm.lib()
+    n = {"qwen2_05b": QWEN_PROMPT, "llama_7b": TP_PROMPT}[name]
+    S = synthetic()
+    path = S.ensure_workload(name, os.environ.get("LLAMINI_WORKDIR", "/tmp/llamini_b200"))
+    model = lm.Model(path, max_seq=n + 8)
+    try:
+        s = model.session()
+        prompt = S.workload_prompt(name, n)
+        stream = torch.cuda.ExternalStream(L.llamini_stream())
+        ms = None
+        for _ in range(2):
+            assert L.llamini_session_begin(s, lm.ptr(prompt), n) == 0, lm.last_error()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            assert L.llamini_session_step(s, n - 1) == 0, lm.last_error()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+        assert L.llamini_session_prefill(s) == 1, "the prompt did not take the prefill path"
+    finally:
+        model.close()
+    print(json.dumps({"profile_prefill": name, "positions": n - 1, "ms": round(ms, 3),
+                      "positions_per_s": round((n - 1) / (ms / 1e3), 1)}))
+
+
 def run_ours(args, ws, rank, local):
     import torch
     dist = init_dist(ws, local, "nccl")
@@ -894,9 +925,14 @@ def main():
     ap.add_argument("--profile-batch", action="store_true",
                     help="no bench line: only a short batch-64 run of llama_1b for profilers "
                          "(4-token prompts, 3 batch steps of identical launch sequences)")
+    ap.add_argument("--profile-prefill", choices=["qwen2_05b", "llama_7b"],
+                    help="no bench line: only one workload's prompt through the chunked prefill, twice")
     args = ap.parse_args()
     if args.profile_batch:
         profile_batch()
+        return
+    if args.profile_prefill:
+        profile_prefill(args.profile_prefill)
         return
     if args.warmup < 3:
         args.warmup = 3
