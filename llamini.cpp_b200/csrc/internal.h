@@ -82,6 +82,24 @@ struct GemvSeg {
 
 constexpr int kMaxSegs = 4;
 
+// Tensor parallelism with the reduction fused into the tensor-core GEMVs
+// (k_gemv_mma.cu): a GEMV whose output is a partial sum (o, ffn_down of a
+// rank's shard) stores its rows straight into fused slot `push` of every rank's
+// buffer (peer memory over NVLink) and signals each rank's arrival counter; the
+// next GEMV reading the residual stream waits for every rank's arrivals of slot
+// `pull`, adds the ranks' rows (rank order) to its input and, in the CTA that
+// finishes last, writes the sum back. kTpNone: no such step.
+constexpr uint32_t kTpNone = 0xFFFFFFFFu;
+constexpr uint32_t kTpFusedFloats = 16384;    // rows of a fused slot (dim <= 16384)
+struct GemvTp {
+    float* slots[8] = {};          // every rank's fused slots [2][8 ranks][kTpFusedFloats]
+    uint32_t* arrive[8] = {};      // every rank's arrival counters [2][8 ranks]
+    uint32_t* gen = nullptr;       // this rank's finished pulls of each slot [2] (device)
+    uint32_t* ticket = nullptr;    // CTAs done reading, per slot [2] (device)
+    uint32_t rank = 0, world = 1;
+    uint32_t push = kTpNone, pull = kTpNone;
+};
+
 struct GemvArgs {
     const float* x = nullptr;      // input vector (normalised first when norm != NONE)
     uint32_t K = 0;
@@ -94,12 +112,15 @@ struct GemvArgs {
     unsigned long long* argmax_key = nullptr;
     float* x_out = nullptr;        // optional: store the normalised x (block 0 writes it)
     uint32_t* err = nullptr;       // error bits (a bounded wait that ran out sets kErrWaitTimeout)
+    GemvTp tp;                     // fused tensor-parallel reduction (tensor-core GEMV only)
 };
 
 bool launch_gemv(const GemvArgs& a, cudaStream_t st);
 // Tensor-core variant (k_gemv_mma.cu); *handled is false when some segment's
 // format has no tensor-core path, and launch_gemv then uses the CUDA-core kernel.
 bool launch_gemv_mma(const GemvArgs& a, cudaStream_t st, bool* handled);
+// Whether launch_gemv runs `a` on the tensor-core kernel.
+bool gemv_mma_takes(const GemvArgs& a);
 
 // Plain multi-column GEMV used by llamini_gemv_* (no fusion).
 bool launch_gemv_plain(uint32_t type, const uint8_t* w, uint32_t rows, uint32_t cols,
@@ -471,6 +492,8 @@ bool tp_alloc_buffer();
 bool launch_tp_allreduce(const float* part, float* out, uint32_t n, uint32_t* err, cudaStream_t st);
 // out[i] += the sum over ranks of part[i], i < n <= kTpWideFloats, slice by slice.
 bool launch_tp_allreduce_wide(const float* part, float* out, uint32_t n, uint32_t* err, cudaStream_t st);
+// The group's fused-reduction pointers (push / pull slots kTpNone).
+GemvTp tp_fused_args(uint32_t push, uint32_t pull);
 
 // ---------------------------------------------------------------- prefill (k_prefill.cu)
 // A chunk's columns are ns sequences x cp positions: column b is position

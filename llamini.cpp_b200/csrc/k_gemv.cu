@@ -279,6 +279,10 @@ bool launch_gemv(const GemvArgs& in, cudaStream_t st) {
         if (!launch_gemv_mma(in, st, &handled)) return false;
         if (handled) return true;
     }
+    if (in.tp.push != kTpNone || in.tp.pull != kTpNone) {
+        set_error("gemv: the fused tensor-parallel reduction runs on the tensor-core GEMV only");
+        return false;
+    }
     size_t smem = gemv_smem(a.K);
     if (smem > 200 * 1024) { set_error("gemv: K=%u too large", a.K); return false; }
     uint32_t want = (tiles + kWarps - 1) / kWarps;

@@ -27,6 +27,7 @@
 #include "mma_gemv.cuh"
 
 #include <cuda_fp16.h>
+#include <cstdlib>
 
 namespace lm {
 
@@ -50,12 +51,84 @@ __device__ void block_sum_max(float& s, float& m, float* red) {
     m = tm;
 }
 
+// ------------------------------------------------------------------ tensor parallelism
+// The fused reduction (GemvTp, internal.h). Every wait is bounded (2 s).
+constexpr uint64_t kTpFuseWaitNs = 2000000000ull;
+__device__ __forceinline__ uint64_t g_time() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ uint32_t ld_acq_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ float ld_rlx_sys(const float* p) {
+    float v;
+    asm volatile("ld.relaxed.sys.global.f32 %0, [%1];\n" : "=f"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Before staging: wait for every rank's rows of slot `pull`, then xf = x +
+// (sum over ranks in rank order) -- the separate allreduce's arithmetic. The
+// CTA that finishes reading last writes the sum back to x (every other CTA has
+// read x by then) and opens the slot's next use. False after a wait ran out.
+__device__ bool tp_pull(const GemvArgs& a, float* xf) {
+    __shared__ uint32_t s_st;
+    const GemvTp& t = a.tp;
+    const uint32_t tid = threadIdx.x, K = a.K, P = t.pull;
+    if (tid == 0) {
+        uint32_t ok = 1;
+        const uint32_t target = (*reinterpret_cast<volatile uint32_t*>(t.gen + P) + 1u) * ((K + 15u) / 16u);
+        const uint32_t* arr = t.arrive[t.rank] + P * 8u;
+        const uint64_t t0 = g_time();
+        for (uint32_t r = 0; r < t.world && ok; r++) {
+            for (uint32_t i = 0;; i++) {
+                if ((int32_t)(ld_acq_sys(arr + r) - target) >= 0) break;
+                if ((i & 63u) == 63u && g_time() - t0 > kTpFuseWaitNs) {
+                    atomicOr(a.err, kErrWaitTimeout);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        s_st = ok;
+    }
+    __syncthreads();
+    if (!s_st) return false;
+    const float* mine = t.slots[t.rank] + (uint64_t)P * 8u * kTpFusedFloats;
+    for (uint32_t i = tid; i < K; i += kMThreads) {
+        float s = 0.f;
+        for (uint32_t r = 0; r < t.world; r++) s += ld_rlx_sys(mine + (uint64_t)r * kTpFusedFloats + i);
+        xf[i] = a.x[i] + s;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        const uint32_t old = atomicAdd(t.ticket + P, 1u);
+        s_st = old + 1u == gridDim.x ? 2u : 1u;
+    }
+    __syncthreads();
+    if (s_st == 2u) {
+        float* xw = const_cast<float*>(a.x);          // the residual stream
+        for (uint32_t i = tid; i < K; i += kMThreads) xw[i] = xf[i];
+        if (tid == 0) {
+            t.ticket[P] = 0u;
+            *reinterpret_cast<volatile uint32_t*>(t.gen + P) = *reinterpret_cast<volatile uint32_t*>(t.gen + P) + 1u;
+        }
+    }
+    return true;
+}
+
 // ------------------------------------------------------------------ x staging
 // Normalise (RMSNorm model.c:4-10 / LayerNorm gpt2.c:130-139), choose E with
 // max|x| 2^E < 2^14, write the fp16 hi/lo split and the scaled 16-element sums.
-__device__ void stage_x(const GemvArgs& a, const MmaSmem& sm, float* s_scale) {
+// x is a.x, or sm.xf itself after tp_pull (each element is read and written by
+// the same thread).
+__device__ void stage_x(const GemvArgs& a, const float* x, const MmaSmem& sm, float* s_scale) {
     const uint32_t K = a.K, n4 = K / 4, tid = threadIdx.x;
-    const float4* x4 = reinterpret_cast<const float4*>(a.x);
+    const float4* x4 = reinterpret_cast<const float4*>(x);
     float4* xf4 = reinterpret_cast<float4*>(sm.xf);
     float s = 0.f, m = 0.f, f = 1.0f;
     if (a.norm == NORM_RMS) {
@@ -205,7 +278,17 @@ gemv_mma_kernel(const __grid_constant__ GemvArgs a, uint32_t stage_bytes, const 
         }
     }
     pdl_wait();                                                   // x comes from the previous kernel
-    stage_x(a, sm, &s_scale);                                     // ends with __syncthreads
+    const bool pulled = a.tp.pull != kTpNone;
+    if (pulled && !tp_pull(a, sm.xf)) {
+        // the error bit is set; the first tiles' copies land before the CTA leaves
+        if (tid == 0)
+            for (uint32_t i = 0; i < kStages; i++)
+                if (blockIdx.x + i * gridDim.x < n_tiles) mbar_wait(&bars[i], 0);
+        return;
+    }
+    stage_x(a, pulled ? sm.xf : a.x, sm, &s_scale);               // ends with __syncthreads
+    const bool push = a.tp.push != kTpNone;
+    const uint64_t push_off = push ? ((uint64_t)a.tp.push * 8u + a.tp.rank) * kTpFusedFloats : 0ull;
 
     const uint32_t lane = tid & 31u, warp = tid >> 5;
     Lane L;
@@ -269,7 +352,15 @@ gemv_mma_kernel(const __grid_constant__ GemvArgs a, uint32_t stage_bytes, const 
             u *= s_scale;
             if (r < tr.nrows) {
                 switch (G.epi) {
-                case EPI_STORE: if (G.bias) v += G.bias[row]; G.out[row] = v; break;
+                case EPI_STORE:
+                    if (G.bias) v += G.bias[row];
+                    if (push) {
+                        // this rank's partial row into every rank's slot (peer memory)
+                        for (uint32_t j = 0; j < a.tp.world; j++) a.tp.slots[j][push_off + row] = v;
+                    } else {
+                        G.out[row] = v;
+                    }
+                    break;
                 case EPI_RESID: if (G.bias) v += G.bias[row]; G.out[row] += v; break;
                 case EPI_GLU_SILU: v = v / (1.0f + expf(-v)) * u; G.out[row] = v; break;   // model.c:22
                 case EPI_GLU_GELU: v = m_gelu(v) * u; G.out[row] = v; break;
@@ -287,6 +378,15 @@ gemv_mma_kernel(const __grid_constant__ GemvArgs a, uint32_t stage_bytes, const 
             if (lane == 0 && key != 0ull) atomicMax(a.argmax_key, key);
         }
         __syncthreads();                          // part[] free for the next tile
+    }
+    if (push) {
+        // this CTA's rows are stored: count its tiles into every rank's arrivals
+        if (tid < 16) __threadfence_system();
+        __syncthreads();
+        if (tid < a.tp.world) {
+            uint32_t* c = a.tp.arrive[tid] + a.tp.push * 8u + a.tp.rank;
+            asm volatile("red.release.sys.global.add.u32 [%0], %1;\n" ::"l"(c), "r"(i) : "memory");
+        }
     }
 }
 
@@ -306,22 +406,24 @@ bool gemv_mma_init() {
            LM_CUDA(cudaFuncSetAttribute(gemv_mma_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
 }
 
-// Launch when every segment is a tensor-core format (a gated pair sharing one
-// format) and the tiles fit in shared memory; *handled = false otherwise, and
-// the caller uses k_gemv.cu.
-bool launch_gemv_mma(const GemvArgs& in, cudaStream_t st, bool* handled) {
-    *handled = false;
-    if (in.K % 32 != 0) return true;
+// The stage size and shared memory of `in` on the tensor-core kernel; false
+// when some segment is not a tensor-core format (a gated pair sharing one
+// format) or the tiles do not fit in shared memory.
+static bool mma_plan(const GemvArgs& in, uint64_t* stage_out, size_t* smem_out) {
+    if (in.K % 32 != 0) return false;
+    if ((in.tp.push != kTpNone || in.tp.pull != kTpNone) &&
+        (in.K > kTpFusedFloats || in.tp.world > 8 || (in.tp.pull != kTpNone && in.x == nullptr)))
+        return false;
     uint64_t stage = 0;
     for (uint32_t i = 0; i < in.nseg; i++) {
         const GemvSeg& g = in.seg[i];
         const bool glu = g.epi == EPI_GLU_SILU || g.epi == EPI_GLU_GELU;
-        if (!mma_type(g.type) || (glu && g.type2 != g.type)) return true;
-        if (type_bytes(g.type, in.K) == 0) return true;
+        if (!mma_type(g.type) || (glu && g.type2 != g.type)) return false;
+        if (type_bytes(g.type, in.K) == 0) return false;
         // bulk copies need 16-byte aligned sources: the matrix base and every
         // tile start (row multiples of 16, so 16 * row_bytes suffices)
         if (reinterpret_cast<uintptr_t>(g.w) % 16 != 0 || (glu && reinterpret_cast<uintptr_t>(g.w2) % 16 != 0))
-            return true;
+            return false;
         const uint64_t t1 = tile_bytes(g.row_bytes);
         const uint64_t t2 = glu ? tile_bytes(g.row_bytes2) : 0;
         stage = stage > t1 + t2 ? stage : t1 + t2;
@@ -330,10 +432,29 @@ bool launch_gemv_mma(const GemvArgs& in, cudaStream_t st, bool* handled) {
     stage = (stage + 16 + 127) & ~uint64_t(127);
     if (in.norm != NORM_NONE && (reinterpret_cast<uintptr_t>(in.norm_w) % 16 != 0 ||
                                  (in.norm == NORM_LAYER && reinterpret_cast<uintptr_t>(in.norm_b) % 16 != 0)))
-        return true;
-    if (reinterpret_cast<uintptr_t>(in.x) % 16 != 0) return true;
+        return false;
+    if (reinterpret_cast<uintptr_t>(in.x) % 16 != 0) return false;
     const size_t smem = kStages * stage + x_smem(in.K) + 128;    // + alignment slack
-    if (smem > kSmemLimit) return true;
+    if (smem > kSmemLimit) return false;
+    *stage_out = stage;
+    *smem_out = smem;
+    return true;
+}
+
+bool gemv_mma_takes(const GemvArgs& a) {
+    static const bool cuda_cores_only = getenv("LLAMINI_GEMV_CUDA_CORES") != nullptr;
+    uint64_t stage;
+    size_t smem;
+    return !cuda_cores_only && mma_plan(a, &stage, &smem);
+}
+
+// Launch when mma_plan takes `in`; *handled = false otherwise, and the caller
+// uses k_gemv.cu (which has no fused tensor-parallel reduction).
+bool launch_gemv_mma(const GemvArgs& in, cudaStream_t st, bool* handled) {
+    *handled = false;
+    uint64_t stage = 0;
+    size_t smem = 0;
+    if (!mma_plan(in, &stage, &smem)) return true;
     GemvArgs a = in;
     uint32_t tiles = 0;
     for (uint32_t i = 0; i < a.nseg; i++) {

@@ -48,6 +48,14 @@ __host__ __device__ __forceinline__ float* tp_wide(float* buf) { return buf + 2 
 __device__ __forceinline__ uint32_t* tp_wflags(float* buf) {
     return reinterpret_cast<uint32_t*>(tp_wide(buf) + 2 * kTpWideFloats);
 }
+// fused slots [2][kTpMaxRanks][kTpFusedFloats] after the wide flags, then the
+// arrival counters [2][kTpMaxRanks]
+__host__ __device__ __forceinline__ float* tp_fslots(float* buf) {
+    return tp_wide(buf) + 2 * kTpWideFloats + kTpMaxRanks * kTpWideCtas;
+}
+__host__ __device__ __forceinline__ uint32_t* tp_farrive(float* buf) {
+    return reinterpret_cast<uint32_t*>(tp_fslots(buf) + 2 * kTpMaxRanks * kTpFusedFloats);
+}
 __device__ __forceinline__ uint64_t tp_time() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
@@ -160,7 +168,27 @@ TpState& tp() { return g_tp; }
 
 size_t tp_buffer_bytes() {
     return (2 * kTpSlotFloats + kTpMaxRanks + 2 * kTpWideFloats) * sizeof(float) +
-           (size_t)kTpMaxRanks * kTpWideCtas * sizeof(uint32_t);
+           (size_t)kTpMaxRanks * kTpWideCtas * sizeof(uint32_t) +
+           (size_t)2 * kTpMaxRanks * kTpFusedFloats * sizeof(float) + 2 * kTpMaxRanks * sizeof(uint32_t);
+}
+
+// device counters after the buffer's: gen (1), wide gen (kTpWideCtas), fused
+// gen (2), fused tickets (2)
+constexpr uint32_t kTpCounterWords = 1 + kTpWideCtas + 4;
+
+GemvTp tp_fused_args(uint32_t push, uint32_t pull) {
+    GemvTp t;
+    for (uint32_t j = 0; j < g_tp.world && j < kTpMaxRanks; j++) {
+        t.slots[j] = tp_fslots(g_tp.peer[j]);
+        t.arrive[j] = tp_farrive(g_tp.peer[j]);
+    }
+    t.gen = g_tp.gen + 1 + kTpWideCtas;
+    t.ticket = t.gen + 2;
+    t.rank = g_tp.rank;
+    t.world = g_tp.world;
+    t.push = push;
+    t.pull = pull;
+    return t;
 }
 
 bool tp_alloc_buffer() {
@@ -170,7 +198,7 @@ bool tp_alloc_buffer() {
     if (!LM_CUDA(cudaMalloc(&p, tp_buffer_bytes()))) return false;
     if (!LM_CUDA(cudaMemset(p, 0, tp_buffer_bytes()))) { cudaFree(p); return false; }
     uint32_t* gen = nullptr;
-    if (!LM_CUDA(cudaMalloc((void**)&gen, 4 * (1 + kTpWideCtas))) || !LM_CUDA(cudaMemset(gen, 0, 4 * (1 + kTpWideCtas)))) {
+    if (!LM_CUDA(cudaMalloc((void**)&gen, 4 * kTpCounterWords)) || !LM_CUDA(cudaMemset(gen, 0, 4 * kTpCounterWords))) {
         cudaFree(p);
         return false;
     }

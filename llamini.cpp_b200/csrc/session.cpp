@@ -72,6 +72,8 @@ struct llamini_session {
     float *part = nullptr, *trace = nullptr;
     float* tp_part = nullptr;           // tensor parallel: this rank's o / down partial sums
     u32 tp_world = 1;                   // ranks the weights are split over
+    int tp_fuse = 0;                    // 0 not decided, 1 reductions fused into the GEMVs, -1 separate
+    bool tp_fuse_now = false;           // the step being enqueued uses the fused reductions
     struct Prefill* pf = nullptr;       // prompt chunks on the tensor-core GEMM (built on first use)
     int pf_state = 0;                   // 0 not tried, 1 built, -1 not available for this model
     u32 *counters = nullptr, *tokens = nullptr;
@@ -282,6 +284,7 @@ GemvArgs qkv_args(llamini_session* s, u32 l) {
         a.seg[1] = {W.k.ptr, nullptr, W.k.row_bytes, 0, W.k.type, 0, W.k.rows, EPI_STORE, s->qkv + s->qd, W.bk, 0, 0};
         a.seg[2] = {W.v.ptr, nullptr, W.v.row_bytes, 0, W.v.type, 0, W.v.rows, EPI_STORE, s->qkv + s->qd + s->kvd, W.bv, 0, 0};
     }
+    if (s->tp_fuse_now && l > 0) a.tp = tp_fused_args(kTpNone, 1);   // the previous layer's down sums
     return a;
 }
 
@@ -319,6 +322,7 @@ GemvArgs o_args(llamini_session* s, u32 l) {
         o.seg[0].epi = EPI_STORE;
         o.seg[0].out = s->tp_part;
         if (tp().rank != 0) o.seg[0].bias = nullptr;  // the bias enters the sum once
+        if (s->tp_fuse_now) o.tp = tp_fused_args(0, kTpNone);
     }
     return o;
 }
@@ -341,6 +345,7 @@ GemvArgs ffn_args(llamini_session* s, u32 l) {
     else
         f.seg[0] = {W.gate.ptr, W.up.ptr, W.gate.row_bytes, W.up.row_bytes, W.gate.type, W.up.type, W.gate.rows,
                     s->act_gelu ? (u32)EPI_GLU_GELU : (u32)EPI_GLU_SILU, s->ffn_h, nullptr, 0, 0};
+    if (s->tp_fuse_now) f.tp = tp_fused_args(kTpNone, 0);                // the o sums
     return f;
 }
 
@@ -357,6 +362,7 @@ GemvArgs down_args(llamini_session* s, u32 l) {
         d.seg[0].epi = EPI_STORE;
         d.seg[0].out = s->tp_part;
         if (tp().rank != 0) d.seg[0].bias = nullptr;
+        if (s->tp_fuse_now) d.tp = tp_fused_args(1, kTpNone);
     }
     return d;
 }
@@ -375,22 +381,46 @@ GemvArgs head_args(llamini_session* s) {
     h.nseg = 1;
     h.seg[0] = {s->head.ptr, nullptr, s->head.row_bytes, 0, s->head.type, 0, s->head.rows, EPI_STORE, s->logits, nullptr, 0, 1};
     h.argmax_key = &s->st->argmax_key;
+    if (s->tp_fuse_now) h.tp = tp_fused_args(kTpNone, 1);               // the last layer's down sums
     return h;
 }
 
+// Whether a tensor-parallel session's steps fuse the o / down reductions into
+// the GEMVs: every GEMV of the step on the tensor-core kernel (the CUDA-core
+// one has no fused path) and LLAMINI_TP_FUSED not 0; decided once.
+bool tp_fused(llamini_session* s) {
+    if (s->tp_world < 2) return false;
+    if (s->tp_fuse) return s->tp_fuse > 0;
+    s->tp_fuse = -1;
+    const char* e = getenv("LLAMINI_TP_FUSED");
+    if ((e && e[0] == '0') || s->dim > kTpFusedFloats) return false;
+    s->tp_fuse_now = true;
+    bool ok = gemv_mma_takes(head_args(s));
+    for (u32 l = 0; ok && l < s->n_layers; l++)
+        ok = gemv_mma_takes(qkv_args(s, l)) && gemv_mma_takes(o_args(s, l)) && gemv_mma_takes(ffn_args(s, l)) &&
+             gemv_mma_takes(down_args(s, l));
+    s->tp_fuse_now = false;
+    s->tp_fuse = ok ? 1 : -1;
+    return ok;
+}
+
 bool enqueue_step(llamini_session* s, cudaStream_t st, bool trace, bool nll) {
-    if (!launch_embed(embed_args(s), st)) return false;
-    for (u32 l = 0; l < s->n_layers; l++) {
-        if (!launch_gemv(qkv_args(s, l), st)) return false;
-        if (!launch_attention(attn_args(s, l), st)) return false;
-        if (!launch_gemv(o_args(s, l), st)) return false;
-        if (s->tp_world > 1 && !launch_tp_allreduce(s->tp_part, s->hidden, s->dim, &s->st->err, st)) return false;
-        if (!launch_gemv(ffn_args(s, l), st)) return false;
-        if (!launch_gemv(down_args(s, l), st)) return false;
-        if (s->tp_world > 1 && !launch_tp_allreduce(s->tp_part, s->hidden, s->dim, &s->st->err, st)) return false;
-        if (trace && !launch_copy_f32(s->trace + (size_t)l * s->dim, s->hidden, s->dim, st)) return false;
+    // tensor parallel: the reductions fused into the GEMVs, except when the
+    // residual stream is traced after every layer (it is complete only after
+    // the next GEMV's pull there)
+    s->tp_fuse_now = !trace && tp_fused(s);
+    const bool sep = s->tp_world > 1 && !s->tp_fuse_now;
+    bool ok = launch_embed(embed_args(s), st);
+    for (u32 l = 0; ok && l < s->n_layers; l++) {
+        ok = launch_gemv(qkv_args(s, l), st) && launch_attention(attn_args(s, l), st) && launch_gemv(o_args(s, l), st) &&
+             (!sep || launch_tp_allreduce(s->tp_part, s->hidden, s->dim, &s->st->err, st)) &&
+             launch_gemv(ffn_args(s, l), st) && launch_gemv(down_args(s, l), st) &&
+             (!sep || launch_tp_allreduce(s->tp_part, s->hidden, s->dim, &s->st->err, st)) &&
+             (!trace || launch_copy_f32(s->trace + (size_t)l * s->dim, s->hidden, s->dim, st));
     }
-    if (!launch_gemv(head_args(s), st)) return false;
+    ok = ok && launch_gemv(head_args(s), st);
+    s->tp_fuse_now = false;
+    if (!ok) return false;
     FinishArgs fa;
     fa.st = s->st;
     fa.tokens = s->tokens;
@@ -2477,7 +2507,7 @@ int llamini_tp_leave(void) {
     T.world = 1;
     // flags and counters from zero for the next group
     return LM_CUDA(cudaMemset(T.local, 0, lm::tp_buffer_bytes())) &&
-                   LM_CUDA(cudaMemset(T.gen, 0, 4 * (1 + lm::kTpWideCtas))) && LM_CUDA(cudaDeviceSynchronize())
+                   LM_CUDA(cudaMemset(T.gen, 0, 4 * (1 + lm::kTpWideCtas + 4))) && LM_CUDA(cudaDeviceSynchronize())
                ? 0 : -1;
 }
 

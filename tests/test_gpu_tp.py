@@ -199,3 +199,72 @@ def test_tp_two_ranks_prefill_and_batch(orc, tiny):
         assert bt == want_b, (rank, bt, want_b)
         assert rel_l2(lg, want_lg) < TOL, (rank, rel_l2(lg, want_lg))
     assert np.array_equal(res[0][3].view(np.uint32), res[1][3].view(np.uint32))
+
+
+def _rank_fused(rank, world, port, path, prompt, n_gen, q):
+    """One rank: the same stream and logits with the o / down reductions fused
+    into the GEMVs (default) and as separate allreduce kernels
+    (LLAMINI_TP_FUSED=0)."""
+    import datetime
+    import importlib.util
+    import torch.distributed as dist
+    import torch
+    spec = importlib.util.spec_from_file_location("llamini_b200", os.path.join(ROOT, "llamini.cpp_b200", "__init__.py"))
+    lm = importlib.util.module_from_spec(spec)
+    sys.modules["llamini_b200"] = lm
+    spec.loader.exec_module(lm)
+    L = lm.lib()
+    try:
+        assert L.llamini_set_device(rank) == 0, lm.last_error()
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:%d" % port, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120))
+        h = np.zeros(64, np.uint8)
+        assert L.llamini_tp_handle(lm.ptr(h)) == 0, lm.last_error()
+        mine = torch.from_numpy(h)
+        hs = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(hs, mine)
+        allh = np.ascontiguousarray(np.concatenate([x.numpy() for x in hs]))
+        assert L.llamini_tp_join(rank, world, lm.ptr(allh)) == 0, lm.last_error()
+        res = []
+        for mode in ("1", "0"):
+            os.environ["LLAMINI_TP_FUSED"] = mode
+            m = lm.Model(path)
+            toks = m.generate(np.array(prompt, np.uint32), n_gen).tolist()
+            lgs = np.stack([m.forward(p, int(toks[p])) for p in range(len(prompt) + 4)])
+            m.close()
+            res.append((toks, lgs))
+            dist.barrier()
+        q.put((rank, res, ""))
+        dist.destroy_process_group()
+    except Exception as e:                            # report, then leave: the parent fails the test
+        q.put((rank, None, repr(e)))
+
+
+def test_tp_fused_reduction_equals_separate(orc, tiny):
+    """The reductions fused into the GEMVs (the o / ffn_down GEMV stores its
+    partial rows into every rank's memory; the next GEMV waits for them and adds
+    them in rank order) give bit-identical logits and the same stream as the
+    separate allreduce kernels, and the oracle's stream."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("tensor parallelism needs two GPUs")
+    path = tiny.ensure("tiny_tp")
+    prompt = np.random.default_rng(44).integers(3, 1000, 9).tolist()
+    n_gen = 20
+    want, _ = _oracle_stream(orc.oracle_model(path), prompt, len(prompt) + n_gen)
+    ctx = mp.get_context("spawn")
+    qq = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_rank_fused, args=(r, 2, port, path, prompt, n_gen, qq)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted((qq.get(timeout=600) for _ in ps), key=lambda r: r[0])
+    for p in ps:
+        p.join(timeout=120)
+    for rank, modes, err in res:
+        assert modes is not None, (rank, err)
+        (tf, lf), (ts, ls) = modes
+        assert tf == want and ts == want, (rank, tf, ts, want)
+        assert np.array_equal(lf.view(np.uint32), ls.view(np.uint32)), rank
+    assert np.array_equal(res[0][1][0][1].view(np.uint32), res[1][1][0][1].view(np.uint32))
