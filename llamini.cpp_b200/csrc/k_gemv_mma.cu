@@ -64,11 +64,6 @@ __device__ __forceinline__ uint32_t ld_acq_sys(const uint32_t* p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ float ld_rlx_sys(const float* p) {
-    float v;
-    asm volatile("ld.relaxed.sys.global.f32 %0, [%1];\n" : "=f"(v) : "l"(p) : "memory");
-    return v;
-}
 
 // Before staging: wait for every rank's rows of slot `pull`, then xf = x +
 // (sum over ranks in rank order) -- the separate allreduce's arithmetic. The
@@ -97,11 +92,19 @@ __device__ bool tp_pull(const GemvArgs& a, float* xf) {
     }
     __syncthreads();
     if (!s_st) return false;
+    // the ranks' rows are in this GPU's memory (peers stored them over NVLink):
+    // after the acquire, L2 loads (not L1, which may hold an earlier use's rows),
+    // all of a thread's loads in flight at once
     const float* mine = t.slots[t.rank] + (uint64_t)P * 8u * kTpFusedFloats;
     for (uint32_t i = tid; i < K; i += kMThreads) {
+        float v[8];
+#pragma unroll
+        for (uint32_t r = 0; r < 8; r++) v[r] = r < t.world ? __ldcg(mine + (uint64_t)r * kTpFusedFloats + i) : 0.f;
         float s = 0.f;
-        for (uint32_t r = 0; r < t.world; r++) s += ld_rlx_sys(mine + (uint64_t)r * kTpFusedFloats + i);
-        xf[i] = a.x[i] + s;
+#pragma unroll
+        for (uint32_t r = 0; r < 8; r++)
+            if (r < t.world) s += v[r];
+        xf[i] = __ldcg(a.x + i) + s;
     }
     __syncthreads();
     if (tid == 0) {

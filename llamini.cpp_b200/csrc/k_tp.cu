@@ -148,10 +148,16 @@ __global__ void __launch_bounds__(256) tp_allreduce_wide_kernel(const TpArgs a) 
     }
     __syncthreads();
     if (s_fail) return;
+    // L2 loads (peer slots over NVLink), every rank's value in flight at once
     for (uint32_t i = i0 + tid; i < i1; i += blockDim.x) {
+        float v[kTpMaxRanks];
+#pragma unroll
+        for (uint32_t j = 0; j < kTpMaxRanks; j++)
+            v[j] = j < a.world ? __ldcg(tp_wide(a.buf[j]) + par * kTpWideFloats + i) : 0.f;
         float s = 0.f;
-        for (uint32_t j = 0; j < a.world; j++)
-            s += j == a.rank ? mine[i] : ld_relaxed_sys(tp_wide(a.buf[j]) + par * kTpWideFloats + i);
+#pragma unroll
+        for (uint32_t j = 0; j < kTpMaxRanks; j++)
+            if (j < a.world) s += v[j];
         a.out[i] += s;
     }
     __syncthreads();
