@@ -151,6 +151,54 @@ bool weight(llamini_session* s, const Tensor* t, u32 rows, u32 cols, DevMat* out
     return true;
 }
 
+void shard_rows(llamini_session* s, DevMat* m, u32 r0, u32 n);
+bool shard_cols(llamini_session* s, DevMat* m, u32 c0, u32 c1);
+
+// Tensor parallelism: rows [r0, r0 + nr) and columns [c0, c1) (on block
+// boundaries) of a rows x cols weight, copied from the mapped GGUF file
+// straight into a matrix of the session's own, so a rank uploads only its
+// shard (gguf.c's mapping, model.c's tensor table). Eager f32 tensors take the
+// whole-matrix path and are cut on the device.
+bool weight_shard(llamini_session* s, const Tensor* t, u32 rows, u32 cols, u32 r0, u32 nr, u32 c0, u32 c1,
+                  DevMat* out) {
+    if (!t) { set_error("missing weight tensor"); return false; }
+    if ((u64)t->size != (u64)rows * cols) { set_error("weight shape mismatch: %u elements, expected %ux%u", t->size, rows, cols); return false; }
+    GGUFFile* gf = nullptr;
+    const GGUFTensorInfo* info = nullptr;
+    if (!t->data) { gf = t->src_gf; info = t->src_info; }
+    else source_of(t, &gf, &info);
+    if (!info) {
+        if (!weight(s, t, rows, cols, out)) return false;
+        if (nr != rows) shard_rows(s, out, r0, nr);
+        return (c0 == 0 && c1 == cols) || shard_cols(s, out, c0, c1);
+    }
+    const uint32_t ty = info->ggml_type;
+    const uint64_t rb = type_bytes(ty, cols), b0 = type_bytes(ty, c0), w = type_bytes(ty, c1 - c0);
+    if (rb == 0 || w == 0 || (c0 && b0 == 0) || r0 + nr > rows || c1 > cols) {
+        set_error("tensor parallel: rows %u+%u, columns %u..%u of tensor %s are not on block boundaries", r0, nr, c0, c1,
+                  info->name);
+        return false;
+    }
+    const uint64_t abs_off = gf->tensor_offset + info->offset;
+    if (abs_off < info->offset || abs_off > gf->size || rb * rows > gf->size - abs_off) {
+        set_error("tensor %s runs past the end of the file", info->name);
+        return false;
+    }
+    uint8_t* d = (uint8_t*)own(s, w * nr + 16);       // 16 bytes of slack for word reads
+    const uint8_t* src = (const uint8_t*)gf->data + abs_off + (uint64_t)r0 * rb + b0;
+    if (!d || !LM_CUDA(cudaMemcpy2D(d, w, src, rb, w, nr, cudaMemcpyHostToDevice)) ||
+        !LM_CUDA(cudaMemset(d + w * nr, 0, 16)))
+        return false;
+    out->ptr = d;
+    out->type = ty;
+    out->rows = nr;
+    out->cols = c1 - c0;
+    out->row_bytes = w;
+    s->gf = gf;
+    s->weight_bytes += w * nr;
+    return true;
+}
+
 const float* vec(llamini_session* s, const Tensor* t, u32 n) {
     if (!t || !t->data || t->size < n) { set_error("missing or short f32 tensor"); return nullptr; }
     s->weight_bytes += (u64)n * 4;
@@ -851,17 +899,20 @@ bool bind_llama(llamini_session* s, LLaMAModel* m, u32 max_seq) {
         const DecoderLayer& L = m->layers[l];
         auto& W = s->layers[l];
         const u32 QD = c.n_heads * c.head_dim, KVD = c.n_heads_kv * c.head_dim;   // whole-model widths
-        ok = weight(s, L.q_proj, QD, c.dim, &W.q) && weight(s, L.k_proj, KVD, c.dim, &W.k) &&
-             weight(s, L.v_proj, KVD, c.dim, &W.v) && weight(s, L.o_proj, c.dim, QD, &W.o) &&
-             weight(s, L.gate_proj, c.ffn_dim, c.dim, &W.gate) && weight(s, L.up_proj, c.ffn_dim, c.dim, &W.up) &&
-             weight(s, L.down_proj, c.dim, c.ffn_dim, &W.down);
-        if (ok && s->tp_world > 1) {
-            shard_rows(s, &W.q, R * s->qd, s->qd);
-            shard_rows(s, &W.k, R * s->kvd, s->kvd);
-            shard_rows(s, &W.v, R * s->kvd, s->kvd);
-            shard_rows(s, &W.gate, f0, f1 - f0);
-            shard_rows(s, &W.up, f0, f1 - f0);
-            ok = shard_cols(s, &W.o, R * s->qd, (R + 1) * s->qd) && shard_cols(s, &W.down, f0, f1);
+        if (s->tp_world > 1) {
+            // this rank's shard only, straight from the mapped file
+            ok = weight_shard(s, L.q_proj, QD, c.dim, R * s->qd, s->qd, 0, c.dim, &W.q) &&
+                 weight_shard(s, L.k_proj, KVD, c.dim, R * s->kvd, s->kvd, 0, c.dim, &W.k) &&
+                 weight_shard(s, L.v_proj, KVD, c.dim, R * s->kvd, s->kvd, 0, c.dim, &W.v) &&
+                 weight_shard(s, L.o_proj, c.dim, QD, 0, c.dim, R * s->qd, (R + 1) * s->qd, &W.o) &&
+                 weight_shard(s, L.gate_proj, c.ffn_dim, c.dim, f0, f1 - f0, 0, c.dim, &W.gate) &&
+                 weight_shard(s, L.up_proj, c.ffn_dim, c.dim, f0, f1 - f0, 0, c.dim, &W.up) &&
+                 weight_shard(s, L.down_proj, c.dim, c.ffn_dim, 0, c.dim, f0, f1, &W.down);
+        } else {
+            ok = weight(s, L.q_proj, QD, c.dim, &W.q) && weight(s, L.k_proj, KVD, c.dim, &W.k) &&
+                 weight(s, L.v_proj, KVD, c.dim, &W.v) && weight(s, L.o_proj, c.dim, QD, &W.o) &&
+                 weight(s, L.gate_proj, c.ffn_dim, c.dim, &W.gate) && weight(s, L.up_proj, c.ffn_dim, c.dim, &W.up) &&
+                 weight(s, L.down_proj, c.dim, c.ffn_dim, &W.down);
         }
         if (ok) { W.n1w = vec(s, L.attn_norm, c.dim); W.n2w = vec(s, L.ffn_norm, c.dim); ok = W.n1w && W.n2w; }
         if (ok && c.qkv_bias) {
