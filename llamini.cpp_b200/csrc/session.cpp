@@ -1077,7 +1077,8 @@ bool check_device_errors(llamini_session* s) {
     uint32_t e = 0;
     if (!LM_CUDA(cudaMemcpy(&e, &s->st->err, 4, cudaMemcpyDeviceToHost))) return false;
     if (e) {
-        set_error("a kernel reported error bits 0x%x (a bounded wait on a weight copy ran out)", e);
+        set_error("a kernel reported error bits 0x%x (a bounded wait ran out: a weight copy, or a tensor-parallel "
+                  "peer that did not arrive; the bits stay set, so the session refuses later steps)", e);
         return false;
     }
     return true;
