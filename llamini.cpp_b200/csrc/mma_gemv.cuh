@@ -1,7 +1,7 @@
 // mma_gemv.cuh -- building blocks of the tensor-core dequant-GEMV, shared by
 // the per-matrix kernel (k_gemv_mma.cu) and the persistent decode-step kernel
 // (k_decode.cu): mbarrier/bulk-copy helpers, the m16n8k16 fragment layout with
-// "slot" columns, and the per-format tile compute for Q4_K, Q6_K, Q8_0, Q4_0.
+// "slot" columns, and the per-format tile compute for Q4_K, Q6_K, Q8_0, Q4_0, Q4_1, Q5_0.
 //
 // Every block format is affine per group of 16 or 32 weights,
 //     w = alpha * q - beta      (q a small unsigned integer, gguf.c:427-590),
@@ -269,6 +269,80 @@ struct FQ40 {
             const uint32_t q = (e_blk + 32 * L.tig) >> 4;
             scale_add(acc, cl, dg, 8.0f * dg, dg8, 8.0f * dg8, sm.sx[q]);
             scale_add(acc, ch, dg * 0.0625f, 8.0f * dg, dg8 * 0.0625f, 8.0f * dg8, sm.sx[q + 1]);
+        }
+    }
+};
+
+// Q4_1 (gguf.c:445-462): w = d q + m; nibbles as Q4_0, qs after d and m.
+struct FQ41 {
+    static constexpr uint32_t SB = 128, SBB = 80, BB = 20;
+    static __device__ __forceinline__ void compute(const uint8_t* bg, const uint8_t* bg8, uint32_t e_blk,
+                                                   uint32_t nvalid, const Lane& L, const MmaSmem& sm, float* acc) {
+        const uint32_t es = e_blk + 32 * L.slot + 4 * L.tig;
+        const BFrag fl = L.slot < nvalid ? bfrag(L, es) : BFrag{0u, 0u};
+        const BFrag fh = L.slot < nvalid ? bfrag(L, es + 16) : BFrag{0u, 0u};
+        float cl[4] = {0.f, 0.f, 0.f, 0.f}, ch[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            if ((uint32_t)k >= nvalid) break;
+            const uint32_t w = lds_u32(bg + k * BB + 4 + 4 * L.tig), v = lds_u32(bg8 + k * BB + 4 + 4 * L.tig);
+            const uint32_t ws = w >> 8, vs = v >> 8;
+            const BFrag bl = bmask(fl, L.slot, k), bh = bmask(fh, L.slot, k);
+            mma16816(cl, w & 0x000F000Fu, v & 0x000F000Fu, ws & 0x000F000Fu, vs & 0x000F000Fu, bl.b0, bl.b1);
+            mma16816(ch, w & 0x00F000F0u, v & 0x00F000F0u, ws & 0x00F000F0u, vs & 0x00F000F0u, bh.b0, bh.b1);
+        }
+        if (L.tig < nvalid) {
+            const uint32_t h = lds_u32(bg + L.tig * BB), h8 = lds_u32(bg8 + L.tig * BB);
+            const float dg = h2f(h & 0xFFFFu), mg = h2f(h >> 16), dg8 = h2f(h8 & 0xFFFFu), mg8 = h2f(h8 >> 16);
+            const uint32_t q = (e_blk + 32 * L.tig) >> 4;
+            scale_add(acc, cl, dg, -mg, dg8, -mg8, sm.sx[q]);
+            scale_add(acc, ch, dg * 0.0625f, -mg, dg8 * 0.0625f, -mg8, sm.sx[q + 1]);
+        }
+    }
+};
+
+// Q5_0 (gguf.c:463-488): w = (q - 16) d, q = nibble | (bit e of qh) << 4; low
+// nibbles are elements 0..15, high nibbles 16..31. The fifth bit is merged
+// into each fp16 half: bit 4 under a low nibble, bit 8 under a high nibble kept
+// in place (16 q).
+struct FQ50 {
+    static constexpr uint32_t SB = 128, SBB = 88, BB = 22;
+    static __device__ __forceinline__ uint32_t lo_even(uint32_t w, uint32_t h) {   // elements e, e + 2
+        return (w & 0x000F000Fu) | ((h << 4) & 0x10u) | ((h << 18) & 0x100000u);
+    }
+    static __device__ __forceinline__ uint32_t lo_odd(uint32_t ws, uint32_t h) {   // elements e + 1, e + 3
+        return (ws & 0x000F000Fu) | ((h << 3) & 0x10u) | ((h << 17) & 0x100000u);
+    }
+    static __device__ __forceinline__ uint32_t hi_even(uint32_t w, uint32_t h) {
+        return (w & 0x00F000F0u) | ((h << 8) & 0x100u) | ((h << 22) & 0x1000000u);
+    }
+    static __device__ __forceinline__ uint32_t hi_odd(uint32_t ws, uint32_t h) {
+        return (ws & 0x00F000F0u) | ((h << 7) & 0x100u) | ((h << 21) & 0x1000000u);
+    }
+    static __device__ __forceinline__ void compute(const uint8_t* bg, const uint8_t* bg8, uint32_t e_blk,
+                                                   uint32_t nvalid, const Lane& L, const MmaSmem& sm, float* acc) {
+        const uint32_t es = e_blk + 32 * L.slot + 4 * L.tig;
+        const BFrag fl = L.slot < nvalid ? bfrag(L, es) : BFrag{0u, 0u};
+        const BFrag fh = L.slot < nvalid ? bfrag(L, es + 16) : BFrag{0u, 0u};
+        float cl[4] = {0.f, 0.f, 0.f, 0.f}, ch[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            if ((uint32_t)k >= nvalid) break;
+            const uint8_t* p = bg + k * BB;
+            const uint8_t* r = bg8 + k * BB;
+            const uint32_t w = lds_u32(p + 6 + 4 * L.tig), v = lds_u32(r + 6 + 4 * L.tig);
+            // high bits of this lane's elements: bits 0..3 = 4 tig .. 4 tig + 3, bits 16..19 = 16 + those
+            const uint32_t hw = lds_u32(p + 2) >> (4 * L.tig), hv = lds_u32(r + 2) >> (4 * L.tig);
+            const uint32_t ws = w >> 8, vs = v >> 8, hw2 = hw >> 16, hv2 = hv >> 16;
+            const BFrag bl = bmask(fl, L.slot, k), bh = bmask(fh, L.slot, k);
+            mma16816(cl, lo_even(w, hw), lo_even(v, hv), lo_odd(ws, hw), lo_odd(vs, hv), bl.b0, bl.b1);
+            mma16816(ch, hi_even(w, hw2), hi_even(v, hv2), hi_odd(ws, hw2), hi_odd(vs, hv2), bh.b0, bh.b1);
+        }
+        if (L.tig < nvalid) {
+            const float dg = h2f(lds_u16(bg + L.tig * BB)), dg8 = h2f(lds_u16(bg8 + L.tig * BB));
+            const uint32_t q = (e_blk + 32 * L.tig) >> 4;
+            scale_add(acc, cl, dg, 16.0f * dg, dg8, 16.0f * dg8, sm.sx[q]);
+            scale_add(acc, ch, dg * 0.0625f, 16.0f * dg, dg8 * 0.0625f, 16.0f * dg8, sm.sx[q + 1]);
         }
     }
 };
