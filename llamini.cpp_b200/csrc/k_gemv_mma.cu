@@ -36,7 +36,7 @@ constexpr int kMThreads = kMWarps * 32;
 constexpr uint32_t kStages = 2;              // weight tiles in flight per CTA
 
 bool mma_type(uint32_t t) {
-    return t == T_Q4_K || t == T_Q6_K || t == T_Q8_0 || t == T_Q4_0 || t == T_Q4_1 || t == T_Q5_0;
+    return t == T_Q4_K || t == T_Q6_K || t == T_Q8_0 || t == T_Q4_0 || t == T_Q4_1 || t == T_Q5_0 || t == T_Q5_K;
 }
 
 // Block-wide (sum of s, max of m) in one round.
@@ -327,6 +327,7 @@ gemv_mma_kernel(const __grid_constant__ GemvArgs a, uint32_t stage_bytes, const 
         case T_Q6_K: tile_rows<FQ6K>(base, rb, K, L, first, step, sm, acc); break;
         case T_Q8_0: tile_rows<FQ80>(base, rb, K, L, first, step, sm, acc); break;
         case T_Q4_1: tile_rows<FQ41>(base, rb, K, L, first, step, sm, acc); break;
+        case T_Q5_K: tile_rows<FQ5K>(base, rb, K, L, first, step, sm, acc); break;
         case T_Q5_0: tile_rows<FQ50>(base, rb, K, L, first, step, sm, acc); break;
         default:     tile_rows<FQ40>(base, rb, K, L, first, step, sm, acc); break;
         }

@@ -168,6 +168,57 @@ struct FQ4K {
     }
 };
 
+// Q5_K (gguf.c:530-560): Q4_K's layout (d, dmin, 12 scale bytes) with qh[32]
+// before qs[128]: bit 2j of qh[l] is the fifth bit of element 64j + l, bit
+// 2j + 1 that of 64j + 32 + l. The bits are merged into the fp16 halves (bit 4
+// under a low nibble, bit 8 under a high nibble kept in place as 16 q).
+struct FQ5K {
+    static constexpr uint32_t SB = 256, SBB = 176;
+    static __device__ __forceinline__ void compute(const uint8_t* bg, const uint8_t* bg8, uint32_t e_blk, uint32_t,
+                                                   const Lane& L, const MmaSmem& sm, float* acc) {
+        const uint4 h = *reinterpret_cast<const uint4*>(bg), h8 = *reinterpret_cast<const uint4*>(bg8);
+        const uint2 hq = *reinterpret_cast<const uint2*>(bg + 16 + 8 * L.tig);
+        const uint2 hq8 = *reinterpret_cast<const uint2*>(bg8 + 16 + 8 * L.tig);
+        const uint32_t eb = e_blk + 64 * L.slot + 8 * L.tig;
+        const BFrag f00 = bfrag(L, eb), f01 = bfrag(L, eb + 4), f10 = bfrag(L, eb + 32), f11 = bfrag(L, eb + 36);
+        float cl[4] = {0.f, 0.f, 0.f, 0.f}, ch[4] = {0.f, 0.f, 0.f, 0.f};
+        constexpr uint32_t L4 = 0x000F000Fu, H4 = 0x00F000F0u, B1 = 0x01010101u;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const uint2 q = *reinterpret_cast<const uint2*>(bg + 48 + 32 * j + 8 * L.tig);
+            const uint2 q8 = *reinterpret_cast<const uint2*>(bg8 + 48 + 32 * j + 8 * L.tig);
+            const uint32_t w0 = q.x, w1 = q.y, v0 = q8.x, v1 = q8.y;
+            const uint32_t w0s = w0 >> 8, w1s = w1 >> 8, v0s = v0 >> 8, v1s = v1 >> 8;
+            // fifth bits of bytes 0..3 of each word at bits 0, 8, 16, 24
+            const uint32_t lw0 = (hq.x >> (2 * j)) & B1, lw1 = (hq.y >> (2 * j)) & B1;
+            const uint32_t lv0 = (hq8.x >> (2 * j)) & B1, lv1 = (hq8.y >> (2 * j)) & B1;
+            const uint32_t uw0 = (hq.x >> (2 * j + 1)) & B1, uw1 = (hq.y >> (2 * j + 1)) & B1;
+            const uint32_t uv0 = (hq8.x >> (2 * j + 1)) & B1, uv1 = (hq8.y >> (2 * j + 1)) & B1;
+            const BFrag b00 = bmask(f00, L.slot, j), b01 = bmask(f01, L.slot, j);
+            const BFrag b10 = bmask(f10, L.slot, j), b11 = bmask(f11, L.slot, j);
+            // low nibbles: bytes 0, 2 (bits 0, 16 -> 4, 20), bytes 1, 3 (bits 8, 24 -> 4, 20)
+            mma16816(cl, (w0 & L4) | ((lw0 << 4) & 0x00100010u), (v0 & L4) | ((lv0 << 4) & 0x00100010u),
+                     (w0s & L4) | ((lw0 >> 4) & 0x00100010u), (v0s & L4) | ((lv0 >> 4) & 0x00100010u), b00.b0, b00.b1);
+            mma16816(cl, (w1 & L4) | ((lw1 << 4) & 0x00100010u), (v1 & L4) | ((lv1 << 4) & 0x00100010u),
+                     (w1s & L4) | ((lw1 >> 4) & 0x00100010u), (v1s & L4) | ((lv1 >> 4) & 0x00100010u), b01.b0, b01.b1);
+            // high nibbles in place (16 q): bytes 0, 2 (bits 0, 16 -> 8, 24), bytes 1, 3 (bits 8, 24 stay)
+            mma16816(ch, (w0 & H4) | ((uw0 << 8) & 0x01000100u), (v0 & H4) | ((uv0 << 8) & 0x01000100u),
+                     (w0s & H4) | (uw0 & 0x01000100u), (v0s & H4) | (uv0 & 0x01000100u), b10.b0, b10.b1);
+            mma16816(ch, (w1 & H4) | ((uw1 << 8) & 0x01000100u), (v1 & H4) | ((uv1 << 8) & 0x01000100u),
+                     (w1s & H4) | (uw1 & 0x01000100u), (v1s & H4) | (uv1 & 0x01000100u), b11.b0, b11.b1);
+        }
+        float sl, ml, sh, mh, tl, nl, th, nh;
+        FQ4K::scales(h.y, h.z, h.w, L.tig, &sl, &ml, &sh, &mh);
+        FQ4K::scales(h8.y, h8.z, h8.w, L.tig, &tl, &nl, &th, &nh);
+        const float dg = h2f(h.x & 0xFFFFu), mg = h2f(h.x >> 16);
+        const float dg8 = h2f(h8.x & 0xFFFFu), mg8 = h2f(h8.x >> 16);
+        const uint32_t q = (e_blk + 64 * L.tig) >> 4;
+        const float sxl = sm.sx[q] + sm.sx[q + 1], sxh = sm.sx[q + 2] + sm.sx[q + 3];
+        scale_add(acc, cl, dg * sl, mg * ml, dg8 * tl, mg8 * nl, sxl);
+        scale_add(acc, ch, dg * sh * 0.0625f, mg * mh, dg8 * th * 0.0625f, mg8 * nh, sxh);
+    }
+};
+
 // Q6_K (gguf.c:561-590): per 128-half H, byte l of ql[64H..], ql[64H+32..] and
 // qh[32H..] give elements 128H + 32c + l (c = 0..3), scale sc[8H + l/16 + 2c].
 // For each (H, u = l/16) the four scale groups c are one MMA each, slot = c.
