@@ -321,7 +321,9 @@ def run_qwen2(args, lm, L, torch, hbm_peak):
         b32 = {"value": round(B * QWEN_STEPS / (bd_ms / 1e3), 1), "unit": "tok/s", "batch": B,
                "ms_per_step": round(bd_ms / QWEN_STEPS, 4),
                "frac_of_hbm": round(bbytes / (bd_ms / 1e3 / QWEN_STEPS) / 1e9 / hbm_peak, 4),
-               "prompt_ms": round(bp_ms, 2), "prompt_path": "batched decode steps, one position at a time"}
+               "prompt_ms": round(bp_ms, 2),
+               "prompt_positions_per_s": round(B * (QWEN_PROMPT - 1) / (bp_ms / 1e3), 1),
+               "prompt_path": "prefill chunks of 2 positions x 32 sequences (tcgen05 GEMM)"}
     finally:
         m.close()
     return {"workload": "qwen2_05b: Qwen2 0.5B shape (24 layers, dim 896, 14/2 heads, ffn 4864, vocab 151936), "
