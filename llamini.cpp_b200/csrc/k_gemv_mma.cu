@@ -76,7 +76,8 @@ __device__ bool tp_pull(const GemvArgs& a, float* xf) {
     const GemvTp& t = a.tp;
     const uint32_t tid = threadIdx.x, K = a.K, P = t.pull;
     if (tid == 0) {
-        uint32_t ok = 1;
+        // a wait of this session that already ran out: the group is broken, fail at once
+        uint32_t ok = (*reinterpret_cast<volatile uint32_t*>(a.err) & kErrWaitTimeout) ? 0u : 1u;
         const uint32_t target = (*reinterpret_cast<volatile uint32_t*>(t.gen + P) + 1u) * ((K + 15u) / 16u);
         const uint32_t* arr = t.arrive[t.rank] + P * 8u;
         const uint64_t t0 = g_time();

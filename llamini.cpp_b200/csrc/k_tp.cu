@@ -95,7 +95,9 @@ __global__ void __launch_bounds__(1024) tp_allreduce_kernel(const TpArgs a) {
         st_release_sys(tp_flags(a.buf[tid]) + a.rank, n);
         const uint32_t* f = tp_flags(a.buf[a.rank]) + tid;
         const uint64_t t0 = tp_time();
-        for (uint32_t i = 0;; i++) {
+        // a wait of this session that already ran out: the group is broken, fail at once
+        if (*reinterpret_cast<volatile uint32_t*>(a.err) & kErrWaitTimeout) s_fail = 1;
+        for (uint32_t i = 0; !s_fail; i++) {
             if ((int32_t)(ld_acquire_sys(f) - n) >= 0) break;
             if ((i & 63u) == 63u && tp_time() - t0 > kTpWaitNs) {
                 atomicOr(a.err, kErrWaitTimeout);
@@ -137,7 +139,8 @@ __global__ void __launch_bounds__(256) tp_allreduce_wide_kernel(const TpArgs a) 
         st_release_sys(tp_wflags(a.buf[tid]) + a.rank * kTpWideCtas + c, n);
         const uint32_t* f = tp_wflags(a.buf[a.rank]) + tid * kTpWideCtas + c;
         const uint64_t t0 = tp_time();
-        for (uint32_t i = 0;; i++) {
+        if (*reinterpret_cast<volatile uint32_t*>(a.err) & kErrWaitTimeout) s_fail = 1;
+        for (uint32_t i = 0; !s_fail; i++) {
             if ((int32_t)(ld_acquire_sys(f) - n) >= 0) break;
             if ((i & 63u) == 63u && tp_time() - t0 > kTpWaitNs) {
                 atomicOr(a.err, kErrWaitTimeout);

@@ -268,3 +268,80 @@ def test_tp_fused_reduction_equals_separate(orc, tiny):
         assert tf == want and ts == want, (rank, tf, ts, want)
         assert np.array_equal(lf.view(np.uint32), ls.view(np.uint32)), rank
     assert np.array_equal(res[0][1][0][1].view(np.uint32), res[1][1][0][1].view(np.uint32))
+
+
+def _rank_dead_peer(rank, world, port, path, q):
+    """Rank 1 joins and builds the session but never steps; rank 0 steps once:
+    its first wait for rank 1's rows runs out (2 s), sets the session's error
+    bit, and every later wait of that step returns at once."""
+    import datetime
+    import importlib.util
+    import time
+    import torch.distributed as dist
+    import torch
+    spec = importlib.util.spec_from_file_location("llamini_b200", os.path.join(ROOT, "llamini.cpp_b200", "__init__.py"))
+    lm = importlib.util.module_from_spec(spec)
+    sys.modules["llamini_b200"] = lm
+    spec.loader.exec_module(lm)
+    L = lm.lib()
+    try:
+        assert L.llamini_set_device(rank) == 0, lm.last_error()
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:%d" % port, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120))
+        h = np.zeros(64, np.uint8)
+        assert L.llamini_tp_handle(lm.ptr(h)) == 0, lm.last_error()
+        mine = torch.from_numpy(h)
+        hs = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(hs, mine)
+        allh = np.ascontiguousarray(np.concatenate([x.numpy() for x in hs]))
+        assert L.llamini_tp_join(rank, world, lm.ptr(allh)) == 0, lm.last_error()
+        m = lm.Model(path)
+        s = m.session()
+        prompt = np.array([5], np.uint32)
+        assert L.llamini_session_begin(s, lm.ptr(prompt), 1) == 0, lm.last_error()
+        dist.barrier()                                # both sessions exist; rank 1 stays idle
+        res = None
+        if rank == 0:
+            out = np.zeros(4, np.uint32)
+            t0 = time.time()
+            assert L.llamini_session_step(s, 1) == 0, lm.last_error()   # enqueued
+            rc = L.llamini_session_tokens(s, lm.ptr(out), 2)               # synchronises, reads the error bits
+            dt = time.time() - t0
+            err = lm.last_error()
+            L.llamini_session_step(s, 1)
+            rc2 = L.llamini_session_tokens(s, lm.ptr(out), 2)              # the bits stay set: refused
+            res = (rc, dt, err, rc2)
+        dist.barrier()                                # rank 1's buffer stays mapped until rank 0 is done
+        m.close()
+        assert L.llamini_tp_leave() == 0, lm.last_error()
+        q.put((rank, res, ""))
+        dist.destroy_process_group()
+    except Exception as e:                            # report, then leave: the parent fails the test
+        q.put((rank, None, repr(e)))
+
+
+def test_tp_peer_that_never_arrives(tiny):
+    """Failure detection without a GPU fault: a rank that never runs its step.
+    The other rank's bounded wait (2 s) ends with the session's error bit, the
+    remaining waits of the step fail at once (the step returns within seconds,
+    not 2 s per reduction), and the session refuses further steps."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("tensor parallelism needs two GPUs")
+    path = tiny.ensure("tiny_tp")
+    ctx = mp.get_context("spawn")
+    qq = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_rank_dead_peer, args=(r, 2, port, path, qq)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted((qq.get(timeout=600) for _ in ps), key=lambda r: r[0])
+    for p in ps:
+        p.join(timeout=120)
+    for rank, r, err in res:
+        assert err == "", (rank, err)
+    rc, dt, msg, rc2 = res[0][1]
+    assert rc == -1 and rc2 == -1, (rc, rc2, msg)
+    assert "tensor-parallel" in msg, msg
+    assert 1.5 < dt < 20.0, dt
