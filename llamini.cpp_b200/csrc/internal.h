@@ -340,6 +340,9 @@ bool flow_encode_maps(FlowOp* ops, uint32_t n_ops, CUtensorMap* d_maps);
 // (rows of an even number of 16-byte units, at most 255 units); false when the
 // driver refuses it.
 bool encode_tile_map(CUtensorMap* m, const uint8_t* w, uint64_t row_bytes, uint32_t rows);
+// The same view with a box of box_units 16-byte units per row (rows of a
+// multiple of 16 bytes); false when the driver refuses it.
+bool encode_box_map(CUtensorMap* m, const uint8_t* w, uint64_t row_bytes, uint32_t rows, uint32_t box_units);
 bool launch_flow(const FlowArgs& a, cudaStream_t st);
 bool launch_flow_embed(const FlowArgs& a, cudaStream_t st);
 

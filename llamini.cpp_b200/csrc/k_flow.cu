@@ -1125,13 +1125,19 @@ static PFN_cuTensorMapEncodeTiled_v12000 flow_encoder() {
 // Rank-3 view of a matrix's rows as uint16: {8 (one 16-byte unit), units per
 // row, rows}, strides {16 bytes, row bytes}; box {8, units + 1, 16}.
 bool encode_tile_map(CUtensorMap* m, const uint8_t* w, uint64_t rb, uint32_t rows) {
+    return encode_box_map(m, w, rb, rows, (uint32_t)(rb / 16 + 1));
+}
+
+// The same view with a box of box_units units (a K-chunk of the rows plus one
+// unit of padding); rows of a multiple of 16 bytes.
+bool encode_box_map(CUtensorMap* m, const uint8_t* w, uint64_t rb, uint32_t rows, uint32_t box_units) {
     PFN_cuTensorMapEncodeTiled_v12000 fn = flow_encoder();
     if (!fn) return false;
     const uint64_t units = rb / 16;
-    if (units + 1 > 256 || reinterpret_cast<uintptr_t>(w) % 16 != 0) return false;
+    if (rb % 16 != 0 || box_units == 0 || box_units > 256 || reinterpret_cast<uintptr_t>(w) % 16 != 0) return false;
     cuuint64_t dims[3] = {8, units, rows};
     cuuint64_t strides[2] = {16, rb};
-    cuuint32_t box[3] = {8, (cuuint32_t)(units + 1), 16};
+    cuuint32_t box[3] = {8, box_units, 16};
     cuuint32_t es[3] = {1, 1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<uint8_t*>(w), dims, strides, box, es,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -35,6 +35,33 @@ constexpr int kMWarps = 8;
 constexpr int kMThreads = kMWarps * 32;
 constexpr uint32_t kStages = 2;              // weight tiles in flight per CTA
 
+// Elements and bytes per iteration of a format's compute (FQ* SB / SBB).
+__host__ __device__ __forceinline__ uint32_t seg_sb(uint32_t t) {
+    return (t == T_Q4_K || t == T_Q5_K || t == T_Q6_K) ? 256u : 128u;
+}
+__host__ __device__ __forceinline__ uint32_t seg_sbb_dev(uint32_t t) {
+    switch (t) {
+    case T_Q4_K: return FQ4K::SBB;
+    case T_Q5_K: return FQ5K::SBB;
+    case T_Q6_K: return FQ6K::SBB;
+    case T_Q8_0: return FQ80::SBB;
+    case T_Q4_1: return FQ41::SBB;
+    case T_Q5_0: return FQ50::SBB;
+    default: return FQ40::SBB;
+    }
+}
+static uint32_t seg_sbb(uint32_t t) {
+    switch (t) {
+    case T_Q4_K: return FQ4K::SBB;
+    case T_Q5_K: return FQ5K::SBB;
+    case T_Q6_K: return FQ6K::SBB;
+    case T_Q8_0: return FQ80::SBB;
+    case T_Q4_1: return FQ41::SBB;
+    case T_Q5_0: return FQ50::SBB;
+    default: return FQ40::SBB;
+    }
+}
+
 bool mma_type(uint32_t t) {
     return t == T_Q4_K || t == T_Q6_K || t == T_Q8_0 || t == T_Q4_0 || t == T_Q4_1 || t == T_Q5_0 || t == T_Q5_K;
 }
@@ -249,10 +276,46 @@ __device__ __forceinline__ void issue_tile(const GemvArgs& a, const GemvMaps& ma
     }
 }
 
+// Thread 0: start the copies of the CTA's work item j (see gemv_mma_kernel).
+// K-chunks of rows of a multiple of 16 bytes: one TMA box (cu = the chunk's
+// units); otherwise (cu = 0) one bulk copy per row of the 16-byte aligned window
+// around the row's chunk, into slots of rsu units.
+__device__ __noinline__ void issue_item(const GemvArgs& a, const GemvMaps& maps, uint32_t j, uint32_t nch,
+                                        uint32_t n_tiles, uint32_t ipc, uint32_t cu, uint32_t rsu, uint8_t* buf,
+                                        uint64_t* bar) {
+    const uint32_t t = blockIdx.x + (j / nch) * gridDim.x;
+    if (t >= n_tiles) return;
+    if (!ipc) {
+        issue_tile(a, maps, t, buf, bar);
+        return;
+    }
+    const TileRef tr = tile_of(a, t);
+    if (cu) {
+        mbar_expect_tx(bar, 256u * (cu + 1u));
+        tma_box(buf, &maps.m[0][0], (int32_t)((j % nch) * cu), (int32_t)tr.row0, bar);
+        return;
+    }
+    const GemvSeg& G = a.seg[0];
+    const uint64_t cb = (uint64_t)ipc * seg_sbb_dev(G.type), c0 = (j % nch) * cb;
+    const uint64_t len = G.row_bytes - c0 < cb ? G.row_bytes - c0 : cb;
+    uint32_t tx = 0;
+    for (uint32_t r = 0; r < tr.nrows; r++) {
+        const uint64_t s0 = (uint64_t)(tr.row0 + r) * G.row_bytes + c0;
+        tx += (uint32_t)(((s0 + len + 15) & ~uint64_t(15)) - (s0 & ~uint64_t(15)));
+    }
+    mbar_expect_tx(bar, tx);
+    for (uint32_t r = 0; r < tr.nrows; r++) {
+        const uint64_t s0 = (uint64_t)(tr.row0 + r) * G.row_bytes + c0;
+        const uint64_t a0 = s0 & ~uint64_t(15);
+        bulk_g2s(buf + (uint64_t)r * 16u * rsu, G.w + a0, (uint32_t)(((s0 + len + 15) & ~uint64_t(15)) - a0), bar);
+    }
+}
+
 // ------------------------------------------------------------------ kernel
 
 __global__ void __launch_bounds__(kMThreads)
-gemv_mma_kernel(const __grid_constant__ GemvArgs a, uint32_t stage_bytes, const __grid_constant__ GemvMaps maps) {
+gemv_mma_kernel(const __grid_constant__ GemvArgs a, uint32_t stage_bytes, const __grid_constant__ GemvMaps maps,
+                uint32_t ipc, uint32_t cu, uint32_t rsu) {
     extern __shared__ __align__(128) uint8_t smem_dyn[];
     // tensor copies need 128-byte aligned destinations
     uint8_t* const smem_raw = smem_dyn + ((128u - (smem_u32(smem_dyn) & 127u)) & 127u);
@@ -273,15 +336,18 @@ gemv_mma_kernel(const __grid_constant__ GemvArgs a, uint32_t stage_bytes, const 
     sm.red = sm.sx + K / 16;
     sm.part = sm.red + 2 * kMWarps;
 
+    // Work items: a tile, or (ipc > 0: rows too long for two whole tiles in shared
+    // memory) each of its nch K-chunks of ipc iterations in turn, chunk c copied
+    // as one TMA box of cu units + 1 from unit c * cu of the 16 rows. The CTA's
+    // item j is chunk j % nch of tile blockIdx.x + (j / nch) * gridDim.x.
+    const uint32_t nit = ipc ? (K + seg_sb(a.seg[0].type) - 1) / seg_sb(a.seg[0].type) : 0u;
+    const uint32_t nch = ipc ? (nit + ipc - 1) / ipc : 1u;
     // weights first: they do not depend on the previous kernel
     if (tid == 0) {
         s_fail = 0;
         for (uint32_t i = 0; i < kStages; i++) mbar_init(&bars[i], 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-        for (uint32_t i = 0; i < kStages; i++) {
-            const uint32_t t = blockIdx.x + i * gridDim.x;
-            if (t < n_tiles) issue_tile(a, maps, t, stages + i * stage_bytes, &bars[i]);
-        }
+        for (uint32_t i = 0; i < kStages; i++) issue_item(a, maps, i, nch, n_tiles, ipc, cu, rsu, stages + i * stage_bytes, &bars[i]);
     }
     pdl_wait();                                                   // x comes from the previous kernel
     const bool pulled = a.tp.pull != kTpNone;
@@ -289,7 +355,7 @@ gemv_mma_kernel(const __grid_constant__ GemvArgs a, uint32_t stage_bytes, const 
         // the error bit is set; the first tiles' copies land before the CTA leaves
         if (tid == 0)
             for (uint32_t i = 0; i < kStages; i++)
-                if (blockIdx.x + i * gridDim.x < n_tiles) mbar_wait(&bars[i], 0);
+                if (blockIdx.x + (i / nch) * gridDim.x < n_tiles) mbar_wait(&bars[i], 0);
         return;
     }
     stage_x(a, pulled ? sm.xf : a.x, sm, &s_scale);               // ends with __syncthreads
@@ -303,49 +369,70 @@ gemv_mma_kernel(const __grid_constant__ GemvArgs a, uint32_t stage_bytes, const 
     L.slot = L.g >> 1;
     L.xpart = (L.g & 1u) ? sm.xl : sm.xh;
 
-    uint32_t i = 0;
-    for (uint32_t t = blockIdx.x; t < n_tiles; t += gridDim.x, i++) {
-        const uint32_t st = i % kStages, parity = (i / kStages) & 1u;
-        uint8_t* buf = stages + st * stage_bytes;
-        if (!mbar_wait(&bars[st], parity)) {
-            atomicOr(a.err, kErrWaitTimeout);
-            s_fail = 1;
-        }
-        __syncthreads();
-        if (s_fail) return;                       // a copy never landed: the flag is set, stop
+    uint32_t i = 0, tiles_done = 0;                // items consumed, tiles finished
+    for (uint32_t t = blockIdx.x; t < n_tiles; t += gridDim.x, tiles_done++) {
         const TileRef tr = tile_of(a, t);
         const GemvSeg& G = a.seg[tr.seg];
         const bool glu = G.epi == EPI_GLU_SILU || G.epi == EPI_GLU_GELU;
         // a gated tile: warps 0..3 take the gate rows, 4..7 the up rows
         const uint32_t half = kMWarps / 2;
         const bool up = glu && warp >= half;
-        const uint8_t* base = up ? buf + up_offset(G) : buf;
-        const uint64_t rb = smem_rs(up ? G.row_bytes2 : G.row_bytes);
         const uint32_t first = glu ? warp % half : warp, step = glu ? half : kMWarps;
         float acc[2] = {0.f, 0.f};
-        switch (G.type) {
-        case T_Q4_K: tile_rows<FQ4K>(base, rb, K, L, first, step, sm, acc); break;
-        case T_Q6_K: tile_rows<FQ6K>(base, rb, K, L, first, step, sm, acc); break;
-        case T_Q8_0: tile_rows<FQ80>(base, rb, K, L, first, step, sm, acc); break;
-        case T_Q4_1: tile_rows<FQ41>(base, rb, K, L, first, step, sm, acc); break;
-        case T_Q5_K: tile_rows<FQ5K>(base, rb, K, L, first, step, sm, acc); break;
-        case T_Q5_0: tile_rows<FQ50>(base, rb, K, L, first, step, sm, acc); break;
-        default:     tile_rows<FQ40>(base, rb, K, L, first, step, sm, acc); break;
-        }
-        // the lanes of a quad hold different slots' sums: combine them
+        for (uint32_t c = 0; c < nch; c++, i++) {
+            const uint32_t st = i % kStages, parity = (i / kStages) & 1u;
+            uint8_t* buf = stages + st * stage_bytes;
+            if (!mbar_wait(&bars[st], parity)) {
+                atomicOr(a.err, kErrWaitTimeout);
+                s_fail = 1;
+            }
+            __syncthreads();
+            if (s_fail) return;                   // a copy never landed: the flag is set, stop
+            if (ipc) {
+                const uint64_t rb = 16u * rsu;
+                const uint32_t it0 = c * ipc, it1 = min(it0 + ipc, nit);
+                uint32_t mis = 0, mis8 = 0;
+                if (!cu) {                        // per-row windows: where each row's chunk starts in its slot
+                    const uint64_t c0 = (uint64_t)it0 * seg_sbb_dev(G.type);
+                    mis = (uint32_t)(((uint64_t)(tr.row0 + L.g) * G.row_bytes + c0) & 15u);
+                    mis8 = (uint32_t)(((uint64_t)(tr.row0 + L.g + 8) * G.row_bytes + c0) & 15u);
+                }
+                switch (G.type) {
+                case T_Q4_K: chunk_rows<FQ4K>(buf, rb, mis, mis8, K, L, first, step, it0, it1, sm, acc); break;
+                case T_Q6_K: chunk_rows<FQ6K>(buf, rb, mis, mis8, K, L, first, step, it0, it1, sm, acc); break;
+                case T_Q8_0: chunk_rows<FQ80>(buf, rb, mis, mis8, K, L, first, step, it0, it1, sm, acc); break;
+                case T_Q4_1: chunk_rows<FQ41>(buf, rb, mis, mis8, K, L, first, step, it0, it1, sm, acc); break;
+                case T_Q5_K: chunk_rows<FQ5K>(buf, rb, mis, mis8, K, L, first, step, it0, it1, sm, acc); break;
+                case T_Q5_0: chunk_rows<FQ50>(buf, rb, mis, mis8, K, L, first, step, it0, it1, sm, acc); break;
+                default:     chunk_rows<FQ40>(buf, rb, mis, mis8, K, L, first, step, it0, it1, sm, acc); break;
+                }
+            } else {
+                const uint8_t* base = up ? buf + up_offset(G) : buf;
+                const uint64_t rb = smem_rs(up ? G.row_bytes2 : G.row_bytes);
+                switch (G.type) {
+                case T_Q4_K: tile_rows<FQ4K>(base, rb, K, L, first, step, sm, acc); break;
+                case T_Q6_K: tile_rows<FQ6K>(base, rb, K, L, first, step, sm, acc); break;
+                case T_Q8_0: tile_rows<FQ80>(base, rb, K, L, first, step, sm, acc); break;
+                case T_Q4_1: tile_rows<FQ41>(base, rb, K, L, first, step, sm, acc); break;
+                case T_Q5_K: tile_rows<FQ5K>(base, rb, K, L, first, step, sm, acc); break;
+                case T_Q5_0: tile_rows<FQ50>(base, rb, K, L, first, step, sm, acc); break;
+                default:     tile_rows<FQ40>(base, rb, K, L, first, step, sm, acc); break;
+                }
+            }
+            if (c + 1 == nch) {
+                // the lanes of a quad hold different slots' sums: combine them
 #pragma unroll
-        for (int r = 0; r < 2; r++) {
-            acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 1);
-            acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 2);
-        }
-        if (L.tig == 0) {
-            sm.part[warp * 16 + L.g] = acc[0];
-            sm.part[warp * 16 + L.g + 8] = acc[1];
-        }
-        __syncthreads();                          // stage buffer consumed, partials ready
-        if (tid == 0) {
-            const uint32_t nt = t + kStages * gridDim.x;
-            if (nt < n_tiles) issue_tile(a, maps, nt, buf, &bars[st]);
+                for (int r = 0; r < 2; r++) {
+                    acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 1);
+                    acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], 2);
+                }
+                if (L.tig == 0) {
+                    sm.part[warp * 16 + L.g] = acc[0];
+                    sm.part[warp * 16 + L.g + 8] = acc[1];
+                }
+            }
+            __syncthreads();                      // stage buffer consumed (last chunk: partials ready)
+            if (tid == 0) issue_item(a, maps, i + kStages, nch, n_tiles, ipc, cu, rsu, buf, &bars[st]);
         }
         // epilogue: thread r < 16 finishes row row0 + r
         unsigned long long key = 0ull;
@@ -394,7 +481,7 @@ gemv_mma_kernel(const __grid_constant__ GemvArgs a, uint32_t stage_bytes, const 
         __syncthreads();
         if (tid < a.tp.world) {
             uint32_t* c = a.tp.arrive[tid] + a.tp.push * 8u + a.tp.rank;
-            asm volatile("red.release.sys.global.add.u32 [%0], %1;\n" ::"l"(c), "r"(i) : "memory");
+            asm volatile("red.release.sys.global.add.u32 [%0], %1;\n" ::"l"(c), "r"(tiles_done) : "memory");
         }
     }
 }
@@ -418,7 +505,15 @@ bool gemv_mma_init() {
 // The stage size and shared memory of `in` on the tensor-core kernel; false
 // when some segment is not a tensor-core format (a gated pair sharing one
 // format) or the tiles do not fit in shared memory.
-static bool mma_plan(const GemvArgs& in, uint64_t* stage_out, size_t* smem_out) {
+// Rows too long for two whole tiles next to the staged input (K = 11008 at the
+// 7B shape) move in K-chunks instead: *ipc_out iterations per chunk, *cu_out
+// 16-byte units (even, so the padded stride cu + 1 keeps the rows an MMA reads
+// in different banks); one segment, not gated, rows of a multiple of 16 bytes.
+static bool mma_plan(const GemvArgs& in, uint64_t* stage_out, size_t* smem_out, uint32_t* ipc_out = nullptr,
+                     uint32_t* cu_out = nullptr, uint32_t* rsu_out = nullptr) {
+    if (ipc_out) *ipc_out = 0;
+    if (cu_out) *cu_out = 0;
+    if (rsu_out) *rsu_out = 0;
     if (in.K % 32 != 0) return false;
     if ((in.tp.push != kTpNone || in.tp.pull != kTpNone) &&
         (in.K > kTpFusedFloats || in.tp.world > 8 || (in.tp.pull != kTpNone && in.x == nullptr)))
@@ -443,8 +538,35 @@ static bool mma_plan(const GemvArgs& in, uint64_t* stage_out, size_t* smem_out) 
                                  (in.norm == NORM_LAYER && reinterpret_cast<uintptr_t>(in.norm_b) % 16 != 0)))
         return false;
     if (reinterpret_cast<uintptr_t>(in.x) % 16 != 0) return false;
-    const size_t smem = kStages * stage + x_smem(in.K) + 128;    // + alignment slack
-    if (smem > kSmemLimit) return false;
+    size_t smem = kStages * stage + x_smem(in.K) + 128;          // + alignment slack
+    if (smem > kSmemLimit) {
+        const GemvSeg& g = in.seg[0];
+        const bool glu = g.epi == EPI_GLU_SILU || g.epi == EPI_GLU_GELU;
+        if (in.nseg != 1 || glu || g.row_bytes % 2 != 0) return false;
+        const size_t xs = x_smem(in.K) + 128;
+        if (xs >= kSmemLimit) return false;
+        const size_t per_stage = (kSmemLimit - xs) / kStages;
+        const uint32_t sbb = seg_sbb(g.type);
+        const bool box = g.row_bytes % 16 == 0;                    // TMA box; else per-row windows
+        uint32_t ipc = 0, cu = 0, rsu = 0;
+        for (uint32_t k = 4000 / sbb; k >= 1 && ipc == 0; k--) {
+            const uint32_t bytes = k * sbb;
+            if (box && (bytes % 16 != 0 || (bytes / 16) % 2 != 0)) continue;
+            // slot units: the chunk (+ one unit of padding), or its aligned window (+ padding), odd
+            const uint32_t su = box ? bytes / 16 + 1 : ((bytes + 30 + 15) / 16 + 1) | 1u;
+            if (su > 256 || (size_t)256 * su > per_stage) continue;
+            ipc = k;
+            cu = box ? bytes / 16 : 0;
+            rsu = su;
+        }
+        if (ipc == 0) return false;
+        stage = 256u * rsu;                                         // a multiple of 128
+        smem = kStages * stage + xs;
+        if (smem > kSmemLimit) return false;
+        if (ipc_out) *ipc_out = ipc;
+        if (cu_out) *cu_out = cu;
+        if (rsu_out) *rsu_out = rsu;
+    }
     *stage_out = stage;
     *smem_out = smem;
     return true;
@@ -463,7 +585,8 @@ bool launch_gemv_mma(const GemvArgs& in, cudaStream_t st, bool* handled) {
     *handled = false;
     uint64_t stage = 0;
     size_t smem = 0;
-    if (!mma_plan(in, &stage, &smem)) return true;
+    uint32_t ipc = 0, cu = 0, rsu = 0;
+    if (!mma_plan(in, &stage, &smem, &ipc, &cu, &rsu)) return true;
     GemvArgs a = in;
     uint32_t tiles = 0;
     for (uint32_t i = 0; i < a.nseg; i++) {
@@ -484,15 +607,21 @@ bool launch_gemv_mma(const GemvArgs& in, cudaStream_t st, bool* handled) {
     // one TMA tensor copy per tile for padded rows (bulk copies per row if the
     // driver refuses a map)
     GemvMaps maps = {};
-    for (uint32_t i = 0; i < a.nseg; i++) {
-        const GemvSeg& g = a.seg[i];
-        const bool glu = g.epi == EPI_GLU_SILU || g.epi == EPI_GLU_GELU;
-        if (padded_rows(g.row_bytes)) maps.has[i][0] = encode_tile_map(&maps.m[i][0], g.w, g.row_bytes, g.rows);
-        if (glu && padded_rows(g.row_bytes2))
-            maps.has[i][1] = encode_tile_map(&maps.m[i][1], g.w2, g.row_bytes2, g.rows);
+    if (ipc && cu) {
+        // K-chunks: one box map of cu + 1 units (the driver may refuse it: then the CUDA-core kernel)
+        if (!encode_box_map(&maps.m[0][0], a.seg[0].w, a.seg[0].row_bytes, a.seg[0].rows, cu + 1)) return true;
+        maps.has[0][0] = 1;
+    } else if (!ipc) {
+        for (uint32_t i = 0; i < a.nseg; i++) {
+            const GemvSeg& g = a.seg[i];
+            const bool glu = g.epi == EPI_GLU_SILU || g.epi == EPI_GLU_GELU;
+            if (padded_rows(g.row_bytes)) maps.has[i][0] = encode_tile_map(&maps.m[i][0], g.w, g.row_bytes, g.rows);
+            if (glu && padded_rows(g.row_bytes2))
+                maps.has[i][1] = encode_tile_map(&maps.m[i][1], g.w2, g.row_bytes2, g.rows);
+        }
     }
     *handled = true;
-    return LM_CUDA(launch_k(gemv_mma_kernel, dim3(grid), dim3(kMThreads), smem, st, a, (uint32_t)stage, maps));
+    return LM_CUDA(launch_k(gemv_mma_kernel, dim3(grid), dim3(kMThreads), smem, st, a, (uint32_t)stage, maps, ipc, cu, rsu));
 }
 
 }  // namespace lm

@@ -435,6 +435,24 @@ __device__ __forceinline__ void tile_rows(const uint8_t* base, uint64_t rb, uint
     }
 }
 
+// Iterations [it0, it1) of one K-chunk of a tile (rows at stride rb from base,
+// the chunk's first byte at base): warps first, first + step, ...
+// mis, mis8: where rows g and g + 8 start in their slots (copies of rows whose
+// chunk does not start on a 16-byte boundary bring the aligned window around it).
+template <class F>
+__device__ __forceinline__ void chunk_rows(const uint8_t* base, uint64_t rb, uint32_t mis, uint32_t mis8, uint32_t K,
+                                           const Lane& L, uint32_t first, uint32_t step, uint32_t it0, uint32_t it1,
+                                           const MmaSmem& sm, float* acc) {
+    const uint32_t nblk32 = K / 32;
+    const uint8_t* rg = base + (uint64_t)L.g * rb + mis;
+    const uint8_t* rg8 = base + (uint64_t)(L.g + 8) * rb + mis8;
+    for (uint32_t it = it0 + first; it < it1; it += step) {
+        const uint32_t nvalid = F::SB == 256 ? 1u : min(4u, nblk32 - it * 4);
+        const uint64_t o = (uint64_t)(it - it0) * F::SBB;
+        F::compute(rg + o, rg8 + o, it * F::SB, nvalid, L, sm, acc);
+    }
+}
+
 // ------------------------------------------------------------------ tiles
 
 struct TileRef {
@@ -475,6 +493,15 @@ __host__ __device__ __forceinline__ uint32_t rows_tx(uint64_t rb, uint32_t nrows
 // so their tiles move as one TMA tensor copy whose box is a unit wider than
 // the row (encode_tile_map), which lands the rows at the padded stride.
 __host__ __device__ __forceinline__ bool padded_rows(uint64_t rb) { return smem_rs(rb) != rb; }
+
+// TMA tensor copy of a K-chunk of a 16-row tile: the map's box starting at
+// unit y of each row. No multicast.
+__device__ __forceinline__ void tma_box(void* dst, const CUtensorMap* map, int32_t y, int32_t row0, uint64_t* bar) {
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3, %4}], [%5];\n"
+                 ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y), "r"(row0),
+                   "r"(smem_u32(bar)) : "memory");
+}
 
 // TMA tensor copy of one 16-row tile: box {8 halves, units + 1, 16 rows} of a
 // rank-3 view {8, units per row, rows} at row row0, written densely; the extra
