@@ -418,7 +418,7 @@ def run_tp7b(args, lm, L, torch, ws, rank, dist, hbm_peak):
         ms = e0.elapsed_time(e1)
         # every rank's decoded tokens (the first 16 after the prompt) must be
         # bit-identical: a rank whose shard or sum went wrong decodes differently
-        n_tok = TP_PROMPT + 16
+        n_tok = TP_PROMPT + min(16, args.warmup + args.tp_steps)
         tk = np.zeros(n_tok, np.uint32)
         assert L.llamini_session_tokens(s, lm.ptr(tk), n_tok) >= n_tok, lm.last_error()
         mine = tk[TP_PROMPT:].astype(np.int64)
