@@ -281,12 +281,14 @@ bool alloc_buffers(llamini_session* s) {
            LM_CUDA(cudaMemset(s->kc, 0, kv_bytes)) && LM_CUDA(cudaMemset(s->vc, 0, kv_bytes));
 }
 
-// Position splits per query head: at most one (head, split) task per SM, so
-// the decode kernel runs its attention in one wave (each split takes >= 64
-// positions, so short contexts use fewer).
+// Position splits per query head of the per-op attention: about two (head,
+// split) CTAs per SM (at the 7B shape, context ~1000: 3.27 ms/step against 3.39
+// with one per SM and 3.52 with four); each split takes >= 64 positions, so short
+// contexts use fewer. The dataflow kernel runs at most one task per CTA
+// (flow_splits).
 u32 choose_splits(u32 n_heads, u32 max_seq) {
     const u32 sms = (u32)sm_count();
-    u32 s = n_heads ? sms / n_heads : 1;
+    u32 s = n_heads ? 2 * sms / n_heads : 1;
     if (s < 1) s = 1;
     if (s > 32) s = 32;
     const u32 by_len = (max_seq + 63) / 64;
@@ -547,6 +549,9 @@ bool build_decode(llamini_session* s) {
     s->dec_counters = (u32*)own(s, counter_words * 4);
     if (!s->dec_counters) return false;
     s->dec_counter_bytes = counter_words * 4;
+    // attention splits: at most one (head, split) task per CTA
+    u32 dns = (u32)sm_count() / s->n_heads;
+    dns = dns < 1 ? 1u : (dns > s->n_split ? s->n_split : dns);
     for (u32 l = 0; l < L && ok; l++) {
         add_gemv(qkv_args(s, l), 0xFFFFFFFFu);
         // attention: one task per (head, split), each leaving a partial
@@ -554,15 +559,16 @@ bool build_decode(llamini_session* s) {
         at.kind = DEC_ATTN;
         at.at = attn_args(s, l);
         at.at.counter = nullptr;
-        at.n_split = s->n_split;
-        at.ntasks = at.ndone = s->n_heads * s->n_split;
+        at.at.n_split = dns;
+        at.n_split = dns;
+        at.ntasks = at.ndone = s->n_heads * dns;
         at.wait = (u32)ops.size() - 1;
         ops.push_back(at);
         // the O projection merges the partials while staging its input
         add_gemv(o_args(s, l), 0xFFFFFFFFu);
         ops.back().x_merge = 1;
         ops.back().at = at.at;
-        ops.back().n_split = s->n_split;
+        ops.back().n_split = dns;
         add_gemv(ffn_args(s, l), 0xFFFFFFFFu);
         add_gemv(down_args(s, l), l * s->dim);
     }
@@ -659,6 +665,10 @@ bool build_flow(llamini_session* s) {
             return true;
     if (!m_ok(s->head) || s->tok.ptr == nullptr) return true;
     const u32 L = s->n_layers;
+    // attention splits of the flow kernel: at most one (head, split) task per CTA
+    // (the partials buffer is sized for the per-op count, which is at least this)
+    u32 fns = (u32)sm_count() / s->n_heads;
+    fns = fns < 1 ? 1u : (fns > s->n_split ? s->n_split : fns);
     // records: A = the residual stream for QKV and the lm_head, B = for gate/up, C = the FFN activation
     auto rec = [&](u32 n, bool ss, FlowRec* r) {
         r->w = (uint32_t*)own(s, (size_t)n * 4);
@@ -713,8 +723,9 @@ bool build_flow(llamini_session* s) {
         at.kind = FLOW_ATTN;
         at.at = attn_args(s, l);
         at.at.counter = nullptr;
-        at.n_split = s->n_split;
-        at.ntasks = s->n_heads * s->n_split;
+        at.at.n_split = fns;
+        at.n_split = fns;
+        at.ntasks = s->n_heads * fns;
         at.wait = qi;
         const u32 ai = finish_op(at);
         FlowOp o = gemv(s->qd, ai);
@@ -722,7 +733,7 @@ bool build_flow(llamini_session* s) {
         o.seg[0] = seg(W.o, EPI_RESID, nullptr, W.bo);
         o.in_attn = 1;
         o.at = ops[ai].at;
-        o.n_split = s->n_split;
+        o.n_split = fns;
         o.out = rb;
         o.out_nw = W.n2w;
         const u32 oi = finish_op(o);
