@@ -61,6 +61,8 @@ def test_tp_join_argument_checks(lm):
     assert L.llamini_tp_join(0, 0, None) == -1
     assert L.llamini_tp_join(0, 1, None) == 0
     assert L.llamini_tp_world() == 1 and L.llamini_tp_rank() == 0
+    assert L.llamini_tp_leave() == 0                  # outside a group: nothing to leave, no device
+    assert L.llamini_tp_world() == 1
     L.llamini_clear_error()
 
 
